@@ -1,0 +1,266 @@
+// The Llama forward over the paged KV cache: lm/forward.py:21-68 + lm/forward.py:71-84.
+//
+// A model handle holds the weight pointers and one TMA descriptor per bf16 weight matrix;
+// specb200_forward launches, per call: prep/embed, then per layer RMSNorm -> QKV GEMM
+// (RoPE + paged KV write epilogue) -> paged attention -> O GEMM (+ residual) -> RMSNorm ->
+// gate/up GEMM (SiLU*mul epilogue) -> down GEMM (+ residual), then the final RMSNorm (with
+// the last-token row selection of lm/forward.py:66-67) and the fp32-accumulated LM head.
+// Every kernel after the first is launched with programmatic dependent launch, so each GEMM
+// starts streaming its weights while the kernel before it drains. The whole sequence is
+// stream-ordered and allocation-free, so callers can capture it in a CUDA graph.
+#include <algorithm>
+#include <vector>
+
+#include "gemm.cuh"
+#include "kernels.cuh"
+
+namespace specb200 {
+namespace {
+
+struct LayerMaps {
+  CUtensorMap qkv, o, gu, down;
+};
+
+struct Model {
+  specb200_model_config cfg;
+  specb200_model_weights w;
+  std::vector<specb200_layer_weights> layers;
+  std::vector<LayerMaps> maps;
+  CUtensorMap head;
+  int qkv_n;
+};
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+struct Carve {
+  size_t hidden, xbuf, qbuf, attn, act, pos, slot, gemm_ws, attn_ws, total;
+  GemmShape g_qkv, g_o, g_gu, g_down, g_head;
+  AttnPlan ap;
+};
+
+Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
+  const specb200_model_config& c = m.cfg;
+  const bool tc = c.dtype == SPECB200_BF16;
+  const size_t el = tc ? 2 : 4;
+  const int M = B * T;
+  const int rows_out = last_only ? B : M;
+  const int qd = c.n_heads * c.head_dim;
+  Carve r;
+  r.g_qkv = plan_gemm(M, m.qkv_n, c.hidden, tc);
+  r.g_o = plan_gemm(M, c.hidden, qd, tc);
+  r.g_gu = plan_gemm(M, 2 * c.intermediate, c.hidden, tc);
+  r.g_down = plan_gemm(M, c.hidden, c.intermediate, tc);
+  r.g_head = plan_gemm(rows_out, c.vocab, c.hidden, tc);
+  r.ap = plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len);
+  size_t off = 0;
+  r.hidden = off; off += align256(static_cast<size_t>(M) * c.hidden * el);
+  r.xbuf = off; off += align256(static_cast<size_t>(M) * c.hidden * el);
+  r.qbuf = off; off += align256(static_cast<size_t>(M) * qd * el);
+  r.attn = off; off += align256(static_cast<size_t>(M) * qd * el);
+  r.act = off; off += align256(static_cast<size_t>(M) * c.intermediate * el);
+  r.pos = off; off += align256(static_cast<size_t>(M) * 4);
+  r.slot = off; off += align256(static_cast<size_t>(M) * 4);
+  size_t gws = 0;
+  for (const GemmShape* s : {&r.g_qkv, &r.g_o, &r.g_gu, &r.g_down, &r.g_head}) gws = std::max(gws, gemm_workspace_bytes(*s));
+  r.gemm_ws = off; off += align256(gws);
+  r.attn_ws = off; off += align256(attention_workspace_bytes(r.ap, B, c.n_kv_heads, c.head_dim));
+  r.total = off;
+  return r;
+}
+
+template <typename T>
+int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv, cudaStream_t s) {
+  const specb200_model_config& c = m.cfg;
+  const bool tc = c.dtype == SPECB200_BF16;
+  const int B = bt.B, Tt = bt.T, M = B * Tt;
+  const int rows_out = bt.last_only ? B : M;
+  const int qd = c.n_heads * c.head_dim;
+  T* hidden = reinterpret_cast<T*>(ws + cv.hidden);
+  T* xbuf = reinterpret_cast<T*>(ws + cv.xbuf);
+  T* qbuf = reinterpret_cast<T*>(ws + cv.qbuf);
+  T* attn = reinterpret_cast<T*>(ws + cv.attn);
+  T* act = reinterpret_cast<T*>(ws + cv.act);
+  int32_t* pos = reinterpret_cast<int32_t*>(ws + cv.pos);
+  int32_t* slot = reinterpret_cast<int32_t*>(ws + cv.slot);
+  void* gws = ws + cv.gemm_ws;
+  void* aws = ws + cv.attn_ws;
+  int32_t* status = bt.status;
+
+  CUtensorMap x_hidden{}, x_attn{}, x_act{}, x_final{};
+  if (tc) {
+    bool ok = make_tmap_bf16_2d(&x_hidden, xbuf, c.hidden, M, kTileK, cv.g_qkv.BN) &&
+              make_tmap_bf16_2d(&x_attn, attn, qd, M, kTileK, cv.g_o.BN) &&
+              make_tmap_bf16_2d(&x_act, act, c.intermediate, M, kTileK, cv.g_down.BN) &&
+              make_tmap_bf16_2d(&x_final, xbuf, c.hidden, rows_out, kTileK, cv.g_head.BN);
+    if (!ok) return SPECB200_ERR_ARG;
+  }
+
+  PrepArgs pa;
+  pa.ids = bt.input_ids;
+  pa.n_new = bt.n_new;
+  pa.past = bt.past_len;
+  pa.table = bt.block_table;
+  pa.table_stride = bt.table_stride;
+  pa.bs = bt.block_size;
+  pa.num_slots = bt.num_slots;
+  pa.max_positions = c.max_positions;
+  pa.M = M;
+  pa.T = Tt;
+  pa.V = c.vocab;
+  pa.H = c.hidden;
+  pa.pos_out = pos;
+  pa.slot_out = slot;
+  pa.status = status;
+  int rc = launch_prep_embed<T>(pa, static_cast<const T*>(m.w.embed), hidden, s, false);
+  if (rc) return rc;
+
+  const bool pdl = true;
+  const size_t layer_pool = static_cast<size_t>(bt.num_slots) * c.n_kv_heads * c.head_dim;
+  auto gemm = [&](const GemmShape& sh, const CUtensorMap* wmap, const CUtensorMap* xmap, const void* w, const T* x,
+                  const Epilogue& e) -> int {
+    if (tc) return launch_gemm_tc(sh, *wmap, *xmap, e, gws, status, s, pdl);
+    return launch_gemm_simt<T>(sh, static_cast<const T*>(w), x, e, gws, status, s, pdl);
+  };
+
+  for (int l = 0; l < c.n_layers; ++l) {
+    const specb200_layer_weights& L = m.layers[l];
+    const LayerMaps* mp = tc ? &m.maps[l] : nullptr;
+    if ((rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.attn_norm), M, c.hidden, c.rms_eps, xbuf, nullptr, 1, s,
+                                pdl)))
+      return rc;
+    Epilogue eq = {};
+    eq.op = EPI_QKV;
+    eq.out = qbuf;
+    eq.ldo = qd;
+    eq.k_pool = static_cast<T*>(bt.k_pool) + l * layer_pool;
+    eq.v_pool = static_cast<T*>(bt.v_pool) + l * layer_pool;
+    eq.slot = slot;
+    eq.pos = pos;
+    eq.rope_cos = m.w.rope_cos;
+    eq.rope_sin = m.w.rope_sin;
+    eq.n_heads = c.n_heads;
+    eq.n_kv_heads = c.n_kv_heads;
+    eq.head_dim = c.head_dim;
+    if ((rc = gemm(cv.g_qkv, mp ? &mp->qkv : nullptr, &x_hidden, L.w_qkv, xbuf, eq))) return rc;
+
+    AttnArgs aa;
+    aa.q = qbuf;
+    aa.k_pool = eq.k_pool;
+    aa.v_pool = eq.v_pool;
+    aa.table = bt.block_table;
+    aa.table_stride = bt.table_stride;
+    aa.bs = bt.block_size;
+    aa.past = bt.past_len;
+    aa.n_new = bt.n_new;
+    aa.B = B;
+    aa.T = Tt;
+    aa.Hq = c.n_heads;
+    aa.Hkv = c.n_kv_heads;
+    aa.D = c.head_dim;
+    aa.scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
+    aa.out = attn;
+    aa.status = status;
+    if ((rc = launch_attention<T>(aa, cv.ap, aws, s, pdl))) return rc;
+
+    Epilogue er = {};
+    er.op = EPI_RESID;
+    er.out = hidden;
+    er.ldo = c.hidden;
+    if ((rc = gemm(cv.g_o, mp ? &mp->o : nullptr, &x_attn, L.w_o, attn, er))) return rc;
+    if ((rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.mlp_norm), M, c.hidden, c.rms_eps, xbuf, nullptr, 1, s,
+                                pdl)))
+      return rc;
+    Epilogue eg = {};
+    eg.op = EPI_SILU_MUL;
+    eg.out = act;
+    eg.ldo = c.intermediate;
+    if ((rc = gemm(cv.g_gu, mp ? &mp->gu : nullptr, &x_hidden, L.w_gate_up, xbuf, eg))) return rc;
+    if ((rc = gemm(cv.g_down, mp ? &mp->down : nullptr, &x_act, L.w_down, act, er))) return rc;
+  }
+  if ((rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(m.w.final_norm), rows_out, c.hidden, c.rms_eps, xbuf,
+                              bt.last_only ? bt.n_new : nullptr, Tt, s, pdl)))
+    return rc;
+  Epilogue eh = {};
+  eh.op = EPI_STORE;
+  eh.out_f32 = 1;
+  eh.out = bt.logits;
+  eh.ldo = c.vocab;
+  return gemm(cv.g_head, &m.head, &x_final, m.w.lm_head, xbuf, eh);
+}
+
+}  // namespace
+}  // namespace specb200
+
+using namespace specb200;
+extern "C" int specb200_set_error(int code, const char* msg);
+
+extern "C" int specb200_model_create(const specb200_model_config* config, const specb200_model_weights* weights,
+                                     void** handle) {
+  if (!config || !weights || !handle || !weights->layers) return specb200_set_error(SPECB200_ERR_ARG, "model: null");
+  const specb200_model_config& c = *config;
+  if (c.n_layers <= 0 || c.hidden <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 || c.n_heads % c.n_kv_heads ||
+      c.vocab <= 0 || c.intermediate <= 0 || c.max_positions <= 0)
+    return specb200_set_error(SPECB200_ERR_ARG, "model: bad dimensions");
+  if (c.head_dim != 16 && c.head_dim != 32 && c.head_dim != 64)
+    return specb200_set_error(SPECB200_ERR_UNSUPPORTED, "model: head_dim must be 16, 32 or 64");
+  if (c.intermediate % 64 || c.hidden % 8 || (c.n_heads * c.head_dim) % 8)
+    return specb200_set_error(SPECB200_ERR_UNSUPPORTED, "model: intermediate % 64 and hidden % 8 required");
+  if (c.dtype != SPECB200_F32 && c.dtype != SPECB200_BF16) return specb200_set_error(SPECB200_ERR_UNSUPPORTED, "model: dtype");
+  Model* m = new Model();
+  m->cfg = c;
+  m->w = *weights;
+  m->layers.assign(weights->layers, weights->layers + c.n_layers);
+  m->w.layers = m->layers.data();
+  m->qkv_n = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+  if (c.dtype == SPECB200_BF16) {
+    const int qd = c.n_heads * c.head_dim;
+    m->maps.resize(c.n_layers);
+    bool ok = make_tmap_bf16_2d(&m->head, weights->lm_head, c.hidden, c.vocab, kTileK, kTileN);
+    for (int l = 0; l < c.n_layers && ok; ++l) {
+      const specb200_layer_weights& L = m->layers[l];
+      ok = make_tmap_bf16_2d(&m->maps[l].qkv, L.w_qkv, c.hidden, m->qkv_n, kTileK, kTileN) &&
+           make_tmap_bf16_2d(&m->maps[l].o, L.w_o, qd, c.hidden, kTileK, kTileN) &&
+           make_tmap_bf16_2d(&m->maps[l].gu, L.w_gate_up, c.hidden, 2 * c.intermediate, kTileK, kTileN) &&
+           make_tmap_bf16_2d(&m->maps[l].down, L.w_down, c.intermediate, c.hidden, kTileK, kTileN);
+    }
+    if (!ok) {
+      delete m;
+      return specb200_set_error(SPECB200_ERR_ARG, "model: TMA descriptor for a weight (16-byte alignment?)");
+    }
+  }
+  *handle = m;
+  return SPECB200_OK;
+}
+
+extern "C" int specb200_model_destroy(void* handle) {
+  delete static_cast<Model*>(handle);
+  return SPECB200_OK;
+}
+
+extern "C" size_t specb200_forward_workspace_bytes(void* model, int B, int T, int max_kv_len) {
+  if (!model || B <= 0 || T <= 0) return 0;
+  const Model& m = *static_cast<Model*>(model);
+  return std::max(carve(m, B, T, max_kv_len, 0).total, carve(m, B, T, max_kv_len, 1).total);
+}
+
+extern "C" int specb200_forward(void* model, const specb200_batch* batch, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  if (!model || !batch || !workspace) return specb200_set_error(SPECB200_ERR_ARG, "forward: null pointer");
+  const Model& m = *static_cast<Model*>(model);
+  const specb200_batch& bt = *batch;
+  if (bt.B <= 0 || bt.T <= 0 || bt.block_size <= 0 || bt.table_stride <= 0 || bt.num_slots <= 0 || bt.max_kv_len <= 0)
+    return specb200_set_error(SPECB200_ERR_ARG, "forward: bad batch sizes");
+  if (!bt.input_ids || !bt.n_new || !bt.past_len || !bt.block_table || !bt.k_pool || !bt.v_pool || !bt.logits)
+    return specb200_set_error(SPECB200_ERR_ARG, "forward: null batch pointer");
+  Carve cv = carve(m, bt.B, bt.T, bt.max_kv_len, bt.last_only);
+  if (workspace_bytes < cv.total) return specb200_set_error(SPECB200_ERR_WORKSPACE, "forward: workspace too small");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (bt.status) cudaMemsetAsync(bt.status, 0, sizeof(int32_t), s);
+  int rc = m.cfg.dtype == SPECB200_BF16 ? run_forward<__nv_bfloat16>(m, bt, static_cast<char*>(workspace), cv, s)
+                                        : run_forward<float>(m, bt, static_cast<char*>(workspace), cv, s);
+  if (rc != SPECB200_OK) {
+    cudaError_t e = cudaGetLastError();
+    return specb200_set_error(rc, e != cudaSuccess ? cudaGetErrorString(e) : "forward: launch failed");
+  }
+  return SPECB200_OK;
+}

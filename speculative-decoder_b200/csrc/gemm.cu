@@ -1,0 +1,477 @@
+// K3/K5/K6/K7: the linear layers of the Llama forward.
+//
+// bf16: a tcgen05 swap-AB GEMM. The weight tile (128 output features x 64 of K, TMA-loaded
+// with the 128-byte swizzle) is the MMA's A operand (M = 128) and the token tile (BN tokens x
+// 64, BN a multiple of 16 up to 256) is its B operand, so a verify step with 5 tokens costs
+// one M=128,N=16 MMA per 64-wide K block while the weights stream from HBM at full rate.
+// fp32 products of bf16 inputs are exact and accumulate in TMEM in fp32. Warp roles: warp 4
+// issues TMA (weights for the first stages before griddepcontrol.wait, so a kernel launched
+// with programmatic dependent launch streams its weights while the previous kernel drains),
+// warp 5 issues tcgen05.mma from one thread and owns the TMEM allocation, warps 0-3 read the
+// accumulator back (tcgen05.ld, one TMEM lane per thread) and run the epilogue.
+//
+// fp32: an FFMA kernel with the same tiling and epilogue (tcgen05 has no fp32 inputs and
+// TF32 would change results; this path serves fp32 models such as BASELINE config 1).
+//
+// K is split across CTAs when the output has too few 128-row tiles to fill 148 SMs. Each CTA
+// writes its fp32 partial tile to the workspace; the last CTA of a tile (atomic ticket, no
+// spin) sums the partials in split order, so results do not depend on scheduling, then runs
+// the fused epilogue (RoPE + paged KV write, SiLU*mul, residual add or fp32 store).
+#include <algorithm>
+#include <mutex>
+
+#include "gemm.cuh"
+#include "kernels.cuh"
+
+namespace specb200 {
+
+// ------------------------------------------------------------------------------ epilogue
+SPECB200_DEVINL void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// tile: fp32 [BN][kEpiPitch] in shared memory, column j = output feature n0 + j.
+// 128 threads; thread t owns feature column t.
+template <typename T>
+__device__ void apply_epilogue(const Epilogue& e, const float* tile, int n0, int m0, int valid, int N) {
+  const int t = threadIdx.x;
+  const int n = n0 + t;
+  switch (e.op) {
+    case EPI_STORE: {
+      if (n >= N) return;
+      for (int tok = 0; tok < valid; ++tok) {
+        const float v = tile[tok * kEpiPitch + t];
+        const int64_t o = static_cast<int64_t>(m0 + tok) * e.ldo + n;
+        if (e.out_f32) static_cast<float*>(e.out)[o] = v;
+        else static_cast<T*>(e.out)[o] = from_f32<T>(v);
+      }
+      return;
+    }
+    case EPI_RESID: {
+      if (n >= N) return;
+      T* out = static_cast<T*>(e.out);
+      for (int tok = 0; tok < valid; ++tok) {
+        const int64_t o = static_cast<int64_t>(m0 + tok) * e.ldo + n;
+        const float proj = round_to<T>(tile[tok * kEpiPitch + t]);
+        out[o] = from_f32<T>(to_f32<T>(out[o]) + proj);
+      }
+      return;
+    }
+    case EPI_SILU_MUL: {
+      if (t >= 64 || n >= N) return;
+      T* out = static_cast<T*>(e.out);
+      const int f = n0 / 2 + t;
+      for (int tok = 0; tok < valid; ++tok) {
+        const float g = round_to<T>(tile[tok * kEpiPitch + t]);
+        const float u = round_to<T>(tile[tok * kEpiPitch + 64 + t]);
+        const float act = round_to<T>(g / (1.0f + expf(-g)));
+        out[static_cast<int64_t>(m0 + tok) * e.ldo + f] = from_f32<T>(act * u);
+      }
+      return;
+    }
+    case EPI_QKV: {
+      if (n >= N) return;
+      const int d = e.head_dim, half = d / 2;
+      const int qd = e.n_heads * d, kd = e.n_kv_heads * d;
+      const int region = n < qd ? 0 : (n < qd + kd ? 1 : 2);
+      const int idx = n - (region == 0 ? 0 : (region == 1 ? qd : qd + kd));
+      const int h = idx / d, i = idx % d;
+      const int partner = i < half ? t + half : t - half;
+      for (int tok = 0; tok < valid; ++tok) {
+        const int m = m0 + tok;
+        float y = round_to<T>(tile[tok * kEpiPitch + t]);
+        if (region < 2) {
+          const float xp = round_to<T>(tile[tok * kEpiPitch + partner]);
+          const float rot = i < half ? -xp : xp;
+          const int64_t p = e.pos[m];
+          const float c = round_to<T>(e.rope_cos[p * half + (i % half)]);
+          const float s = round_to<T>(e.rope_sin[p * half + (i % half)]);
+          y = round_to<T>(round_to<T>(y * c) + round_to<T>(rot * s));
+        }
+        if (region == 0) {
+          static_cast<T*>(e.out)[static_cast<int64_t>(m) * e.ldo + n] = from_f32<T>(y);
+        } else {
+          const int slot = e.slot[m];
+          if (slot >= 0) {
+            T* pool = static_cast<T*>(region == 1 ? e.k_pool : e.v_pool);
+            pool[(static_cast<int64_t>(slot) * e.n_kv_heads + h) * d + i] = from_f32<T>(y);
+          }
+        }
+      }
+      return;
+    }
+    default:
+      return;
+  }
+}
+
+// Split-K reduction (when splits > 1) followed by the epilogue. Called by 128 threads that
+// hold this CTA's partial tile in `tile`; returns early in every CTA but the last of a tile.
+template <typename T>
+__device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, void* workspace, int tile_id,
+                            int split, int n0, int m0) {
+  __shared__ int sh_last;
+  const int t = threadIdx.x;
+  const int valid = min(s.BN, s.M - m0);
+  if (s.splits > 1) {
+    int* counters = static_cast<int*>(workspace);
+    const size_t counter_bytes = ((static_cast<size_t>(s.n_tiles) * s.m_tiles * sizeof(int) + 255) / 256) * 256;
+    float* parts = reinterpret_cast<float*>(static_cast<char*>(workspace) + counter_bytes);
+    const size_t tile_elems = static_cast<size_t>(s.BN) * kTileN;
+    float* mine = parts + (static_cast<size_t>(tile_id) * s.splits + split) * tile_elems;
+    for (int tok = 0; tok < valid; ++tok) mine[tok * kTileN + t] = tile[tok * kEpiPitch + t];
+    __threadfence();
+    epi_bar_sync();
+    if (t == 0) sh_last = (atomicAdd(counters + tile_id, 1) == s.splits - 1);
+    epi_bar_sync();
+    if (!sh_last) return;
+    __threadfence();
+    const float* base = parts + static_cast<size_t>(tile_id) * s.splits * tile_elems;
+    for (int tok = 0; tok < valid; ++tok) {
+      float acc = 0.f;
+      for (int sp = 0; sp < s.splits; ++sp) acc += __ldcg(base + sp * tile_elems + tok * kTileN + t);
+      tile[tok * kEpiPitch + t] = acc;
+    }
+    if (t == 0) counters[tile_id] = 0;
+    epi_bar_sync();
+  }
+  apply_epilogue<T>(e, tile, n0, m0, valid, s.N);
+}
+
+SPECB200_DEVINL void split_range(const GemmShape& s, int split, int& kb0, int& kb1) {
+  kb0 = static_cast<int>(static_cast<int64_t>(s.kblocks) * split / s.splits);
+  kb1 = static_cast<int>(static_cast<int64_t>(s.kblocks) * (split + 1) / s.splits);
+}
+
+// ------------------------------------------------------------------------------ tcgen05 kernel
+constexpr int kTcThreads = 192;
+constexpr uint32_t kWTileBytes = kTileN * kTileK * 2;  // 16 KB
+
+SPECB200_DEVINL uint32_t tmem_cols_for(int BN) { return BN <= 32 ? 32u : BN <= 64 ? 64u : BN <= 128 ? 128u : 256u; }
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map, GemmShape s,
+                   Epilogue e, void* workspace, int32_t* status, int stages) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int BN = s.BN;
+  const uint32_t x_bytes = static_cast<uint32_t>(BN) * kTileK * 2;
+  const uint32_t stage_bytes = kWTileBytes + x_bytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * stage_bytes);
+  uint64_t* empty = full + stages;
+  uint64_t* tmem_full = empty + stages;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_full + 1);
+  int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_tile = blockIdx.x, split = blockIdx.y, m_tile = blockIdx.z;
+  const int tile_id = m_tile * s.n_tiles + n_tile;
+  int kb0, kb1;
+  split_range(s, split, kb0, kb1);
+  const int nkb = kb1 - kb0;
+  const uint32_t tmem_cols = tmem_cols_for(BN);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(tmem_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_holder, tmem_cols);
+    tmem_relinquish();
+  }
+  pdl_launch_dependents();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  if (warp == 4) {
+    if (lane == 0) {
+      tma_prefetch_desc(&w_map);
+      tma_prefetch_desc(&x_map);
+      const uint64_t pol_w = l2_policy_evict_first();
+      const int pre = min(stages, nkb);
+      // Weights do not depend on the previous kernel: start streaming them before the wait.
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], stage_bytes);
+        tma_load_2d_hint(smem + i * stage_bytes, &w_map, &full[i], (kb0 + i) * kTileK, n_tile * kTileN, pol_w);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(smem + i * stage_bytes + kWTileBytes, &x_map, &full[i], (kb0 + i) * kTileK, m_tile * BN);
+      for (int i = pre; i < nkb; ++i) {
+        const int st = i % stages;
+        if (!mbar_wait_bounded(&empty[st], ((i / stages) - 1) & 1, status, abort_flag)) break;
+        mbar_arrive_expect_tx(&full[st], stage_bytes);
+        tma_load_2d_hint(smem + st * stage_bytes, &w_map, &full[st], (kb0 + i) * kTileK, n_tile * kTileN, pol_w);
+        tma_load_2d(smem + st * stage_bytes + kWTileBytes, &x_map, &full[st], (kb0 + i) * kTileK, m_tile * BN);
+      }
+      // Tail: wait until the MMAs have released the last use of every stage, so that no
+      // tcgen05.commit arrive lands on this CTA's shared memory after it has exited.
+      for (int i = max(0, nkb - stages); i < nkb; ++i)
+        if (!mbar_wait_bounded(&empty[i % stages], (i / stages) & 1, status, abort_flag)) break;
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(kTileN, BN);
+      for (int i = 0; i < nkb; ++i) {
+        const int st = i % stages;
+        if (!mbar_wait_bounded(&full[st], (i / stages) & 1, status, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t wa = smem_u32(smem + st * stage_bytes);
+        const uint32_t xa = wa + kWTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kTileK / 16; ++kk)
+          umma_bf16(tmem_base, umma_desc_sw128(wa + kk * 32), umma_desc_sw128(xa + kk * 32), idesc,
+                    (i > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&empty[st]);  // frees the stage once these MMAs have read it
+      }
+      umma_commit(tmem_full);
+    }
+    __syncwarp();
+  } else {
+    pdl_wait();
+    const bool ok = mbar_wait_bounded(tmem_full, 0, status, abort_flag);
+    tc_fence_after();
+    float* tile = reinterpret_cast<float*>(smem);  // the pipeline stages are idle now
+    if (ok) {
+      for (int c = 0; c < BN; c += 16) {
+        float v[16];
+        tmem_ld16(tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + c, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) tile[(c + j) * kEpiPitch + warp * 32 + lane] = v[j];
+      }
+    }
+    epi_bar_sync();
+    if (ok && !*reinterpret_cast<volatile int*>(abort_flag))
+      finish_tile<__nv_bfloat16>(s, e, tile, workspace, tile_id, split, n_tile * kTileN, m_tile * BN);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, tmem_cols);
+  }
+}
+
+// ------------------------------------------------------------------------------ FFMA kernel
+constexpr int kSimtThreads = 128;
+constexpr int kSimtKC = 256;   // K chunk staged in shared memory
+constexpr int kSimtMaxBN = 32;
+
+template <typename T> SPECB200_DEVINL void load4(const T* p, float (&v)[4]);
+template <> SPECB200_DEVINL void load4<float>(const float* p, float (&v)[4]) {
+  float4 q = *reinterpret_cast<const float4*>(p);
+  v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+}
+template <> SPECB200_DEVINL void load4<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[4]) {
+  uint2 q = *reinterpret_cast<const uint2*>(p);
+  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162*>(&q.x), b = *reinterpret_cast<__nv_bfloat162*>(&q.y);
+  float2 fa = __bfloat1622float2(a), fb = __bfloat1622float2(b);
+  v[0] = fa.x; v[1] = fa.y; v[2] = fb.x; v[3] = fb.y;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSimtThreads)
+    gemm_simt_kernel(const T* __restrict__ w, const T* __restrict__ x, GemmShape s, Epilogue e, void* workspace) {
+  extern __shared__ float xs[];  // [BN][kSimtKC], reused as the epilogue tile
+  pdl_launch_dependents();
+  pdl_wait();
+  const int n_tile = blockIdx.x, split = blockIdx.y, m_tile = blockIdx.z;
+  const int tile_id = m_tile * s.n_tiles + n_tile;
+  const int n0 = n_tile * kTileN, m0 = m_tile * s.BN;
+  const int BN = s.BN;
+  int kb0, kb1;
+  split_range(s, split, kb0, kb1);
+  const int kbeg = kb0 * kTileK, kend = min(s.K, kb1 * kTileK);
+  const int row = n0 + threadIdx.x;
+  float acc[kSimtMaxBN];
+#pragma unroll
+  for (int j = 0; j < kSimtMaxBN; ++j) acc[j] = 0.f;
+  for (int k0 = kbeg; k0 < kend; k0 += kSimtKC) {
+    const int kc = min(kSimtKC, kend - k0);
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < BN * kSimtKC; idx += kSimtThreads) {
+      const int tok = idx / kSimtKC, kk = idx % kSimtKC;
+      float v = 0.f;
+      if (m0 + tok < s.M && kk < kc) v = to_f32<T>(x[static_cast<int64_t>(m0 + tok) * s.K + k0 + kk]);
+      xs[idx] = v;
+    }
+    __syncthreads();
+    if (row < s.N) {
+      const T* wr = w + static_cast<int64_t>(row) * s.K + k0;
+      for (int kk = 0; kk < kc; kk += 4) {
+        float wv[4];
+        load4<T>(wr + kk, wv);
+#pragma unroll
+        for (int j = 0; j < kSimtMaxBN; ++j) {
+          if (j < BN) {
+            const float* xr = xs + j * kSimtKC + kk;
+            acc[j] = fmaf(wv[0], xr[0], acc[j]);
+            acc[j] = fmaf(wv[1], xr[1], acc[j]);
+            acc[j] = fmaf(wv[2], xr[2], acc[j]);
+            acc[j] = fmaf(wv[3], xr[3], acc[j]);
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  float* tile = xs;
+#pragma unroll
+  for (int j = 0; j < kSimtMaxBN; ++j)
+    if (j < BN) tile[j * kEpiPitch + threadIdx.x] = acc[j];
+  __syncthreads();
+  finish_tile<T>(s, e, tile, workspace, tile_id, split, n0, m0);
+}
+
+// ------------------------------------------------------------------------------ host side
+GemmShape plan_gemm(int M, int N, int K, bool tensor_core) {
+  GemmShape s;
+  s.M = M;
+  s.N = N;
+  s.K = K;
+  if (tensor_core) s.BN = std::min(256, ((M + 15) / 16) * 16);
+  else s.BN = std::min(kSimtMaxBN, ((M + 3) / 4) * 4);
+  s.m_tiles = (M + s.BN - 1) / s.BN;
+  s.n_tiles = (N + kTileN - 1) / kTileN;
+  s.kblocks = (K + kTileK - 1) / kTileK;
+  const int ctas = s.n_tiles * s.m_tiles;
+  int splits = (148 + ctas / 2) / ctas;
+  splits = std::max(1, std::min(splits, std::min(16, s.kblocks)));
+  s.splits = splits;
+  return s;
+}
+
+size_t gemm_workspace_bytes(const GemmShape& s) {
+  const size_t counter_bytes = ((static_cast<size_t>(s.n_tiles) * s.m_tiles * sizeof(int) + 255) / 256) * 256;
+  const size_t parts = s.splits > 1 ? static_cast<size_t>(s.n_tiles) * s.m_tiles * s.splits * s.BN * kTileN * 4 : 0;
+  return counter_bytes + parts;
+}
+
+namespace {
+int tc_stages(int BN, size_t* smem_bytes) {
+  const size_t stage = kWTileBytes + static_cast<size_t>(BN) * kTileK * 2;
+  const size_t tile = static_cast<size_t>(BN) * kEpiPitch * 4;
+  const size_t budget = 200 * 1024;
+  int stages = static_cast<int>(std::min<size_t>(8, budget / stage));
+  while (static_cast<size_t>(stages) * stage < tile) ++stages;
+  stages = std::max(stages, 2);
+  *smem_bytes = 1024 + stages * stage + 256;
+  return stages;
+}
+
+}  // namespace
+
+int launch_gemm_tc(const GemmShape& s, const CUtensorMap& w_map, const CUtensorMap& x_map, const Epilogue& epi,
+                   void* workspace, int32_t* status, cudaStream_t stream, bool pdl) {
+  size_t smem = 0;
+  const int stages = tc_stages(s.BN, &smem);
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+  });
+  cudaError_t err = launch_kernel(gemm_tc_kernel, dim3(s.n_tiles, s.splits, s.m_tiles), dim3(kTcThreads), smem, stream, pdl,
+                           w_map, x_map, s, epi, workspace, status, stages);
+  return err == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
+}
+
+template <typename T>
+int launch_gemm_simt(const GemmShape& s, const T* w, const T* x, const Epilogue& epi, void* workspace, int32_t* status,
+                     cudaStream_t stream, bool pdl) {
+  (void)status;
+  const size_t smem = std::max(static_cast<size_t>(s.BN) * kSimtKC, static_cast<size_t>(s.BN) * kEpiPitch) * 4;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaFuncSetAttribute(gemm_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+  });
+  cudaError_t err = launch_kernel(gemm_simt_kernel<T>, dim3(s.n_tiles, s.splits, s.m_tiles), dim3(kSimtThreads), smem, stream,
+                           pdl, w, x, s, epi, workspace);
+  return err == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
+}
+template int launch_gemm_simt<float>(const GemmShape&, const float*, const float*, const Epilogue&, void*, int32_t*,
+                                     cudaStream_t, bool);
+template int launch_gemm_simt<__nv_bfloat16>(const GemmShape&, const __nv_bfloat16*, const __nv_bfloat16*,
+                                             const Epilogue&, void*, int32_t*, cudaStream_t, bool);
+
+// ------------------------------------------------------------------------------ TMA descriptors
+namespace {
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  return fn;
+}
+}  // namespace
+
+bool make_tmap_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer, uint32_t box_inner,
+                       uint32_t box_outer) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (inner * 2) % 16) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+}  // namespace specb200
+
+// ------------------------------------------------------------------------------ C ABI
+using namespace specb200;
+extern "C" int specb200_set_error(int code, const char* msg);
+
+extern "C" size_t specb200_linear_workspace_bytes(int M, int N, int K) {
+  GemmShape s = plan_gemm(M, N, K, true);
+  GemmShape f = plan_gemm(M, N, K, false);
+  return std::max(gemm_workspace_bytes(s), gemm_workspace_bytes(f));
+}
+
+extern "C" int specb200_linear(int dtype, const void* w, const void* x, int M, int N, int K, int out_f32, void* y,
+                               void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  if (M <= 0 || N <= 0 || K <= 0 || K % 8) return specb200_set_error(SPECB200_ERR_ARG, "linear: bad M/N/K (K % 8 == 0)");
+  if (!w || !x || !y || !workspace) return specb200_set_error(SPECB200_ERR_ARG, "linear: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (status) cudaMemsetAsync(status, 0, sizeof(int32_t), s);
+  Epilogue e = {};
+  e.op = EPI_STORE;
+  e.out_f32 = out_f32;
+  e.out = y;
+  e.ldo = N;
+  if (dtype == SPECB200_BF16) {
+    GemmShape sh = plan_gemm(M, N, K, true);
+    if (workspace_bytes < gemm_workspace_bytes(sh)) return specb200_set_error(SPECB200_ERR_WORKSPACE, "linear: workspace");
+    CUtensorMap wm, xm;
+    if (!make_tmap_bf16_2d(&wm, w, K, N, kTileK, kTileN) || !make_tmap_bf16_2d(&xm, x, K, M, kTileK, sh.BN))
+      return specb200_set_error(SPECB200_ERR_ARG, "linear: TMA descriptor (16-byte alignment?)");
+    if (launch_gemm_tc(sh, wm, xm, e, workspace, status, s, false) != SPECB200_OK)
+      return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+  } else if (dtype == SPECB200_F32) {
+    GemmShape sh = plan_gemm(M, N, K, false);
+    if (workspace_bytes < gemm_workspace_bytes(sh)) return specb200_set_error(SPECB200_ERR_WORKSPACE, "linear: workspace");
+    if (launch_gemm_simt<float>(sh, static_cast<const float*>(w), static_cast<const float*>(x), e, workspace, status, s,
+                                false) != SPECB200_OK)
+      return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+  } else {
+    return specb200_set_error(SPECB200_ERR_UNSUPPORTED, "linear: dtype");
+  }
+  return SPECB200_OK;
+}

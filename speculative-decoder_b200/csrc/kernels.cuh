@@ -1,0 +1,65 @@
+// Host-side launchers shared by the forward orchestration (forward.cu) and the C ABI.
+#pragma once
+#include "common.cuh"
+
+namespace specb200 {
+
+// Launch with the programmatic-dependent-launch attribute when `pdl` is set: the kernel may
+// start while the previous kernel on the stream drains, and orders itself after it with
+// griddepcontrol.wait (every kernel here calls pdl_wait() before reading dependent data).
+template <typename K, typename... Args>
+cudaError_t launch_kernel(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+struct PrepArgs {
+  const int32_t* ids;
+  const int32_t* n_new;
+  const int32_t* past;
+  const int32_t* table;
+  int table_stride, bs, num_slots, max_positions;
+  int M, T, V, H;
+  int32_t* pos_out;
+  int32_t* slot_out;
+  int32_t* status;
+};
+
+template <typename T>
+int launch_prep_embed(const PrepArgs& a, const T* embed, T* hidden, cudaStream_t s, bool pdl);
+template <typename T>
+int launch_rmsnorm(const T* x, const T* w, int rows, int H, float eps, T* y, const int32_t* sel_n_new, int T_tokens,
+                   cudaStream_t s, bool pdl);
+
+struct AttnArgs {
+  const void* q;        // [B*T, Hq, D]
+  const void* k_pool;   // [num_slots, Hkv, D] (one layer)
+  const void* v_pool;
+  const int32_t* table;
+  int table_stride, bs;
+  const int32_t* past;
+  const int32_t* n_new;
+  int B, T, Hq, Hkv, D;
+  float scale;
+  void* out;            // [B*T, Hq, D]
+  int32_t* status;
+};
+
+struct AttnPlan {
+  int chunk, splits_max, qtiles;
+};
+AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len);
+size_t attention_workspace_bytes(const AttnPlan& p, int B, int Hkv, int D);
+template <typename T>
+int launch_attention(const AttnArgs& a, const AttnPlan& p, void* workspace, cudaStream_t s, bool pdl);
+
+}  // namespace specb200

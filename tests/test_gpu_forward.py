@@ -1,0 +1,202 @@
+"""Forward and round parity on the GPU: the engine's cached forward against the reference's
+fp64 logits (golden) and the bf16 oracle, and spec.loop.generate / plain decoding against the
+reference's outputs and statistics on the tiny model, plus the reference's rollback and
+bonus-token tests."""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+from transformers import LlamaConfig, LlamaForCausalLM
+
+from conftest import early_exit, random_prompts, tiny_fp32
+from oracle import forward as ofw
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def new_cache(model, block_size: int = 4, num_blocks: int = 4096):
+    from cache.kv import KVCache
+
+    return KVCache.for_model(model.config, num_blocks=num_blocks, block_size=block_size, dtype=model.dtype, device=DEV)
+
+
+@pytest.fixture(scope="module")
+def tiny():
+    return tiny_fp32().to(DEV)
+
+
+# ---------------------------------------------------------------- forward
+@pytest.mark.parametrize("bs", [1, 4])
+def test_forward_fp32_matches_reference_fp64(tiny, golden_forward, bs):
+    """Mixed-length padded batches, multi-token appends and truncate-then-append: the fp32
+    engine is within 2e-5 of the reference's fp64 logits on identical weights."""
+    from lm.forward import forward
+
+    g = golden_forward
+    cache = new_cache(tiny, block_size=bs, num_blocks=256)
+    for s in range(3):
+        cache.add(s)
+    for r in range(4):
+        n_new = [int(x) for x in g[f"bs{bs}_r{r}_n_new"]]
+        got = forward(tiny, cache, [0, 1, 2], torch.from_numpy(g[f"bs{bs}_r{r}_ids"]), n_new).cpu().numpy()
+        want = g[f"bs{bs}_r{r}_logits"]
+        for b, n in enumerate(n_new):
+            assert np.abs(got[b, :n] - want[b, :n]).max() <= 2e-5, (r, b)
+    cache.truncate(0, cache.length(0) - 2)
+    got = forward(tiny, cache, [0], torch.from_numpy(g[f"bs{bs}_trunc_ids"]), [3]).cpu().numpy()
+    assert np.abs(got - g[f"bs{bs}_trunc_logits"]).max() <= 2e-5
+
+
+def _bf16_model(hidden, layers, heads, kv, inter, vocab, seed, theta=10000.0):
+    cfg = LlamaConfig(vocab_size=vocab, hidden_size=hidden, intermediate_size=inter, num_hidden_layers=layers,
+                      num_attention_heads=heads, num_key_value_heads=kv, max_position_embeddings=8192,
+                      rope_parameters={"rope_type": "default", "rope_theta": theta}, rms_norm_eps=1e-5,
+                      tie_word_embeddings=True, attn_implementation="sdpa")
+    torch.manual_seed(seed)
+    return LlamaForCausalLM(cfg).to(torch.bfloat16).eval()
+
+
+@pytest.mark.parametrize("dims", [(128, 2, 2, 1, 256, 512), (576, 2, 9, 3, 1536, 49152), (2048, 2, 32, 32, 8192, 49152)])
+def test_forward_bf16_matches_oracle(dims):
+    """bf16 engine (tcgen05 GEMMs) vs the bf16 oracle over a prefill and a (k+1)-token verify:
+    logits within rtol 2e-2 of the largest logit, argmax agreeing except at near ties."""
+    from lm.forward import forward
+
+    model = _bf16_model(*dims, seed=11, theta=130000.0)
+    w = ofw.weights_from_model(model)
+    prec = ofw.Precision("bf16")
+    model = model.to(DEV)
+    cache = new_cache(model, block_size=16)
+    ocache = ofw.Cache(w, 4096, 16, prec)
+    prompts = [torch.randint(0, dims[-1], (n,), generator=torch.Generator().manual_seed(n)).tolist() for n in (40, 17)]
+    for s in range(2):
+        cache.add(s)
+        ocache.add(s)
+    width = 40
+    ids = np.array([p + [0] * (width - len(p)) for p in prompts])
+    steps = [(ids, [40, 17]), (np.array([[1, 2, 3, 4, 5], [6, 7, 8, 9, 10]]), [5, 5])]
+    for ids_np, n_new in steps:
+        got = forward(model, cache, [0, 1], torch.from_numpy(ids_np), n_new).float().cpu().numpy()
+        want = ofw.forward(w, ocache, [0, 1], ids_np, n_new, prec)
+        for b, n in enumerate(n_new):
+            g, o = got[b, :n], want[b, :n]
+            scale = np.abs(o).max()
+            assert np.abs(g - o).max() <= 2e-2 * scale + 1e-3, (b, np.abs(g - o).max(), scale)
+            top2 = np.sort(o, axis=-1)[:, -2:]
+            gap = top2[:, 1] - top2[:, 0]
+            agree = g.argmax(-1) == o.argmax(-1)
+            assert np.all(agree | (gap < 2e-2 * scale)), (b, gap[~agree])
+
+
+# ---------------------------------------------------------------- generate (composable path)
+@pytest.mark.parametrize("name", ["ngram_k1", "ngram_k4", "draft_k1", "draft_k4"])
+def test_generate_matches_reference(tiny, golden_generate, name):
+    """Greedy spec.loop.generate on the fp32 engine reproduces the reference's fp64 outputs
+    and every SpecStats counter."""
+    from spec.draft import ModelDraft
+    from spec.loop import generate
+    from spec.ngram import NGramDraft
+
+    g = golden_generate
+    k = int(name[-1])
+    drafter = NGramDraft(256) if name.startswith("ngram") else ModelDraft(early_exit(tiny), None)
+    if isinstance(drafter, ModelDraft):
+        drafter.cache = new_cache(drafter.model)
+    out, st = generate(tiny, new_cache(tiny), drafter, g["prompts"] + g["repetitive"], g["max_new"], k=k)
+    want = g[name]
+    assert out == want["outputs"]
+    for key in ("rounds", "drafted", "accepted", "attempts", "accepts", "emitted_per_round", "drafted_per_round"):
+        assert getattr(st, key) == want[key], key
+
+
+def test_plain_decode_matches_reference(tiny, golden_generate):
+    from baselines import cached_autoregressive
+
+    g = golden_generate
+    for p, want in zip(g["prompts"] + g["repetitive"], g["plain"]):
+        assert cached_autoregressive.generate(tiny, new_cache(tiny), p, g["max_new"]) == want
+
+
+def test_batched_plain_decode_matches_one_at_a_time(tiny, golden_generate):
+    from baselines import cached_autoregressive
+
+    g = golden_generate
+    cache = new_cache(tiny, block_size=16, num_blocks=128)
+    prompts = g["prompts"]
+    for i in range(0, len(prompts), 8):
+        assert cached_autoregressive.generate_batch(tiny, cache, prompts[i:i + 8], g["max_new"]) == g["plain"][i:i + 8]
+    assert cache.allocator.num_used == 0 and not cache.tables
+
+
+class ScriptedDraft:
+    """Proposes the target's own continuation for the first j positions, then a wrong token
+    (the reference's tests/test_rollback.py:13-34)."""
+
+    def __init__(self, reference, prompt_len, j, vocab):
+        self.reference, self.prompt_len, self.j, self.vocab = reference, prompt_len, j, vocab
+
+    def prefill(self, seq_ids, prompts):
+        pass
+
+    def propose(self, seq_ids, contexts, k, temperature, generator):
+        done = len(contexts[0]) - self.prompt_len
+        right = self.reference[done:done + k] + [0] * k
+        draft = [right[i] if i < self.j else (right[i] + 1) % self.vocab for i in range(k)]
+        tokens = torch.tensor([draft])
+        return tokens, torch.nn.functional.one_hot(tokens, self.vocab).float()
+
+    def rollback(self, seq_id, keep):
+        pass
+
+    def release(self, seq_id):
+        pass
+
+
+@pytest.mark.parametrize("j", range(5))
+def test_exactly_j_accepted_every_round(tiny, j):
+    from baselines import cached_autoregressive
+    from spec.loop import generate
+
+    prompt = random_prompts(1, 256, seed=3)[0]
+    want = cached_autoregressive.generate(tiny, new_cache(tiny), prompt, 30 + 5)
+    out, st = generate(tiny, new_cache(tiny), ScriptedDraft(want, len(prompt), j, 256), [prompt], 30, k=4)
+    assert out[0] == want[:30]
+    assert st.accepts[:j] == st.attempts[:j] and all(a == 0 for a in st.accepts[j:])
+    assert all(e == j + 1 for e in st.emitted_per_round[:-1])
+
+
+@pytest.mark.parametrize(("k", "max_new"), [(1, 20), (4, 21), (4, 23), (7, 30)])
+def test_full_acceptance_emits_k_plus_one(tiny, k, max_new):
+    from baselines import cached_autoregressive
+    from spec.draft import ModelDraft
+    from spec.loop import generate
+
+    prompt = random_prompts(1, 256, seed=5)[0]
+    want = cached_autoregressive.generate(tiny, new_cache(tiny), prompt, max_new)
+    out, st = generate(tiny, new_cache(tiny), ModelDraft(tiny, new_cache(tiny)), [prompt], max_new, k=k)
+    assert out[0] == want
+    assert st.rounds == math.ceil((max_new - 1) / (k + 1))
+    assert all(e == k + 1 for e in st.emitted_per_round[:-1])
+
+
+def test_sampled_copy_draft_never_rejects(tiny):
+    from spec.draft import ModelDraft
+    from spec.loop import generate
+
+    prompts = random_prompts(20, 256, seed=6)
+    _, st = generate(tiny, new_cache(tiny), ModelDraft(tiny, new_cache(tiny)), prompts, 20, k=4, temperature=1.0,
+                     generator=torch.Generator().manual_seed(0))
+    assert st.accepted == st.drafted
+
+
+def test_verify_invariant_raises(tiny):
+    from spec.verify import verify
+
+    cache = new_cache(tiny)
+    cache.add(0)
+    with pytest.raises(RuntimeError, match="target cache holds"):
+        verify(tiny, cache, [0], [[1, 2, 3]], torch.tensor([[4, 5]]), 0.0)
