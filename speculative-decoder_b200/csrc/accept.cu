@@ -239,7 +239,7 @@ __device__ int64_t residual_sample(const AcceptArgs& a, int b, int n, const RowS
 
 __global__ void __launch_bounds__(kAcceptThreads) accept_kernel(AcceptArgs a) {
   pdl_wait();
-  const int r = blockIdx.x, b = blockIdx.y;
+  const int r = blockIdx.x % a.R, b = blockIdx.x / a.R;  // b-major: a row's CTAs run together
   RowStat* st = a.stats + static_cast<int64_t>(b) * a.R;
   row_statistics(a, b, r, st + r);
   __shared__ int sh_last;
@@ -404,7 +404,9 @@ extern "C" int specb200_accept(const float* p, const float* q, const int64_t* dr
     return specb200_set_error(SPECB200_ERR_WORKSPACE, "accept: workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (status) cudaMemsetAsync(status, 0, sizeof(int32_t), s);
-  accept_kernel<<<dim3(a.R, B), kAcceptThreads, 0, s>>>(a);
+  // The ticket counters sit where a call with another B may have left statistics: clear them.
+  cudaMemsetAsync(a.counters, 0, static_cast<size_t>(B) * sizeof(int), s);
+  accept_kernel<<<static_cast<unsigned>(a.R) * B, kAcceptThreads, 0, s>>>(a);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
   return SPECB200_OK;

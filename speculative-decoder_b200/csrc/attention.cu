@@ -211,13 +211,12 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnKernelArgs 
 }
 
 template <typename T, int D>
-cudaError_t launch_d(const AttnArgs& a, const AttnPlan& p, void* ws, cudaStream_t s, bool pdl) {
+cudaError_t launch_d(const AttnArgs& a, const AttnPlan& p, int* counters, float* partials, cudaStream_t s, bool pdl) {
   AttnKernelArgs ka;
   ka.a = a;
   ka.p = p;
-  const size_t counter_bytes = ((static_cast<size_t>(a.B) * a.Hkv * p.qtiles * sizeof(int) + 255) / 256) * 256;
-  ka.counters = static_cast<int*>(ws);
-  ka.part = reinterpret_cast<float*>(static_cast<char*>(ws) + counter_bytes);
+  ka.counters = counters;
+  ka.part = partials;
   return launch_kernel(attention_kernel<T, D>, dim3(p.splits_max, a.Hkv * p.qtiles, a.B), dim3(kAttnThreads), 0, s, pdl,
                        ka);
 }
@@ -230,6 +229,7 @@ AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len) {
   p.qtiles = (T * G + kRows - 1) / kRows;
   const int groups = B * Hkv * p.qtiles;
   int splits = std::max(1, (2 * 148 + groups - 1) / groups);
+  if (groups > kAttnMaxCounters) splits = 1;
   const int max_len = std::max(1, max_kv_len);
   splits = std::min(splits, (max_len + kKeys - 1) / kKeys);
   p.chunk = (((max_len + splits - 1) / splits) + kKeys - 1) / kKeys * kKeys;
@@ -237,25 +237,28 @@ AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len) {
   return p;
 }
 
-size_t attention_workspace_bytes(const AttnPlan& p, int B, int Hkv, int D) {
+size_t attention_partials_bytes(const AttnPlan& p, int B, int Hkv, int D) {
   const size_t groups = static_cast<size_t>(B) * Hkv * p.qtiles;
-  const size_t counter_bytes = ((groups * sizeof(int) + 255) / 256) * 256;
-  return counter_bytes + groups * p.splits_max * kRows * (D + 2) * sizeof(float);
+  return p.splits_max > 1 ? groups * p.splits_max * kRows * (D + 2) * sizeof(float) : 0;
+}
+
+size_t attention_workspace_bytes(const AttnPlan& p, int B, int Hkv, int D) {
+  return kAttnCounterBytes + attention_partials_bytes(p, B, Hkv, D);
 }
 
 template <typename T>
-int launch_attention(const AttnArgs& a, const AttnPlan& p, void* ws, cudaStream_t s, bool pdl) {
+int launch_attention(const AttnArgs& a, const AttnPlan& p, int* counters, float* partials, cudaStream_t s, bool pdl) {
   cudaError_t e;
   switch (a.D) {
-    case 16: e = launch_d<T, 16>(a, p, ws, s, pdl); break;
-    case 32: e = launch_d<T, 32>(a, p, ws, s, pdl); break;
-    case 64: e = launch_d<T, 64>(a, p, ws, s, pdl); break;
+    case 16: e = launch_d<T, 16>(a, p, counters, partials, s, pdl); break;
+    case 32: e = launch_d<T, 32>(a, p, counters, partials, s, pdl); break;
+    case 64: e = launch_d<T, 64>(a, p, counters, partials, s, pdl); break;
     default: return SPECB200_ERR_UNSUPPORTED;
   }
   return e == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
 }
-template int launch_attention<float>(const AttnArgs&, const AttnPlan&, void*, cudaStream_t, bool);
-template int launch_attention<__nv_bfloat16>(const AttnArgs&, const AttnPlan&, void*, cudaStream_t, bool);
+template int launch_attention<float>(const AttnArgs&, const AttnPlan&, int*, float*, cudaStream_t, bool);
+template int launch_attention<__nv_bfloat16>(const AttnArgs&, const AttnPlan&, int*, float*, cudaStream_t, bool);
 
 }  // namespace specb200
 
@@ -301,8 +304,10 @@ extern "C" int specb200_attention(int dtype, const void* q, const void* k_pool, 
   a.status = status;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (status) cudaMemsetAsync(status, 0, sizeof(int32_t), s);
-  int rc = dtype == SPECB200_BF16 ? launch_attention<__nv_bfloat16>(a, p, workspace, s, false)
-                                  : launch_attention<float>(a, p, workspace, s, false);
+  int* counters = static_cast<int*>(workspace);
+  float* partials = reinterpret_cast<float*>(static_cast<char*>(workspace) + kAttnCounterBytes);
+  int rc = dtype == SPECB200_BF16 ? launch_attention<__nv_bfloat16>(a, p, counters, partials, s, false)
+                                  : launch_attention<float>(a, p, counters, partials, s, false);
   if (rc != SPECB200_OK) return specb200_set_error(rc, cudaGetErrorString(cudaGetLastError()));
   return SPECB200_OK;
 }

@@ -33,7 +33,7 @@ struct Model {
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 struct Carve {
-  size_t hidden, xbuf, qbuf, attn, act, pos, slot, gemm_ws, attn_ws, total;
+  size_t gemm_counters, attn_counters, hidden, xbuf, qbuf, attn, act, pos, slot, gemm_parts, attn_parts, total;
   GemmShape g_qkv, g_o, g_gu, g_down, g_head;
   AttnPlan ap;
 };
@@ -52,7 +52,11 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   r.g_down = plan_gemm(M, c.hidden, c.intermediate, tc);
   r.g_head = plan_gemm(rows_out, c.vocab, c.hidden, tc);
   r.ap = plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len);
+  // The two ticket-counter regions sit at fixed offsets so that they stay zero across calls
+  // of every shape; everything after them is rewritten before it is read.
   size_t off = 0;
+  r.gemm_counters = off; off += align256(kGemmCounterBytes);
+  r.attn_counters = off; off += align256(kAttnCounterBytes);
   r.hidden = off; off += align256(static_cast<size_t>(M) * c.hidden * el);
   r.xbuf = off; off += align256(static_cast<size_t>(M) * c.hidden * el);
   r.qbuf = off; off += align256(static_cast<size_t>(M) * qd * el);
@@ -61,9 +65,9 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   r.pos = off; off += align256(static_cast<size_t>(M) * 4);
   r.slot = off; off += align256(static_cast<size_t>(M) * 4);
   size_t gws = 0;
-  for (const GemmShape* s : {&r.g_qkv, &r.g_o, &r.g_gu, &r.g_down, &r.g_head}) gws = std::max(gws, gemm_workspace_bytes(*s));
-  r.gemm_ws = off; off += align256(gws);
-  r.attn_ws = off; off += align256(attention_workspace_bytes(r.ap, B, c.n_kv_heads, c.head_dim));
+  for (const GemmShape* s : {&r.g_qkv, &r.g_o, &r.g_gu, &r.g_down, &r.g_head}) gws = std::max(gws, gemm_partials_bytes(*s));
+  r.gemm_parts = off; off += align256(gws);
+  r.attn_parts = off; off += align256(attention_partials_bytes(r.ap, B, c.n_kv_heads, c.head_dim));
   r.total = off;
   return r;
 }
@@ -82,8 +86,9 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
   T* act = reinterpret_cast<T*>(ws + cv.act);
   int32_t* pos = reinterpret_cast<int32_t*>(ws + cv.pos);
   int32_t* slot = reinterpret_cast<int32_t*>(ws + cv.slot);
-  void* gws = ws + cv.gemm_ws;
-  void* aws = ws + cv.attn_ws;
+  GemmScratch gscr{reinterpret_cast<int*>(ws + cv.gemm_counters), reinterpret_cast<float*>(ws + cv.gemm_parts)};
+  int* attn_counters = reinterpret_cast<int*>(ws + cv.attn_counters);
+  float* attn_parts = reinterpret_cast<float*>(ws + cv.attn_parts);
   int32_t* status = bt.status;
 
   CUtensorMap x_hidden{}, x_attn{}, x_act{}, x_final{};
@@ -118,8 +123,8 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
   const size_t layer_pool = static_cast<size_t>(bt.num_slots) * c.n_kv_heads * c.head_dim;
   auto gemm = [&](const GemmShape& sh, const CUtensorMap* wmap, const CUtensorMap* xmap, const void* w, const T* x,
                   const Epilogue& e) -> int {
-    if (tc) return launch_gemm_tc(sh, *wmap, *xmap, e, gws, status, s, pdl);
-    return launch_gemm_simt<T>(sh, static_cast<const T*>(w), x, e, gws, status, s, pdl);
+    if (tc) return launch_gemm_tc(sh, *wmap, *xmap, e, gscr, status, s, pdl);
+    return launch_gemm_simt<T>(sh, static_cast<const T*>(w), x, e, gscr, status, s, pdl);
   };
 
   for (int l = 0; l < c.n_layers; ++l) {
@@ -160,7 +165,7 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     aa.scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
     aa.out = attn;
     aa.status = status;
-    if ((rc = launch_attention<T>(aa, cv.ap, aws, s, pdl))) return rc;
+    if ((rc = launch_attention<T>(aa, cv.ap, attn_counters, attn_parts, s, pdl))) return rc;
 
     Epilogue er = {};
     er.op = EPI_RESID;

@@ -106,15 +106,14 @@ __device__ void apply_epilogue(const Epilogue& e, const float* tile, int n0, int
 // Split-K reduction (when splits > 1) followed by the epilogue. Called by 128 threads that
 // hold this CTA's partial tile in `tile`; returns early in every CTA but the last of a tile.
 template <typename T>
-__device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, void* workspace, int tile_id,
+__device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, GemmScratch scratch, int tile_id,
                             int split, int n0, int m0) {
   __shared__ int sh_last;
   const int t = threadIdx.x;
   const int valid = min(s.BN, s.M - m0);
   if (s.splits > 1) {
-    int* counters = static_cast<int*>(workspace);
-    const size_t counter_bytes = ((static_cast<size_t>(s.n_tiles) * s.m_tiles * sizeof(int) + 255) / 256) * 256;
-    float* parts = reinterpret_cast<float*>(static_cast<char*>(workspace) + counter_bytes);
+    int* counters = scratch.counters;
+    float* parts = scratch.partials;
     const size_t tile_elems = static_cast<size_t>(s.BN) * kTileN;
     float* mine = parts + (static_cast<size_t>(tile_id) * s.splits + split) * tile_elems;
     for (int tok = 0; tok < valid; ++tok) mine[tok * kTileN + t] = tile[tok * kEpiPitch + t];
@@ -149,7 +148,7 @@ SPECB200_DEVINL uint32_t tmem_cols_for(int BN) { return BN <= 32 ? 32u : BN <= 6
 
 __global__ void __launch_bounds__(kTcThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map, GemmShape s,
-                   Epilogue e, void* workspace, int32_t* status, int stages) {
+                   Epilogue e, GemmScratch scratch, int32_t* status, int stages) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int BN = s.BN;
@@ -249,7 +248,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     epi_bar_sync();
     if (ok && !*reinterpret_cast<volatile int*>(abort_flag))
-      finish_tile<__nv_bfloat16>(s, e, tile, workspace, tile_id, split, n_tile * kTileN, m_tile * BN);
+      finish_tile<__nv_bfloat16>(s, e, tile, scratch, tile_id, split, n_tile * kTileN, m_tile * BN);
   }
   tc_fence_before();
   __syncthreads();
@@ -278,7 +277,7 @@ template <> SPECB200_DEVINL void load4<__nv_bfloat16>(const __nv_bfloat16* p, fl
 
 template <typename T>
 __global__ void __launch_bounds__(kSimtThreads)
-    gemm_simt_kernel(const T* __restrict__ w, const T* __restrict__ x, GemmShape s, Epilogue e, void* workspace) {
+    gemm_simt_kernel(const T* __restrict__ w, const T* __restrict__ x, GemmShape s, Epilogue e, GemmScratch scratch) {
   extern __shared__ float xs[];  // [BN][kSimtKC], reused as the epilogue tile
   pdl_launch_dependents();
   pdl_wait();
@@ -327,7 +326,7 @@ __global__ void __launch_bounds__(kSimtThreads)
   for (int j = 0; j < kSimtMaxBN; ++j)
     if (j < BN) tile[j * kEpiPitch + threadIdx.x] = acc[j];
   __syncthreads();
-  finish_tile<T>(s, e, tile, workspace, tile_id, split, n0, m0);
+  finish_tile<T>(s, e, tile, scratch, tile_id, split, n0, m0);
 }
 
 // ------------------------------------------------------------------------------ host side
@@ -344,15 +343,16 @@ GemmShape plan_gemm(int M, int N, int K, bool tensor_core) {
   const int ctas = s.n_tiles * s.m_tiles;
   int splits = (148 + ctas / 2) / ctas;
   splits = std::max(1, std::min(splits, std::min(16, s.kblocks)));
+  if (ctas > kGemmMaxCounters) splits = 1;
   s.splits = splits;
   return s;
 }
 
-size_t gemm_workspace_bytes(const GemmShape& s) {
-  const size_t counter_bytes = ((static_cast<size_t>(s.n_tiles) * s.m_tiles * sizeof(int) + 255) / 256) * 256;
-  const size_t parts = s.splits > 1 ? static_cast<size_t>(s.n_tiles) * s.m_tiles * s.splits * s.BN * kTileN * 4 : 0;
-  return counter_bytes + parts;
+size_t gemm_partials_bytes(const GemmShape& s) {
+  return s.splits > 1 ? static_cast<size_t>(s.n_tiles) * s.m_tiles * s.splits * s.BN * kTileN * 4 : 0;
 }
+
+size_t gemm_workspace_bytes(const GemmShape& s) { return kGemmCounterBytes + gemm_partials_bytes(s); }
 
 namespace {
 int tc_stages(int BN, size_t* smem_bytes) {
@@ -369,35 +369,44 @@ int tc_stages(int BN, size_t* smem_bytes) {
 }  // namespace
 
 int launch_gemm_tc(const GemmShape& s, const CUtensorMap& w_map, const CUtensorMap& x_map, const Epilogue& epi,
-                   void* workspace, int32_t* status, cudaStream_t stream, bool pdl) {
+                   GemmScratch scratch, int32_t* status, cudaStream_t stream, bool pdl) {
   size_t smem = 0;
   const int stages = tc_stages(s.BN, &smem);
-  static std::once_flag once;
-  std::call_once(once, [] {
-    cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-  });
+  static std::mutex mu;
+  static size_t smem_set = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (smem > smem_set) {
+      if (cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+          cudaSuccess)
+        return SPECB200_ERR_CUDA;
+      smem_set = smem;
+    }
+  }
   cudaError_t err = launch_kernel(gemm_tc_kernel, dim3(s.n_tiles, s.splits, s.m_tiles), dim3(kTcThreads), smem, stream, pdl,
-                           w_map, x_map, s, epi, workspace, status, stages);
+                           w_map, x_map, s, epi, scratch, status, stages);
   return err == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
 }
 
 template <typename T>
-int launch_gemm_simt(const GemmShape& s, const T* w, const T* x, const Epilogue& epi, void* workspace, int32_t* status,
-                     cudaStream_t stream, bool pdl) {
+int launch_gemm_simt(const GemmShape& s, const T* w, const T* x, const Epilogue& epi, GemmScratch scratch,
+                     int32_t* status, cudaStream_t stream, bool pdl) {
   (void)status;
   const size_t smem = std::max(static_cast<size_t>(s.BN) * kSimtKC, static_cast<size_t>(s.BN) * kEpiPitch) * 4;
   static std::once_flag once;
+  static cudaError_t attr_err = cudaSuccess;
   std::call_once(once, [] {
-    cudaFuncSetAttribute(gemm_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
+    attr_err = cudaFuncSetAttribute(gemm_simt_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 64 * 1024);
   });
+  if (attr_err != cudaSuccess) return SPECB200_ERR_CUDA;
   cudaError_t err = launch_kernel(gemm_simt_kernel<T>, dim3(s.n_tiles, s.splits, s.m_tiles), dim3(kSimtThreads), smem, stream,
-                           pdl, w, x, s, epi, workspace);
+                           pdl, w, x, s, epi, scratch);
   return err == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
 }
-template int launch_gemm_simt<float>(const GemmShape&, const float*, const float*, const Epilogue&, void*, int32_t*,
-                                     cudaStream_t, bool);
+template int launch_gemm_simt<float>(const GemmShape&, const float*, const float*, const Epilogue&, GemmScratch,
+                                     int32_t*, cudaStream_t, bool);
 template int launch_gemm_simt<__nv_bfloat16>(const GemmShape&, const __nv_bfloat16*, const __nv_bfloat16*,
-                                             const Epilogue&, void*, int32_t*, cudaStream_t, bool);
+                                             const Epilogue&, GemmScratch, int32_t*, cudaStream_t, bool);
 
 // ------------------------------------------------------------------------------ TMA descriptors
 namespace {
@@ -456,18 +465,20 @@ extern "C" int specb200_linear(int dtype, const void* w, const void* x, int M, i
   e.out_f32 = out_f32;
   e.out = y;
   e.ldo = N;
+  GemmScratch scratch{static_cast<int*>(workspace),
+                      reinterpret_cast<float*>(static_cast<char*>(workspace) + kGemmCounterBytes)};
   if (dtype == SPECB200_BF16) {
     GemmShape sh = plan_gemm(M, N, K, true);
     if (workspace_bytes < gemm_workspace_bytes(sh)) return specb200_set_error(SPECB200_ERR_WORKSPACE, "linear: workspace");
     CUtensorMap wm, xm;
     if (!make_tmap_bf16_2d(&wm, w, K, N, kTileK, kTileN) || !make_tmap_bf16_2d(&xm, x, K, M, kTileK, sh.BN))
       return specb200_set_error(SPECB200_ERR_ARG, "linear: TMA descriptor (16-byte alignment?)");
-    if (launch_gemm_tc(sh, wm, xm, e, workspace, status, s, false) != SPECB200_OK)
+    if (launch_gemm_tc(sh, wm, xm, e, scratch, status, s, false) != SPECB200_OK)
       return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
   } else if (dtype == SPECB200_F32) {
     GemmShape sh = plan_gemm(M, N, K, false);
     if (workspace_bytes < gemm_workspace_bytes(sh)) return specb200_set_error(SPECB200_ERR_WORKSPACE, "linear: workspace");
-    if (launch_gemm_simt<float>(sh, static_cast<const float*>(w), static_cast<const float*>(x), e, workspace, status, s,
+    if (launch_gemm_simt<float>(sh, static_cast<const float*>(w), static_cast<const float*>(x), e, scratch, status, s,
                                 false) != SPECB200_OK)
       return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
   } else {

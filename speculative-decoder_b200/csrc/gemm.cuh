@@ -30,6 +30,11 @@ struct Epilogue {
 constexpr int kTileN = 128;
 constexpr int kTileK = 64;  // one 128-byte swizzle atom of bf16
 constexpr int kEpiPitch = kTileN + 4;  // fp32 epilogue tile row pitch (floats)
+// Split-K tickets live in a fixed region at the start of every GEMM workspace that nothing
+// else writes; each ticket returns to zero when its tile is done, so the region stays zero
+// across calls of any shape. Split-K is only planned when the tile count fits in it.
+constexpr int kGemmMaxCounters = 1024;
+constexpr size_t kGemmCounterBytes = kGemmMaxCounters * sizeof(int);
 
 struct GemmShape {
   int M, N, K;
@@ -44,10 +49,17 @@ size_t gemm_workspace_bytes(const GemmShape& s);
 
 // Launchers (gemm.cu). w_map is a tensor map over W [N, K] with box {64, 128}; x_map over
 // X [M, K] with box {64, BN}. Both 128-byte swizzled bf16.
+// counters: kGemmMaxCounters ints that start zero (the kernels leave them zero);
+// partials: gemm_partials_bytes(s) of scratch.
+struct GemmScratch {
+  int* counters;
+  float* partials;
+};
+size_t gemm_partials_bytes(const GemmShape& s);
 int launch_gemm_tc(const GemmShape& s, const CUtensorMap& w_map, const CUtensorMap& x_map, const Epilogue& epi,
-                   void* workspace, int32_t* status, cudaStream_t stream, bool pdl);
+                   GemmScratch scratch, int32_t* status, cudaStream_t stream, bool pdl);
 template <typename T>
-int launch_gemm_simt(const GemmShape& s, const T* w, const T* x, const Epilogue& epi, void* workspace,
+int launch_gemm_simt(const GemmShape& s, const T* w, const T* x, const Epilogue& epi, GemmScratch scratch,
                      int32_t* status, cudaStream_t stream, bool pdl);
 
 // TMA descriptor helpers (forward.cu / gemm.cu).

@@ -54,12 +54,19 @@ struct AttnArgs {
   int32_t* status;
 };
 
+// Split-KV merge tickets: a fixed region at the start of the attention workspace (see the
+// GEMM's kGemmMaxCounters). Split-KV is only planned when the group count fits in it.
+constexpr int kAttnMaxCounters = 65536;
+constexpr size_t kAttnCounterBytes = kAttnMaxCounters * sizeof(int);
+
 struct AttnPlan {
   int chunk, splits_max, qtiles;
 };
 AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len);
-size_t attention_workspace_bytes(const AttnPlan& p, int B, int Hkv, int D);
+size_t attention_partials_bytes(const AttnPlan& p, int B, int Hkv, int D);
+size_t attention_workspace_bytes(const AttnPlan& p, int B, int Hkv, int D);  // counters + partials
+// counters: kAttnMaxCounters ints that start zero (left zero); partials: attention_partials_bytes.
 template <typename T>
-int launch_attention(const AttnArgs& a, const AttnPlan& p, void* workspace, cudaStream_t s, bool pdl);
+int launch_attention(const AttnArgs& a, const AttnPlan& p, int* counters, float* partials, cudaStream_t s, bool pdl);
 
 }  // namespace specb200

@@ -1,7 +1,7 @@
 """The engine's view of a Hugging Face Llama/Qwen2 model: packed weights + the C model handle.
 
-Packing (done once per model, cached on the model object like the reference caches its fp32
-head at lm/forward.py:80-83):
+Packing (done once per model and cached, as the reference caches its fp32 head at
+lm/forward.py:80-83):
   w_qkv      = cat(q_proj, k_proj, v_proj)                     [(Hq + 2 Hkv) d, H]
   w_gate_up  = 64-row groups, gate rows 64g..64g+63 then up rows [2 I, H]
                (a 128-row GEMM tile then holds the gate and up rows of the same 64 features,
@@ -14,6 +14,7 @@ The K/V pool is the KVCache's own tensors; the forward writes new entries into t
 from __future__ import annotations
 
 import ctypes
+import weakref
 
 import torch
 
@@ -152,9 +153,16 @@ class Engine:
         return logits
 
 
+# Packed engines by model, held weakly so a model can be deep-copied or dropped freely.
+_ENGINES: "weakref.WeakKeyDictionary[torch.nn.Module, Engine]" = weakref.WeakKeyDictionary()
+
+
 def engine_for(model: torch.nn.Module) -> Engine:
-    eng = getattr(model, "_specb200_engine", None)
-    if eng is None or eng.device != model.model.embed_tokens.weight.device:
+    """The model's packed engine, built on first use and rebuilt if the model moved devices
+    or changed dtype (weights are assumed fixed after packing, as for inference)."""
+    eng = _ENGINES.get(model)
+    w = model.model.embed_tokens.weight
+    if eng is None or eng.device != w.device or eng.dtype != w.dtype or eng.n_layers != len(model.model.layers):
         eng = Engine(model)
-        model._specb200_engine = eng
+        _ENGINES[model] = eng
     return eng

@@ -83,6 +83,4 @@ def early_exit(model, n_layers: int = 1):
     draft = copy.deepcopy(model)
     draft.model.layers = draft.model.layers[:n_layers]
     draft.config.num_hidden_layers = n_layers
-    if hasattr(draft, "_specb200_engine"):
-        del draft._specb200_engine
     return draft
