@@ -1,0 +1,377 @@
+"""Benchmark: generated tokens/s of the speculative round on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl engine|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
+
+Workload: SmolLM2-1.7B-architecture target (hidden 2048, 24
+layers, 32/32 heads, MLP 8192, vocab 49152, RoPE theta 130000, tied) and SmolLM2-135M-
+architecture draft (576, 30 layers, 9/3 heads, MLP 1536), both random-init N(0, 0.02) in fp32
+then cast to bf16 (no checkpoints: synthetic weights), one 512-token uniform-random prompt
+per GPU, k = 4, greedy, 256 new tokens, paged KV block size 16. A step is one
+spec.loop.generate() call over the GPU's request (prefill, first token, rounds until 256
+tokens); requests are independent, so N GPUs run N requests with no collective in the timed
+region (weak scaling) and gather tokens and statistics over NCCL afterwards.
+
+Reported: `value` = generated tokens / device time (CUDA events on the launching stream,
+max over ranks); `e2e` = the same tokens / host wall time of the public generate() call,
+prompts and outputs as host lists (H2D of the prompt and per-round inputs, D2H of per-round
+results inside the timed region); `roofline` = the verify step (the (k+1)-token target
+forward, replayed from a CUDA graph) against measured HBM bandwidth, algorithmic bytes =
+bf16 weights read once (3,422,752,768 B) + 196,608 B of KV per cached token; `accept` = the
+fused accept kernel on BASELINE config 3 (B=64, k=4, V=49152, 113,246,208 B of logits, L2
+flushed between launches); `cpu_baseline` = the CPU oracle (numpy restatement of the
+reference path) timed on this host on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path[:0] = [str(ROOT), str(ROOT / "speculative-decoder_b200")]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+TARGET = dict(hidden_size=2048, num_hidden_layers=24, num_attention_heads=32, num_key_value_heads=32,
+              intermediate_size=8192, vocab_size=49152, rope_theta=130000.0, max_position_embeddings=8192)
+DRAFT = dict(hidden_size=576, num_hidden_layers=30, num_attention_heads=9, num_key_value_heads=3,
+             intermediate_size=1536, vocab_size=49152, rope_theta=100000.0, max_position_embeddings=8192)
+PROMPT_LEN, NEW_TOKENS, K, BLOCK = 512, 256, 4, 16
+WEIGHT_BYTES = 3_422_752_768          # 1.7B linears + tied embedding, bf16, read once per verify
+KV_BYTES_PER_TOKEN = 196_608          # 24 layers x 2 x 32 heads x 64 x 2 B
+ACCEPT_BYTES = 113_246_208            # config 3: 64 x (5 + 4) x 49152 x 4 B
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def make_model(spec: dict, seed: int, device):
+    from transformers import LlamaConfig, LlamaForCausalLM
+
+    cfg = LlamaConfig(vocab_size=spec["vocab_size"], hidden_size=spec["hidden_size"],
+                      intermediate_size=spec["intermediate_size"], num_hidden_layers=spec["num_hidden_layers"],
+                      num_attention_heads=spec["num_attention_heads"], num_key_value_heads=spec["num_key_value_heads"],
+                      max_position_embeddings=spec["max_position_embeddings"], rms_norm_eps=1e-5,
+                      rope_parameters={"rope_type": "default", "rope_theta": spec["rope_theta"]},
+                      tie_word_embeddings=True, initializer_range=0.02, attn_implementation="sdpa")
+    torch.manual_seed(seed)
+    with torch.device(device):
+        model = LlamaForCausalLM(cfg)
+    return model.to(torch.bfloat16).eval()
+
+
+def prompts_for(rank: int, n: int) -> list[list[int]]:
+    g = torch.Generator().manual_seed(1000 + rank)
+    return [torch.randint(0, TARGET["vocab_size"], (PROMPT_LEN,), generator=g).tolist() for _ in range(n)]
+
+
+class Clocks:
+    """nvidia-smi samples of SM clock and throttle reasons during the timed region."""
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            self.proc.wait()
+
+    def summary(self) -> dict:
+        if not self.path or not os.path.exists(self.path):
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.path).read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30) -> dict:
+    """The (k+1)-token target forward of one round at B=1 with `context_len` cached tokens,
+    captured in a CUDA graph and replayed; CUDA events on the replay stream."""
+    from specb200.engine import engine_for
+
+    eng = engine_for(target)
+    cache = cache_cls.for_model(target.config, num_blocks=(context_len + 64) // BLOCK + 4, block_size=BLOCK,
+                                dtype=torch.bfloat16, device=device)
+    cache.add(0)
+    cache.reserve([0], [context_len - 1])
+    past = cache.length(0)
+    cache.reserve([0], [K + 1])
+    cap = context_len + 64
+    table = torch.zeros(1, -(-cap // BLOCK), dtype=torch.int32, device=device)
+    blocks = cache.tables[0].blocks
+    table[0, : len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+    ids = torch.randint(0, TARGET["vocab_size"], (1, K + 1), dtype=torch.int32, device=device)
+    n_new = torch.tensor([K + 1], dtype=torch.int32, device=device)
+    pastt = torch.tensor([past], dtype=torch.int32, device=device)
+    logits = torch.empty(1, K + 1, TARGET["vocab_size"], dtype=torch.float32, device=device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    ws = torch.zeros(eng.workspace_bytes(1, K + 1, cap), dtype=torch.uint8, device=device)
+    run = lambda: eng.forward_device(cache, ids, n_new, pastt, table, cap, False, logits, status, ws)  # noqa: E731
+    run()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        run()
+    torch.cuda.current_stream(device).wait_stream(side)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(reps):
+        g.replay()
+    en.record()
+    en.synchronize()
+    ms = st.elapsed_time(en) / reps
+    assert int(status.item()) == 0
+    kv_tokens = past + K + 1
+    return {"us": ms * 1e3, "bytes": WEIGHT_BYTES + KV_BYTES_PER_TOKEN * kv_tokens, "context": kv_tokens,
+            "launches_per_step": 3 + 7 * TARGET["num_hidden_layers"]}
+
+
+def time_accept(device, reps: int = 20) -> dict:
+    """BASELINE config 3 through the fused kernel in logit mode at T = 1, L2 flushed between
+    launches (the 113 MB of inputs fit in the 126 MB L2)."""
+    from specb200 import ops
+
+    B, V = 64, 49152
+    g = torch.Generator(device=device).manual_seed(3)
+    pl = torch.randn(B, K + 1, V, generator=g, device=device) * 3.0
+    ql = pl[:, :K] + torch.randn(B, K, V, generator=g, device=device)
+    draft = torch.multinomial(torch.softmax(ql, -1).reshape(-1, V), 1, generator=g).reshape(B, K)
+    ua, ur = torch.rand(B, K, generator=g, device=device), torch.rand(B, generator=g, device=device)
+    out = (torch.empty(B, dtype=torch.int64, device=device), torch.empty(B, dtype=torch.int64, device=device))
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    for _ in range(3):
+        ops.accept(pl, ql, draft, ua, ur, logits=True, temperature=1.0, check=False, out=out)
+    times = []
+    for _ in range(reps):
+        flush.fill_(1)
+        st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        st.record()
+        ops.accept(pl, ql, draft, ua, ur, logits=True, temperature=1.0, check=False, out=out)
+        en.record()
+        en.synchronize()
+        times.append(st.elapsed_time(en))
+    return {"us": statistics.median(times) * 1e3, "bytes": ACCEPT_BYTES}
+
+
+def cpu_baseline(target, draft, prompt: list[int], engine_rounds: int | None, max_rounds: int = 2) -> dict:
+    """The CPU oracle (numpy restatement of the reference path, oracle/) on this host: target
+    and draft prefill, first token and `max_rounds` rounds of config 2; tokens/s is then
+    extrapolated to the full 256-token request with the engine's round count (the same
+    greedy algorithm makes the same number of rounds)."""
+    from oracle import forward as ofw
+    from oracle import loop as oloop
+
+    prec = ofw.Precision("bf16")
+    tw = ofw.weights_from_model(target)
+    dw = ofw.weights_from_model(draft)
+    drafter = oloop.ModelDraft(dw, prec, num_blocks=64, block_size=BLOCK)
+    _, st = oloop.generate(tw, prec, drafter, [prompt], NEW_TOKENS, K, num_blocks=64, block_size=BLOCK,
+                           max_rounds=max_rounds)
+    per_round = st["seconds_rounds"] / max(1, st["rounds"])
+    if engine_rounds is None:  # no engine run to take the round count from: the sample's own acceptance
+        emitted = max(1.0, sum(st["emitted_per_round"]) / max(1, len(st["emitted_per_round"])))
+        engine_rounds = int(np.ceil((NEW_TOKENS - 1) / emitted))
+    total = st["seconds_prefill"] + per_round * engine_rounds
+    return {"value": NEW_TOKENS / total, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": (f"CPU oracle (numpy, bf16 rounding) on config 2 at B=1: prefill of the {PROMPT_LEN}-token "
+                       f"prompt on target and draft + first token ({st['seconds_prefill']:.2f} s) and "
+                       f"{st['rounds']} rounds ({per_round:.3f} s each), extrapolated to {engine_rounds} rounds "
+                       f"for {NEW_TOKENS} tokens")}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    metric = "generated tokens/s, 1.7B target k=4 @B1 (config 2, 135M draft, greedy)"
+    config = {"workload": "config2: 1.7B-arch target + 135M-arch draft, bf16 random init, B=1 per GPU, prompt 512, "
+                          "k=4, greedy, 256 new tokens, block 16",
+              "global_batch": world, "seq_len": PROMPT_LEN + NEW_TOKENS, "parallelism": f"requests sharded x{world}",
+              "l2": "weights 3.4 GB >> 126 MB L2 (no flush needed); accept microbench flushes L2 between launches"}
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        torch.set_num_threads(os.cpu_count() or 1)
+        target = make_model(TARGET, 0, "cpu")
+        draft = make_model(DRAFT, 1, "cpu")
+        prompt = prompts_for(0, 1)[0]
+        # each step is a bounded sample (prefill + 2 rounds), extrapolated to the 256-token request
+        vals = []
+        for _ in range(max(1, args.steps)):
+            cb = cpu_baseline(target, draft, prompt, engine_rounds=None, max_rounds=2)
+            vals.append(cb["value"])
+        v = statistics.median(vals)
+        cb["value"] = v
+        print(json.dumps({"impl": "reference", "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": 0,
+                          "steps": args.steps, "warmup": 0, "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
+                          "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                                                      "d2h_bytes_per_step": 0}}))
+        return
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    from cache.kv import KVCache
+    from spec.draft import ModelDraft
+    from spec.loop import generate
+
+    target = make_model(TARGET, 0, device)
+    draft = make_model(DRAFT, 1, device)
+    prompts = prompts_for(rank, 1)
+    blocks = (PROMPT_LEN + NEW_TOKENS + 2 * K + 8) // BLOCK + 2
+
+    def step():
+        cache = KVCache.for_model(target.config, num_blocks=blocks, block_size=BLOCK, dtype=torch.bfloat16, device=device)
+        dcache = KVCache.for_model(draft.config, num_blocks=blocks, block_size=BLOCK, dtype=torch.bfloat16,
+                                   device=device)
+        return generate(target, cache, ModelDraft(draft, dcache), prompts, NEW_TOKENS, k=K)
+
+    for _ in range(args.warmup):
+        out, stats = step()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clocks:
+        torch.cuda.synchronize()
+        ev0.record()
+        w0 = time.perf_counter()
+        tokens = 0
+        rounds = 0
+        for _ in range(args.steps):
+            out, stats = step()
+            tokens += sum(len(o) for o in out)
+            rounds += stats.rounds
+        ev1.record()
+        torch.cuda.synchronize()
+        wall = time.perf_counter() - w0
+    dev_s = ev0.elapsed_time(ev1) / 1e3
+    if world > 1:
+        import torch.distributed as dist
+
+        t = torch.tensor([dev_s, wall, float(tokens)], device=device, dtype=torch.float64)
+        mx = t.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        sm = t.clone()
+        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
+        dev_s, wall, tokens_all = mx[0].item(), mx[1].item(), sm[2].item()
+        # collect outputs (kilobytes) over NCCL after the timed region
+        mine = torch.tensor(out[0] + [0] * (NEW_TOKENS - len(out[0])), dtype=torch.int32, device=device)
+        gathered = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(gathered, mine)
+    else:
+        tokens_all = float(tokens)
+    if rank != 0:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+        return
+
+    vstep = time_verify_step(target, KVCache, device, PROMPT_LEN + NEW_TOKENS // 2)
+    acc = time_accept(device)
+    pk = peaks()
+    achieved = vstep["bytes"] / (vstep["us"] * 1e-6) / 1e9
+    acc_gbs = acc["bytes"] / (acc["us"] * 1e-6) / 1e9
+    alpha = stats.accepted / max(1, stats.drafted)
+    per_forward = lambda layers: 3 + 7 * layers  # noqa: E731  (prep, 7 per layer, final norm, head)
+    launches_per_round = K * (per_forward(DRAFT["num_hidden_layers"]) + 2) + 1 + per_forward(
+        TARGET["num_hidden_layers"]) + 2
+    launches = args.steps * (per_forward(TARGET["num_hidden_layers"]) + per_forward(DRAFT["num_hidden_layers"]) + 1) \
+        + rounds * launches_per_round
+    cb = None
+    if not args.no_cpu_baseline and world == 1:
+        try:
+            cb = cpu_baseline(target.cpu(), draft.cpu(), prompts[0], engine_rounds=rounds // max(1, args.steps))
+        except Exception as e:  # noqa: BLE001
+            cb = {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {e}"}
+    value = tokens_all / dev_s
+    line = {
+        "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dev_s * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, uniform-random prompts)",
+        "config": config,
+        "e2e": {"value": tokens_all / wall, "unit": "tokens/s", "h2d_bytes_per_step": PROMPT_LEN * 8 * world,
+                "d2h_bytes_per_step": NEW_TOKENS * 8 * world},
+        "roofline": {"bound": "hbm", "kernel": "verify step (one (k+1)-token target forward, CUDA graph)",
+                     "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+                     "traffic": None, "peak_source": pk["source"], "verify_step_us": vstep["us"],
+                     "algorithmic_bytes": vstep["bytes"], "context_tokens": vstep["context"]},
+        "accept": {"us": acc["us"], "achieved": acc_gbs, "frac": acc_gbs / pk["hbm_gbs"], "unit": "GB/s",
+                   "algorithmic_bytes": acc["bytes"], "config": "B=64, k=4, V=49152 fp32 logits, T=1"},
+        "acceptance": alpha, "rounds_per_step": rounds / args.steps,
+        "gpu_launches": launches,
+        "clocks": clocks.summary(),
+        "cpu_baseline": cb,
+    }
+    print(json.dumps(line))
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

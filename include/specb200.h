@@ -67,6 +67,7 @@ const char* specb200_last_error(void);
 #define SPECB200_ACCEPT_LOGITS 1
 #define SPECB200_ACCEPT_Q_ONEHOT 2
 #define SPECB200_ACCEPT_DECIDE_ONLY 4
+#define SPECB200_ACCEPT_Q_STEP_MAJOR 8   /* q is laid out [k, B, V] (one draft step per block) */
 size_t specb200_accept_workspace_bytes(int B, int k);
 int specb200_accept(const float* p, const float* q, const int64_t* draft, const float* u_accept,
                     const float* u_residual, int B, int k, int V, int flags, float temperature,
@@ -103,9 +104,18 @@ int specb200_commit_tokens(int32_t* ctx, int64_t ctx_stride, int32_t* ctx_len, c
                            int B, int k, void* stream);
 
 /* ids[b, 0] = ctx[b, len[b]-1], ids[b, 1+j] = draft[b, j]: the (k+1)-token verify input of
- * spec/verify.py:26-27, built on the device. */
+ * spec/verify.py:26-27, built on the device. When given, past[b] = len[b] - 1 (the cache
+ * invariant spec/verify.py:23-25 asserts) and n_new[b] = k + 1, or 0 for rows whose active
+ * flag is 0 (active may be NULL: all rows active). */
 int specb200_verify_ids(const int32_t* ctx, int64_t ctx_stride, const int32_t* ctx_len,
-                        const int64_t* draft, int B, int k, int32_t* ids, void* stream);
+                        const int64_t* draft, const int32_t* active, int B, int k, int32_t* ids,
+                        int32_t* past, int32_t* n_new, void* stream);
+
+/* draft[b, j] = tokens[b] (draft [B, k], may be NULL) and ids[b] = tokens[b] as int32 (may be
+ * NULL): hands one draft step's sampled token to the next draft step and to the verify input
+ * (the token loop of spec/draft.py:50-55). */
+int specb200_scatter_tokens(const int64_t* tokens, int B, int k, int j, int64_t* draft, int32_t* ids,
+                            void* stream);
 
 /* ======================================================================================
  * Llama verify / decode / prefill forward

@@ -96,6 +96,9 @@ def generate(w: dict, prec: fw.Precision, drafter, prompts: list[list[int]], max
              num_blocks: int = 4096, block_size: int = 16, max_rounds: int | None = None):
     """spec/loop.py:38-104. Returns (outputs, stats dict). max_rounds bounds a CPU-baseline
     sample (None runs to completion)."""
+    import time
+
+    t_start = time.perf_counter()
     generator = generator or torch.Generator().manual_seed(0)
     cache = fw.Cache(w, num_blocks, block_size, prec)
     stats = new_stats(k)
@@ -105,6 +108,8 @@ def generate(w: dict, prec: fw.Precision, drafter, prompts: list[list[int]], max
     first = sample(acc.probabilities(run(w, cache, seq_ids, prompts, prec).astype(np.float32), temperature),
                    generator).tolist()
     drafter.prefill(seq_ids, prompts)
+    t_rounds = time.perf_counter()
+    stats["seconds_prefill"] = t_rounds - t_start
     contexts = [p + [t] for p, t in zip(prompts, first)]
     outputs = [[t] for t in first]
 
@@ -157,6 +162,7 @@ def generate(w: dict, prec: fw.Precision, drafter, prompts: list[list[int]], max
             drafter.rollback(s, before + n)
             still.append(s)
         active = still
+    stats["seconds_rounds"] = time.perf_counter() - t_rounds
     return outputs, stats
 
 

@@ -38,7 +38,7 @@ struct AcceptArgs {
   const float* u_accept;
   const float* u_residual;
   int B, k, V, R;
-  int logits, greedy, q_onehot, q_present, decide_only;
+  int logits, greedy, q_onehot, q_present, decide_only, q_step_major;
   float temperature;
   int64_t* n_accepted;
   int64_t* next_token;
@@ -50,7 +50,9 @@ struct AcceptArgs {
 SPECB200_DEVINL const float* row_ptr(const AcceptArgs& a, int b, int r) {
   // rows 0..k: target positions; rows k+1..2k: draft positions 0..k-1
   if (r <= a.k) return a.p + (static_cast<int64_t>(b) * (a.k + 1) + r) * a.V;
-  return a.q + (static_cast<int64_t>(b) * a.k + (r - a.k - 1)) * a.V;
+  const int i = r - a.k - 1;
+  if (a.q_step_major) return a.q + (static_cast<int64_t>(i) * a.B + b) * a.V;  // q [k, B, V]
+  return a.q + (static_cast<int64_t>(b) * a.k + i) * a.V;                       // q [B, k, V]
 }
 
 // Block-wide combination of per-thread (max, sum-exp) pairs.
@@ -393,6 +395,7 @@ extern "C" int specb200_accept(const float* p, const float* q, const int64_t* dr
   a.logits = logits ? 1 : 0;
   a.greedy = (logits && temperature == 0.f) ? 1 : 0;
   a.decide_only = (flags & SPECB200_ACCEPT_DECIDE_ONLY) ? 1 : 0;
+  a.q_step_major = (flags & SPECB200_ACCEPT_Q_STEP_MAJOR) ? 1 : 0;
   a.temperature = temperature;
   a.n_accepted = n_accepted;
   a.next_token = next_token;

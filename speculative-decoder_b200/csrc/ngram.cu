@@ -97,11 +97,13 @@ __global__ void commit_kernel(int32_t* ctx, int64_t stride, int32_t* ctx_len, co
   ctx_len[b] = min(L + n + 1, static_cast<int>(stride));
 }
 
-__global__ void verify_ids_kernel(const int32_t* ctx, int64_t stride, const int32_t* ctx_len, const int64_t* draft, int B,
-                                  int k, int32_t* ids) {
+__global__ void verify_ids_kernel(const int32_t* ctx, int64_t stride, const int32_t* ctx_len, const int64_t* draft,
+                                  const int32_t* active, int B, int k, int32_t* ids, int32_t* past, int32_t* n_new) {
   pdl_wait();
   const int b = blockIdx.x;
   const int j = threadIdx.x;
+  if (j == 0 && past) past[b] = max(ctx_len[b] - 1, 0);
+  if (j == 0 && n_new) n_new[b] = (active == nullptr || active[b]) ? k + 1 : 0;
   if (j > k) return;
   int32_t v;
   if (j == 0) {
@@ -146,11 +148,36 @@ extern "C" int specb200_commit_tokens(int32_t* ctx, int64_t ctx_stride, int32_t*
 }
 
 extern "C" int specb200_verify_ids(const int32_t* ctx, int64_t ctx_stride, const int32_t* ctx_len, const int64_t* draft,
-                                   int B, int k, int32_t* ids, void* stream) {
+                                   const int32_t* active, int B, int k, int32_t* ids, int32_t* past, int32_t* n_new,
+                                   void* stream) {
   if (B <= 0 || k < 0 || k > 1023 || ctx_stride <= 0) return specb200_set_error(SPECB200_ERR_ARG, "verify_ids: bad sizes");
   if (!ctx || !ctx_len || !ids || (k > 0 && !draft)) return specb200_set_error(SPECB200_ERR_ARG, "verify_ids: null pointer");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  verify_ids_kernel<<<B, ((k + 1 + 31) / 32) * 32, 0, s>>>(ctx, ctx_stride, ctx_len, draft, B, k, ids);
+  verify_ids_kernel<<<B, ((k + 1 + 31) / 32) * 32, 0, s>>>(ctx, ctx_stride, ctx_len, draft, active, B, k, ids, past,
+                                                            n_new);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
+  return SPECB200_OK;
+}
+
+namespace specb200 {
+namespace {
+__global__ void scatter_tokens_kernel(const int64_t* tok, int B, int k, int j, int64_t* draft, int32_t* ids) {
+  pdl_wait();
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b >= B) return;
+  const int64_t t = tok[b];
+  if (draft) draft[static_cast<int64_t>(b) * k + j] = t;
+  if (ids) ids[b] = static_cast<int32_t>(t);
+}
+}  // namespace
+}  // namespace specb200
+
+extern "C" int specb200_scatter_tokens(const int64_t* tokens, int B, int k, int j, int64_t* draft, int32_t* ids,
+                                       void* stream) {
+  if (B <= 0 || !tokens || (draft && (k <= 0 || j < 0 || j >= k)))
+    return specb200_set_error(SPECB200_ERR_ARG, "scatter_tokens: bad arguments");
+  scatter_tokens_kernel<<<(B + 127) / 128, 128, 0, static_cast<cudaStream_t>(stream)>>>(tokens, B, k, j, draft, ids);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
   return SPECB200_OK;

@@ -63,7 +63,8 @@ __global__ void __launch_bounds__(256)
   pdl_launch_dependents();
   pdl_wait();
   const int row = blockIdx.x;
-  const int64_t src = sel_n_new ? static_cast<int64_t>(row) * T_tokens + (sel_n_new[row] - 1) : row;
+  // A masked-out row (n_new == 0) selects its first token: finite, and never read back.
+  const int64_t src = sel_n_new ? static_cast<int64_t>(row) * T_tokens + max(sel_n_new[row] - 1, 0) : row;
   const T* xr = x + src * H;
   float ss = 0.f;
   for (int i = threadIdx.x; i < H; i += blockDim.x) {

@@ -19,7 +19,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libspecb200.so"
 
 OK, ERR_ARG, ERR_RANGE, ERR_ZERO_Q, ERR_CUDA, ERR_TIMEOUT, ERR_UNSUPPORTED, ERR_WORKSPACE = range(8)
 F32, BF16 = 0, 1
-ACCEPT_LOGITS, ACCEPT_Q_ONEHOT, ACCEPT_DECIDE_ONLY = 1, 2, 4
+ACCEPT_LOGITS, ACCEPT_Q_ONEHOT, ACCEPT_DECIDE_ONLY, ACCEPT_Q_STEP_MAJOR = 1, 2, 4, 8
 
 c_int, c_float, c_size_t, c_void_p, c_int64 = ctypes.c_int, ctypes.c_float, ctypes.c_size_t, ctypes.c_void_p, ctypes.c_int64
 
@@ -58,7 +58,9 @@ PROTOTYPES: dict[str, tuple] = {
     "specb200_ngram": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "specb200_commit_tokens": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                        c_int, c_void_p]),
-    "specb200_verify_ids": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p]),
+    "specb200_verify_ids": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p,
+                                    c_void_p, c_void_p]),
+    "specb200_scatter_tokens": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "specb200_model_create": (c_int, [ctypes.POINTER(ModelConfig), ctypes.POINTER(ModelWeights),
                                       ctypes.POINTER(c_void_p)]),
     "specb200_model_destroy": (c_int, [c_void_p]),

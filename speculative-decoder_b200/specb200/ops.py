@@ -145,9 +145,12 @@ def commit_tokens(ctx: torch.Tensor, ctx_len: torch.Tensor, draft: torch.Tensor,
     raise_for(rc, "specb200_commit_tokens")
 
 
-def verify_ids(ctx: torch.Tensor, ctx_len: torch.Tensor, draft: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+def verify_ids(ctx: torch.Tensor, ctx_len: torch.Tensor, draft: torch.Tensor, out: torch.Tensor,
+               active: torch.Tensor | None = None, past: torch.Tensor | None = None,
+               n_new: torch.Tensor | None = None) -> torch.Tensor:
     b, stride = ctx.shape
     k = draft.shape[1]
-    rc = lib().specb200_verify_ids(ptr(ctx), stride, ptr(ctx_len), ptr(draft), b, k, ptr(out), stream_ptr(ctx.device))
+    rc = lib().specb200_verify_ids(ptr(ctx), stride, ptr(ctx_len), ptr(draft), ptr(active), b, k, ptr(out), ptr(past),
+                                   ptr(n_new), stream_ptr(ctx.device))
     raise_for(rc, "specb200_verify_ids")
     return out

@@ -92,9 +92,18 @@ def test_forward_bf16_matches_oracle(dims):
             assert np.all(agree | (gap < 2e-2 * scale)), (b, gap[~agree])
 
 
-# ---------------------------------------------------------------- generate (composable path)
+# ---------------------------------------------------------------- generate
+@pytest.fixture(params=["fused", "composable"])
+def path(request, monkeypatch):
+    """Run generate() through the CUDA-graph round (engine drafters) or through the
+    module-by-module path that custom drafters and patched verify/accept_reject take."""
+    if request.param == "composable":
+        monkeypatch.setattr("specb200.rounds.fused_path_available", lambda *a: False)
+    return request.param
+
+
 @pytest.mark.parametrize("name", ["ngram_k1", "ngram_k4", "draft_k1", "draft_k4"])
-def test_generate_matches_reference(tiny, golden_generate, name):
+def test_generate_matches_reference(tiny, golden_generate, name, path):
     """Greedy spec.loop.generate on the fp32 engine reproduces the reference's fp64 outputs
     and every SpecStats counter."""
     from spec.draft import ModelDraft
@@ -111,6 +120,32 @@ def test_generate_matches_reference(tiny, golden_generate, name):
     assert out == want["outputs"]
     for key in ("rounds", "drafted", "accepted", "attempts", "accepts", "emitted_per_round", "drafted_per_round"):
         assert getattr(st, key) == want[key], key
+
+
+def test_sampled_generate_matches_reference(tiny, golden_generate, path):
+    """Temperature 1 with a seeded generator: the uniforms are drawn in the reference's order,
+    so draft samples, accept decisions and residual samples reproduce its output."""
+    from spec.draft import ModelDraft
+    from spec.loop import generate
+
+    g = golden_generate
+    d = early_exit(tiny)
+    out, st = generate(tiny, new_cache(tiny), ModelDraft(d, new_cache(d)), g["prompts"][:6], 16, k=3,
+                       temperature=1.0, generator=torch.Generator().manual_seed(5))
+    assert out == g["sampled_draft_k3"]["outputs"]
+    assert (st.accepted, st.drafted) == (g["sampled_draft_k3"]["accepted"], g["sampled_draft_k3"]["drafted"])
+
+
+def test_fused_path_is_taken_for_engine_drafters(tiny, monkeypatch):
+    from spec.loop import generate
+    from spec.ngram import NGramDraft
+    from specb200 import rounds
+
+    calls = []
+    real = rounds.generate_fused
+    monkeypatch.setattr(rounds, "generate_fused", lambda *a, **kw: calls.append(1) or real(*a, **kw))
+    out, _ = generate(tiny, new_cache(tiny), NGramDraft(256), [[1, 2, 3, 1, 2]], 8, k=4)
+    assert calls == [1] and len(out[0]) == 8
 
 
 def test_plain_decode_matches_reference(tiny, golden_generate):
