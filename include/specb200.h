@@ -74,6 +74,20 @@ int specb200_accept(const float* p, const float* q, const int64_t* draft, const 
                     int64_t* n_accepted, int64_t* next_token, int32_t* status, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of specb200_accept (no counterpart in the reference): same
+ * arguments and results, minus the workspace. For callers that cannot allocate device memory
+ * or hold a scratch buffer for this library (a runtime that reserves all HBM up front and
+ * forbids later cudaMalloc, or an operator interface that passes only inputs and outputs).
+ * Its scratch is a fixed device array inside the library (about 250 KB per GPU, held until
+ * exit), so B is limited to specb200_accept_noalloc_max_rows() (512) and k to 15; larger
+ * calls return SPECB200_ERR_ARG. The first call on each device looks up the array's device
+ * address with that device current: make it before any stream capture. Every call shares the
+ * array: calls that overlap on the GPU race, so serialise them (one stream per process). */
+size_t specb200_accept_noalloc_max_rows(void);
+int specb200_accept_noalloc(const float* p, const float* q, const int64_t* draft, const float* u_accept,
+                            const float* u_residual, int B, int k, int V, int flags, float temperature,
+                            int64_t* n_accepted, int64_t* next_token, int32_t* status, void* stream);
+
 /* probabilities() of lm/sampling.py:13-18 written out as rows: out[r] = one-hot of the first
  * maximum of logits[r] at temperature 0, else softmax(logits[r] / temperature). [rows, V]. */
 int specb200_probabilities(const float* logits, int rows, int V, float temperature, float* out, void* stream);

@@ -423,3 +423,103 @@ extern "C" int specb200_probabilities(const float* logits, int rows, int V, floa
   if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
   return SPECB200_OK;
 }
+
+// ---------------------------------------------------------------------------------------
+// Allocation-free variant of specb200_accept.
+//
+// Some callers cannot hand this library a workspace: a serving runtime that reserves all of
+// HBM for weights and KV pages at start-up and treats any later cudaMalloc as an error, or a
+// plugin host whose operator interface passes only input and output buffers. For them the
+// accept kernel's scratch (one ticket counter per row and the per-row statistics) lives in
+// g_accept_scratch, a file-scope device array of fixed size that every GPU loading this
+// library holds until the process exits. Limits: B <= kNoAllocMaxB rows and k <= 15.
+//
+// Host code cannot use g_accept_scratch as an address (on the host the name is only a
+// stand-in for the device symbol), so the first call on each device, with that device
+// current, looks the address up with cudaGetSymbolAddress and caches it; make that first call
+// before any stream capture. All calls share the array and it keeps the last call's contents:
+// the counters that must start at zero are cleared by every call, and two calls that overlap
+// on the GPU (different streams, or different host threads) race on it.
+// ---------------------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+constexpr int kNoAllocMaxB = 512;
+constexpr int kNoAllocMaxK = 15;
+constexpr size_t kNoAllocCounterBytes = ((kNoAllocMaxB * sizeof(int) + 255) / 256) * 256;
+constexpr size_t kNoAllocScratchBytes =
+    kNoAllocCounterBytes + static_cast<size_t>(kNoAllocMaxB) * (2 * kNoAllocMaxK + 1) * sizeof(RowStat);
+
+static __device__ __align__(256) unsigned char g_accept_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of g_accept_scratch on the current device, looked up once per device.
+int scratch_for_current_device(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return specb200_set_error(SPECB200_ERR_ARG, "accept_noalloc: device index too large");
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_accept_scratch);
+    if (e != cudaSuccess || !p) return specb200_set_error(SPECB200_ERR_CUDA, "accept_noalloc: cudaGetSymbolAddress failed");
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return SPECB200_OK;
+}
+}  // namespace
+
+extern "C" size_t specb200_accept_noalloc_max_rows(void) { return kNoAllocMaxB; }
+
+extern "C" int specb200_accept_noalloc(const float* p, const float* q, const int64_t* draft, const float* u_accept,
+                                       const float* u_residual, int B, int k, int V, int flags, float temperature,
+                                       int64_t* n_accepted, int64_t* next_token, int32_t* status, void* stream) {
+  if (B <= 0 || k < 0 || V <= 0) return specb200_set_error(SPECB200_ERR_ARG, "accept_noalloc: bad B/k/V");
+  if (B > kNoAllocMaxB || k > kNoAllocMaxK)
+    return specb200_set_error(SPECB200_ERR_ARG,
+                              "accept_noalloc: B must be <= 512 and k <= 15 (fixed device scratch); "
+                              "use specb200_accept with a caller workspace for larger batches");
+  if (!p || !n_accepted || !u_residual) return specb200_set_error(SPECB200_ERR_ARG, "accept_noalloc: null pointer");
+  if (k > 0 && (!draft || !u_accept)) return specb200_set_error(SPECB200_ERR_ARG, "accept_noalloc: null draft/u_accept");
+  if (!(flags & SPECB200_ACCEPT_DECIDE_ONLY) && !next_token)
+    return specb200_set_error(SPECB200_ERR_ARG, "accept_noalloc: null next_token");
+  const bool logits = flags & SPECB200_ACCEPT_LOGITS;
+  if (logits && !(temperature >= 0.f)) return specb200_set_error(SPECB200_ERR_ARG, "accept_noalloc: temperature < 0");
+  void* scratch = nullptr;
+  int rc = scratch_for_current_device(&scratch);
+  if (rc != SPECB200_OK) return rc;
+  AcceptArgs a;
+  a.p = p;
+  a.q = q;
+  a.draft = draft;
+  a.u_accept = u_accept;
+  a.u_residual = u_residual;
+  a.B = B;
+  a.k = k;
+  a.V = V;
+  a.q_onehot = (flags & SPECB200_ACCEPT_Q_ONEHOT) ? 1 : 0;
+  a.q_present = (k > 0) && (q != nullptr || a.q_onehot);
+  a.R = (k + 1) + ((a.q_present && !a.q_onehot) ? k : 0);
+  a.logits = logits ? 1 : 0;
+  a.greedy = (logits && temperature == 0.f) ? 1 : 0;
+  a.decide_only = (flags & SPECB200_ACCEPT_DECIDE_ONLY) ? 1 : 0;
+  a.q_step_major = (flags & SPECB200_ACCEPT_Q_STEP_MAJOR) ? 1 : 0;
+  a.temperature = temperature;
+  a.n_accepted = n_accepted;
+  a.next_token = next_token;
+  a.status = status;
+  a.counters = static_cast<int*>(scratch);
+  a.stats = reinterpret_cast<RowStat*>(static_cast<char*>(scratch) + kNoAllocCounterBytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (status) cudaMemsetAsync(status, 0, sizeof(int32_t), s);
+  cudaMemsetAsync(a.counters, 0, static_cast<size_t>(B) * sizeof(int), s);  // the array keeps old tickets
+  accept_kernel<<<static_cast<unsigned>(a.R) * B, kAcceptThreads, 0, s>>>(a);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
+  return SPECB200_OK;
+}

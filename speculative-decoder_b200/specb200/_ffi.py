@@ -55,6 +55,9 @@ PROTOTYPES: dict[str, tuple] = {
     "specb200_accept": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float,
                                 c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "specb200_probabilities": (c_int, [c_void_p, c_int, c_int, c_float, c_void_p, c_void_p]),
+    "specb200_accept_noalloc_max_rows": (c_size_t, []),
+    "specb200_accept_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int,
+                                        c_float, c_void_p, c_void_p, c_void_p, c_void_p]),
     "specb200_ngram": (c_int, [c_void_p, c_int64, c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
     "specb200_commit_tokens": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
                                        c_int, c_void_p]),
