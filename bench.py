@@ -50,6 +50,21 @@ KV_BYTES_PER_TOKEN = 196_608          # 24 layers x 2 x 32 heads x 64 x 2 B
 ACCEPT_BYTES = 113_246_208            # config 3: 64 x (5 + 4) x 49152 x 4 B
 
 
+def weight_bytes(spec: dict) -> int:
+    """bf16 bytes of every weight read once per forward: linears, RMSNorm weights and the tied
+    embedding/head (3,422,752,768 B for the 1.7B architecture)."""
+    H, L, I, V = spec["hidden_size"], spec["num_hidden_layers"], spec["intermediate_size"], spec["vocab_size"]
+    d = H // spec["num_attention_heads"]
+    qkv = H * (spec["num_attention_heads"] + 2 * spec["num_key_value_heads"]) * d
+    per_layer = qkv + spec["num_attention_heads"] * d * H + 3 * H * I
+    return 2 * (L * per_layer + V * H + (2 * L + 1) * H)
+
+
+def kv_bytes_per_token(spec: dict) -> int:
+    d = spec["hidden_size"] // spec["num_attention_heads"]
+    return spec["num_hidden_layers"] * 2 * spec["num_key_value_heads"] * d * 2
+
+
 def log(*a):
     print(*a, file=sys.stderr, flush=True)
 
@@ -130,7 +145,32 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30) -> dict:
+def trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
+    """Per phase kind, medians over CTAs and layers (us) from the layer-stream kernel's
+    globaltimer stamps [grid, phases, 8]: barrier wait (and its minimum over CTAs: the last
+    arriver's, i.e. the barrier's own latency), operand build, MMA span, first accumulator,
+    work after the barrier (median and max over CTAs)."""
+    t = trace.double().cpu()
+
+    def med(x):
+        return float(x.median()) if x.numel() else None
+
+    out = {}
+    for j, name in enumerate(["qkv", "attn", "o", "gate_up", "down"]):
+        ph = t[:, [1 + 5 * l + j for l in range(n_layers)], :]
+        ok = ph[..., 3] > 0
+        d = lambda a, b: (ph[..., a] - ph[..., b])[ok & (ph[..., a] > 0) & (ph[..., b] > 0)] / 1e3  # noqa: E731
+        bar = d(1, 0)
+        per_layer_min = ((ph[..., 1] - ph[..., 0]).where(ok, torch.tensor(float("inf"))).amin(0)) / 1e3
+        out[name] = {"barrier_us": med(bar), "barrier_min_us": med(per_layer_min), "operand_us": med(d(2, 1)),
+                     "mma_span_us": med(d(5, 4)), "first_acc_us": med(d(6, 1)), "work_us": med(d(3, 1)),
+                     "work_max_us": float(d(3, 1).max()) if d(3, 1).numel() else None}
+    first = t[:, 0, 0][t[:, 0, 0] > 0].min()
+    out["total_us"] = float((t[:, :, 3].max() - first) / 1e3)
+    return out
+
+
+def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30, trace: bool = False) -> dict:
     """The (k+1)-token target forward of one round at B=1 with `context_len` cached tokens,
     captured in a CUDA graph and replayed; CUDA events on the replay stream."""
     from specb200.engine import engine_for
@@ -173,8 +213,62 @@ def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30
     ms = st.elapsed_time(en) / reps
     assert int(status.item()) == 0
     kv_tokens = past + K + 1
-    return {"us": ms * 1e3, "bytes": WEIGHT_BYTES + KV_BYTES_PER_TOKEN * kv_tokens, "context": kv_tokens,
-            "launches_per_step": 3 + 7 * TARGET["num_hidden_layers"]}
+    spec = dict(TARGET, num_hidden_layers=target.config.num_hidden_layers)
+    r = {"us": ms * 1e3, "bytes": weight_bytes(spec) + kv_bytes_per_token(spec) * kv_tokens, "context": kv_tokens,
+         "layers": spec["num_hidden_layers"]}
+    if trace:
+        n_ph = 2 + 5 * spec["num_hidden_layers"]
+        tr = torch.zeros(torch.cuda.get_device_properties(device).multi_processor_count, n_ph, 8, dtype=torch.int64,
+                         device=device)
+        eng.forward_device(cache, ids, n_new, pastt, table, cap, False, logits, status, ws, trace=tr)
+        torch.cuda.synchronize()
+        r["trace"] = trace_summary(tr, spec["num_hidden_layers"])
+    return r
+
+
+def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30) -> dict:
+    """One single-token draft-model forward (135M architecture, B=1), CUDA graph, as in each
+    of the k draft steps of a round."""
+    from specb200.engine import engine_for
+
+    eng = engine_for(draft)
+    cache = cache_cls.for_model(draft.config, num_blocks=(context_len + 64) // BLOCK + 4, block_size=BLOCK,
+                                dtype=torch.bfloat16, device=device)
+    cache.add(0)
+    past = cache.reserve([0], [context_len])[0]
+    cap = context_len + 64
+    table = torch.zeros(1, -(-cap // BLOCK), dtype=torch.int32, device=device)
+    blocks = cache.tables[0].blocks
+    table[0, : len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+    ids = torch.randint(0, DRAFT["vocab_size"], (1, 1), dtype=torch.int32, device=device)
+    one = torch.ones(1, dtype=torch.int32, device=device)
+    pastt = torch.tensor([context_len - 1], dtype=torch.int32, device=device)
+    logits = torch.empty(1, DRAFT["vocab_size"], dtype=torch.float32, device=device)
+    status = torch.zeros(1, dtype=torch.int32, device=device)
+    ws = torch.zeros(eng.workspace_bytes(1, 1, cap), dtype=torch.uint8, device=device)
+    run = lambda: eng.forward_device(cache, ids, one, pastt, table, cap, True, logits, status, ws)  # noqa: E731
+    run()
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=side):
+        run()
+    torch.cuda.current_stream(device).wait_stream(side)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(reps):
+        g.replay()
+    en.record()
+    en.synchronize()
+    del past
+    spec = dict(DRAFT, num_hidden_layers=draft.config.num_hidden_layers)
+    return {"us": st.elapsed_time(en) / reps * 1e3,
+            "bytes": weight_bytes(spec) + kv_bytes_per_token(spec) * context_len, "context": context_len,
+            "layers": spec["num_hidden_layers"]}
 
 
 def time_accept(device, reps: int = 20) -> dict:
@@ -237,6 +331,13 @@ def main() -> None:
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="with --only: build the models with this many layers (smaller profiling runs)")
+    ap.add_argument("--trace", action="store_true",
+                    help="with --only verify/draft: per-phase timings of the layer-stream kernel")
+    ap.add_argument("--only", choices=["verify", "accept", "draft"],
+                    help="time one piece alone (for profiling): the verify forward, the accept kernel or one "
+                         "draft-model forward step")
     args = ap.parse_args()
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -271,6 +372,24 @@ def main() -> None:
 
     device = torch.device("cuda", local)
     torch.cuda.set_device(device)
+    if args.only:
+        from cache.kv import KVCache
+
+        pk = peaks()
+        if args.only == "accept":
+            r = time_accept(device, reps=max(1, args.steps))
+        elif args.only == "verify":
+            spec = dict(TARGET, num_hidden_layers=args.layers or TARGET["num_hidden_layers"])
+            r = time_verify_step(make_model(spec, 0, device), KVCache, device, PROMPT_LEN + NEW_TOKENS // 2,
+                                 reps=max(1, args.steps), trace=args.trace)
+        else:
+            spec = dict(DRAFT, num_hidden_layers=args.layers or DRAFT["num_hidden_layers"])
+            r = time_draft_step(make_model(spec, 1, device), KVCache, device, PROMPT_LEN + NEW_TOKENS // 2,
+                                reps=max(1, args.steps))
+        r["gbs"] = r["bytes"] / (r["us"] * 1e-6) / 1e9
+        r["frac"] = r["gbs"] / pk["hbm_gbs"]
+        print(json.dumps({"only": args.only, **r}))
+        return
     if world > 1:
         import datetime
 

@@ -107,25 +107,41 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, RowStat* out) 
     }
     return;
   }
-  // softmax statistics of z = x / T, online per thread
+  // softmax statistics of z = x / T, online per thread: 8 float4 (32 values) per chunk, one
+  // rescale per chunk; at T == 1 the division is skipped (x / 1 is exact)
   const float T = a.temperature;
+  const bool unit_t = (T == 1.f);
   float m = -INFINITY, s = 0.f;
   if (vec) {
     const float4* r4 = reinterpret_cast<const float4*>(row);
     const int n4 = a.V / 4;
-#pragma unroll 8
-    for (int j = tid; j < n4; j += kAcceptThreads) {
-      float4 v = __ldg(r4 + j);
-      float z0 = v.x / T, z1 = v.y / T, z2 = v.z / T, z3 = v.w / T;
-      float mx = fmaxf(fmaxf(fmaxf(z0, z1), fmaxf(z2, z3)), m);
+    constexpr int kU = 8;
+    for (int j0 = tid; j0 < n4; j0 += kU * kAcceptThreads) {
+      float z[kU * 4];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int j = j0 + u * kAcceptThreads;
+        float4 v = j < n4 ? __ldg(r4 + j) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        z[4 * u] = v.x; z[4 * u + 1] = v.y; z[4 * u + 2] = v.z; z[4 * u + 3] = v.w;
+      }
+      float mx = m;
+#pragma unroll
+      for (int i = 0; i < kU * 4; ++i) {
+        if (!unit_t) z[i] = z[i] / T;
+        mx = fmaxf(mx, z[i]);
+      }
       if (mx != -INFINITY) {
-        s = s * expf(m - mx) + expf(z0 - mx) + expf(z1 - mx) + expf(z2 - mx) + expf(z3 - mx);
+        float acc = s * expf(m - mx);
+#pragma unroll
+        for (int i = 0; i < kU * 4; ++i) acc += expf(z[i] - mx);
+        s = acc;
         m = mx;
       }
     }
   } else {
     for (int j = tid; j < a.V; j += kAcceptThreads) {
-      float z = __ldg(row + j) / T;
+      float z = __ldg(row + j);
+      if (!unit_t) z = z / T;
       float mx = fmaxf(z, m);
       if (mx != -INFINITY) {
         s = s * expf(m - mx) + expf(z - mx);
@@ -157,8 +173,54 @@ SPECB200_DEVINL float prob_at(const AcceptArgs& a, const float* row, const RowSt
 }
 
 // Residual sampling at row n: r = max(0, p_n - q_n); sample by inverse CDF with u.
+// Pass A: the row is cut into 128-element segments (one warp x 4 consecutive elements per
+// lane); every warp sums its segments (float4 loads, several segments in flight) into
+// shared memory. The total gives the target u * total; warp 0 scans the segment sums to find
+// the segment holding the crossing, then scans that segment element by element (pass B).
+// Sums accumulate in double so both passes agree except within a few ulps of a boundary.
+constexpr int kSeg = 128;
+constexpr int kMaxSegs = 4096;  // V <= 524288
+SPECB200_DEVINL void seg_values(const AcceptArgs& a, const float* prow, const RowStat& ps, float p_inv,
+                                const float* qrow, const RowStat& qs, float q_inv, bool q_row, bool q_hot,
+                                int64_t dn, int use_p, int x0, float (&v)[4]) {
+  // 4 consecutive elements x0..x0+3 (x0 % 4 == 0); out-of-range elements are 0
+  float pv[4], qv[4] = {0.f, 0.f, 0.f, 0.f};
+  const bool full = x0 + 3 < a.V;
+  const bool vec = full && (a.V % 4 == 0);
+  if (vec) {
+    const float4 t = *reinterpret_cast<const float4*>(prow + x0);
+    pv[0] = t.x; pv[1] = t.y; pv[2] = t.z; pv[3] = t.w;
+    if (q_row && !use_p) {
+      const float4 u = *reinterpret_cast<const float4*>(qrow + x0);
+      qv[0] = u.x; qv[1] = u.y; qv[2] = u.z; qv[3] = u.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      pv[j] = x0 + j < a.V ? prow[x0 + j] : -INFINITY;
+      if (q_row && !use_p) qv[j] = x0 + j < a.V ? qrow[x0 + j] : -INFINITY;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (x0 + j >= a.V) { v[j] = 0.f; continue; }
+    float px = pv[j];
+    if (a.logits) px = expf((a.temperature == 1.f ? px : px / a.temperature) - ps.m) * p_inv;
+    if (use_p) { v[j] = px; continue; }
+    float qx = 0.f;
+    if (q_row) {
+      qx = qv[j];
+      if (a.logits) qx = expf((a.temperature == 1.f ? qx : qx / a.temperature) - qs.m) * q_inv;
+    } else if (q_hot) {
+      qx = (x0 + j == dn) ? 1.f : 0.f;
+    }
+    v[j] = fmaxf(px - qx, 0.f);  // torch.clamp(p - q, min=0)
+  }
+}
+
 __device__ int64_t residual_sample(const AcceptArgs& a, int b, int n, const RowStat* st) {
-  __shared__ double sh_chunk[kAcceptWarps];
+  __shared__ double sh_seg[kMaxSegs];
+  __shared__ double sh_part[kAcceptWarps];
   __shared__ double sh_total;
   __shared__ int64_t sh_token;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -173,66 +235,97 @@ __device__ int64_t residual_sample(const AcceptArgs& a, int b, int n, const RowS
   const float* qrow = q_row ? row_ptr(a, b, a.k + 1 + n) : nullptr;
   const RowStat qs = q_row ? st[a.k + 1 + n] : RowStat{0.f, 1.f, 0.f, 0};
   const float q_inv = 1.0f / qs.s;
-  const int chunk = ((a.V + kAcceptWarps - 1) / kAcceptWarps + 31) / 32 * 32;
+  const int nseg = (a.V + kSeg - 1) / kSeg;
 
-  auto value = [&](int x, int use_p) -> float {
-    float px = prob_at(a, prow, ps, p_inv, x);
-    if (use_p) return px;
-    float qx = 0.f;
-    if (q_row) qx = prob_at(a, qrow, qs, q_inv, x);
-    else if (q_hot) qx = (x == dn) ? 1.f : 0.f;
-    return fmaxf(px - qx, 0.f);  // torch.clamp(p - q, min=0)
-  };
-
-  // Chunk sums of the residual (or of p when the residual has no mass), in warp order.
-  auto chunk_sums = [&](int use_p) {
-    const int c0 = warp * chunk, c1 = min(a.V, c0 + chunk);
-    double acc = 0.0;
-    for (int x = c0 + lane; x < c1; x += 32) acc += static_cast<double>(value(x, use_p));
-    acc = warp_sum_d(acc);
-    if (lane == 0) sh_chunk[warp] = acc;
+  auto segment_sums = [&](int use_p) {
+    for (int s0 = warp; s0 < nseg; s0 += 4 * kAcceptWarps) {
+      double acc[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int sg = s0 + u * kAcceptWarps;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (sg < nseg) seg_values(a, prow, ps, p_inv, qrow, qs, q_inv, q_row, q_hot, dn, use_p, sg * kSeg + 4 * lane, v);
+        acc[u] = static_cast<double>(v[0]) + v[1] + v[2] + v[3];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const double t = warp_sum_d(acc[u]);
+        const int sg = s0 + u * kAcceptWarps;
+        if (lane == 0 && sg < nseg) sh_seg[sg] = t;
+      }
+    }
+    __syncthreads();
+    double t = 0.0;
+    for (int sg = tid; sg < nseg; sg += kAcceptThreads) t += sh_seg[sg];
+    t = warp_sum_d(t);
+    if (lane == 0) sh_part[warp] = t;
     __syncthreads();
     if (tid == 0) {
-      double t = 0.0;
-      for (int w = 0; w < kAcceptWarps; ++w) t += sh_chunk[w];
-      sh_total = t;
+      double tot = 0.0;
+      for (int w = 0; w < kAcceptWarps; ++w) tot += sh_part[w];
+      sh_total = tot;
     }
     __syncthreads();
   };
-  chunk_sums(0);
+  segment_sums(0);
   int use_p = 0;
   if (!(sh_total > 0.0)) {  // residual sums to 0: residual_distribution falls back to p
     use_p = 1;
-    chunk_sums(1);
+    segment_sums(1);
   }
   const double target = static_cast<double>(a.u_residual[b]) * sh_total;
   if (tid == 0) sh_token = a.V - 1;  // searchsorted past the end, clamped
   __syncthreads();
   if (warp == 0) {
-    // first chunk whose running sum passes the target, then a sequential warp scan from there
+    // first segment whose running sum passes the target (warp scan over segment sums)
     double base = 0.0;
-    int w0 = kAcceptWarps;
-    for (int w = 0; w < kAcceptWarps; ++w) {
-      if (base + sh_chunk[w] > target) { w0 = w; break; }
-      base += sh_chunk[w];
-    }
-    if (w0 < kAcceptWarps) {
-      bool found = false;
-      for (int x0 = w0 * chunk; x0 < a.V && !found; x0 += 32) {
-        const int x = x0 + lane;
-        double v = x < a.V ? static_cast<double>(value(x, use_p)) : 0.0;
+    int s_hit = nseg;
+    for (int s0 = 0; s0 < nseg && s_hit == nseg; s0 += 32) {
+      const int sg = s0 + lane;
+      double v = sg < nseg ? sh_seg[sg] : 0.0;
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          double t = __shfl_up_sync(0xffffffffu, v, o);
-          if (lane >= o) v += t;
-        }
-        const unsigned hit = __ballot_sync(0xffffffffu, x < a.V && base + v > target);
-        if (hit) {
-          if (lane == 0) sh_token = x0 + __ffs(hit) - 1;
-          found = true;
-        }
+      for (int o = 1; o < 32; o <<= 1) {
+        const double t = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += t;
+      }
+      const unsigned hit = __ballot_sync(0xffffffffu, sg < nseg && base + v > target);
+      if (hit) {
+        const int l = __ffs(hit) - 1;
+        s_hit = s0 + l;
+        const double before = __shfl_sync(0xffffffffu, v, l) - __shfl_sync(0xffffffffu, sg < nseg ? sh_seg[sg] : 0.0, l);
+        base += before;
+      } else {
         base += __shfl_sync(0xffffffffu, v, 31);
       }
+    }
+    // element scan from that segment on (continues if rounding put the crossing later)
+    for (int sg = s_hit; sg < nseg; ++sg) {
+      float v4[4];
+      seg_values(a, prow, ps, p_inv, qrow, qs, q_inv, q_row, q_hot, dn, use_p, sg * kSeg + 4 * lane, v4);
+      double e[4];
+      e[0] = v4[0];
+      e[1] = e[0] + v4[1];
+      e[2] = e[1] + v4[2];
+      e[3] = e[2] + v4[3];
+      double lsum = e[3];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double t = __shfl_up_sync(0xffffffffu, lsum, o);
+        if (lane >= o) lsum += t;
+      }
+      const double excl = base + lsum - e[3];
+      int first = 4;
+#pragma unroll
+      for (int j = 3; j >= 0; --j)
+        if (sg * kSeg + 4 * lane + j < a.V && excl + e[j] > target) first = j;
+      const unsigned hit = __ballot_sync(0xffffffffu, first < 4);
+      if (hit) {
+        const int l = __ffs(hit) - 1;
+        const int fj = __shfl_sync(0xffffffffu, first, l);
+        if (lane == 0) sh_token = sg * kSeg + 4 * l + fj;
+        break;
+      }
+      base += __shfl_sync(0xffffffffu, lsum, 31);
     }
   }
   __syncthreads();
@@ -372,7 +465,8 @@ extern "C" int specb200_accept(const float* p, const float* q, const int64_t* dr
                                const float* u_residual, int B, int k, int V, int flags, float temperature,
                                int64_t* n_accepted, int64_t* next_token, int32_t* status, void* workspace,
                                size_t workspace_bytes, void* stream) {
-  if (B <= 0 || k < 0 || V <= 0 || k > 15) return specb200_set_error(SPECB200_ERR_ARG, "accept: bad B/k/V (k must be 0..15)");
+  if (B <= 0 || k < 0 || V <= 0 || k > 15 || V > kMaxSegs * kSeg)
+    return specb200_set_error(SPECB200_ERR_ARG, "accept: bad B/k/V (k must be 0..15, V <= 524288)");
   if (!p || !n_accepted || !workspace || !u_residual) return specb200_set_error(SPECB200_ERR_ARG, "accept: null pointer");
   if (k > 0 && (!draft || !u_accept)) return specb200_set_error(SPECB200_ERR_ARG, "accept: null draft/u_accept");
   if (!(flags & SPECB200_ACCEPT_DECIDE_ONLY) && !next_token) return specb200_set_error(SPECB200_ERR_ARG, "accept: null next_token");
@@ -479,7 +573,8 @@ extern "C" size_t specb200_accept_noalloc_max_rows(void) { return kNoAllocMaxB; 
 extern "C" int specb200_accept_noalloc(const float* p, const float* q, const int64_t* draft, const float* u_accept,
                                        const float* u_residual, int B, int k, int V, int flags, float temperature,
                                        int64_t* n_accepted, int64_t* next_token, int32_t* status, void* stream) {
-  if (B <= 0 || k < 0 || V <= 0) return specb200_set_error(SPECB200_ERR_ARG, "accept_noalloc: bad B/k/V");
+  if (B <= 0 || k < 0 || V <= 0 || V > kMaxSegs * kSeg)
+    return specb200_set_error(SPECB200_ERR_ARG, "accept_noalloc: bad B/k/V (V <= 524288)");
   if (B > kNoAllocMaxB || k > kNoAllocMaxK)
     return specb200_set_error(SPECB200_ERR_ARG,
                               "accept_noalloc: B must be <= 512 and k <= 15 (fixed device scratch); "

@@ -9,10 +9,13 @@
 // starts streaming its weights while the kernel before it drains. The whole sequence is
 // stream-ordered and allocation-free, so callers can capture it in a CUDA graph.
 #include <algorithm>
+#include <cstdlib>
 #include <vector>
 
+#include "attn_core.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
+#include "stream.cuh"
 
 namespace specb200 {
 namespace {
@@ -28,12 +31,37 @@ struct Model {
   std::vector<LayerMaps> maps;
   CUtensorMap head;
   int qkv_n;
+  bool stream_ok;  // packed weights present and shapes within the layer-stream kernel's limits
 };
+
+// Whether a call of this shape runs the persistent layer-stream kernel; fills its grid size
+// and the stream-K partial slots it needs.
+bool use_stream(const Model& m, int B, int T, int* grid, int* max_contrib) {
+  const specb200_model_config& c = m.cfg;
+  if (!m.stream_ok || B * T > kStreamBN) return false;
+  if (T * (m.cfg.n_heads / m.cfg.n_kv_heads) > 32) return false;  // one 32-row query tile per KV head
+  const int G = stream_grid_size();
+  if (G <= 0) return false;
+  if (!stream_units_fit(c.hidden, c.intermediate, G)) return false;
+  const int qd = c.n_heads * c.head_dim;
+  int mc = 1;
+  mc = std::max(mc, stream_max_contrib(m.qkv_n, c.hidden, G));
+  mc = std::max(mc, stream_max_contrib(c.hidden, qd, G));
+  mc = std::max(mc, stream_max_contrib(2 * c.intermediate, c.hidden, G));
+  mc = std::max(mc, stream_max_contrib(c.hidden, c.intermediate, G));
+  mc = std::max(mc, stream_max_contrib(c.vocab, c.hidden, G));
+  *grid = G;
+  *max_contrib = mc;
+  return true;
+}
 
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 struct Carve {
-  size_t gemm_counters, attn_counters, hidden, xbuf, qbuf, attn, act, pos, slot, gemm_parts, attn_parts, total;
+  size_t gemm_counters, attn_counters, stream_ctl, hidden, xbuf, qbuf, attn, act, pos, slot, gemm_parts, attn_parts,
+      stream_parts, total;
+  bool stream;
+  int grid, max_contrib;
   GemmShape g_qkv, g_o, g_gu, g_down, g_head;
   AttnPlan ap;
 };
@@ -51,12 +79,15 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   r.g_gu = plan_gemm(M, 2 * c.intermediate, c.hidden, tc);
   r.g_down = plan_gemm(M, c.hidden, c.intermediate, tc);
   r.g_head = plan_gemm(rows_out, c.vocab, c.hidden, tc);
-  r.ap = plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len);
+  r.stream = use_stream(m, B, T, &r.grid, &r.max_contrib);
+  r.ap = r.stream ? plan_attention_decode(B, c.n_kv_heads, max_kv_len, r.grid)
+                  : plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len);
   // The two ticket-counter regions sit at fixed offsets so that they stay zero across calls
   // of every shape; everything after them is rewritten before it is read.
   size_t off = 0;
   r.gemm_counters = off; off += align256(kGemmCounterBytes);
   r.attn_counters = off; off += align256(kAttnCounterBytes);
+  r.stream_ctl = off; off += 256;
   r.hidden = off; off += align256(static_cast<size_t>(M) * c.hidden * el);
   r.xbuf = off; off += align256(static_cast<size_t>(M) * c.hidden * el);
   r.qbuf = off; off += align256(static_cast<size_t>(M) * qd * el);
@@ -68,8 +99,81 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   for (const GemmShape* s : {&r.g_qkv, &r.g_o, &r.g_gu, &r.g_down, &r.g_head}) gws = std::max(gws, gemm_partials_bytes(*s));
   r.gemm_parts = off; off += align256(gws);
   r.attn_parts = off; off += align256(attention_partials_bytes(r.ap, B, c.n_kv_heads, c.head_dim));
+  r.stream_parts = off;
+  if (r.stream) {
+    const int max_tiles = std::max({(m.qkv_n + 127) / 128, (c.hidden + 127) / 128, (2 * c.intermediate + 127) / 128,
+                                    (c.vocab + 127) / 128});
+    off += align256(static_cast<size_t>(max_tiles) * r.max_contrib * kStreamBN * 128 * sizeof(float));
+  }
   r.total = off;
   return r;
+}
+
+int run_stream(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv, cudaStream_t s) {
+  const specb200_model_config& c = m.cfg;
+  const int B = bt.B, Tt = bt.T, M = B * Tt;
+  const int qd = c.n_heads * c.head_dim;
+  StreamArgs a = {};
+  a.n_layers = c.n_layers;
+  a.H = c.hidden;
+  a.Hq = c.n_heads;
+  a.Hkv = c.n_kv_heads;
+  a.D = c.head_dim;
+  a.I = c.intermediate;
+  a.V = c.vocab;
+  a.eps = c.rms_eps;
+  a.attn_scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
+  a.max_positions = c.max_positions;
+  a.embed = static_cast<const __nv_bfloat16*>(m.w.embed);
+  a.final_norm = static_cast<const __nv_bfloat16*>(m.w.final_norm);
+  a.head = static_cast<const uint8_t*>(m.w.p_lm_head);
+  a.rope_cos = m.w.rope_cos;
+  a.rope_sin = m.w.rope_sin;
+  for (int l = 0; l < c.n_layers; ++l) {
+    const specb200_layer_weights& L = m.layers[l];
+    a.layers[l].attn_norm = static_cast<const __nv_bfloat16*>(L.attn_norm);
+    a.layers[l].mlp_norm = static_cast<const __nv_bfloat16*>(L.mlp_norm);
+    a.layers[l].qkv = static_cast<const uint8_t*>(L.p_qkv);
+    a.layers[l].o = static_cast<const uint8_t*>(L.p_o);
+    a.layers[l].gu = static_cast<const uint8_t*>(L.p_gate_up);
+    a.layers[l].down = static_cast<const uint8_t*>(L.p_down);
+  }
+  a.B = B;
+  a.T = Tt;
+  a.M = M;
+  a.last_only = bt.last_only;
+  a.ids = bt.input_ids;
+  a.n_new = bt.n_new;
+  a.past = bt.past_len;
+  a.table = bt.block_table;
+  a.table_stride = bt.table_stride;
+  a.bs = bt.block_size;
+  a.num_slots = bt.num_slots;
+  a.k_pool = static_cast<__nv_bfloat16*>(bt.k_pool);
+  a.v_pool = static_cast<__nv_bfloat16*>(bt.v_pool);
+  a.logits = bt.logits;
+  a.h = reinterpret_cast<__nv_bfloat16*>(ws + cv.hidden);
+  a.q = reinterpret_cast<__nv_bfloat16*>(ws + cv.qbuf);
+  a.attn = reinterpret_cast<__nv_bfloat16*>(ws + cv.attn);
+  a.act = reinterpret_cast<__nv_bfloat16*>(ws + cv.act);
+  a.pos = reinterpret_cast<int32_t*>(ws + cv.pos);
+  a.slot = reinterpret_cast<int32_t*>(ws + cv.slot);
+  a.tile_counters = reinterpret_cast<int*>(ws + cv.gemm_counters);
+  a.partials = reinterpret_cast<float*>(ws + cv.stream_parts);
+  a.max_contrib = cv.max_contrib;
+  a.barrier = reinterpret_cast<unsigned*>(ws + cv.stream_ctl);
+  a.abort_flag = reinterpret_cast<int*>(ws + cv.stream_ctl + 64);
+  a.ap = cv.ap;
+  a.attn_counters = reinterpret_cast<int*>(ws + cv.attn_counters);
+  a.attn_partials = reinterpret_cast<float*>(ws + cv.attn_parts);
+  a.status = bt.status;
+  a.trace = reinterpret_cast<unsigned long long*>(bt.trace);
+  CUtensorMap map_attn{}, map_act{};
+  if (!make_tmap_bf16_2d(&map_attn, a.attn, qd, M, kTileK, kStreamBN) ||
+      !make_tmap_bf16_2d(&map_act, a.act, c.intermediate, M, kTileK, kStreamBN))
+    return SPECB200_ERR_ARG;
+  cudaMemsetAsync(ws + cv.stream_ctl, 0, 128, s);  // barrier arrivals/generation and the abort flag
+  return launch_stream(a, map_attn, map_act, cv.grid, s);
 }
 
 template <typename T>
@@ -217,6 +321,17 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
   m->layers.assign(weights->layers, weights->layers + c.n_layers);
   m->w.layers = m->layers.data();
   m->qkv_n = (c.n_heads + 2 * c.n_kv_heads) * c.head_dim;
+  m->stream_ok = c.dtype == SPECB200_BF16 && c.head_dim == 64 && c.n_layers <= kStreamMaxLayers &&
+                 c.hidden <= 2048 && c.n_heads * c.head_dim <= 2048 && c.hidden % 64 == 0 && weights->p_lm_head;
+  for (int l = 0; l < c.n_layers && m->stream_ok; ++l) {
+    const specb200_layer_weights& L = weights->layers[l];
+    m->stream_ok = L.p_qkv && L.p_o && L.p_gate_up && L.p_down;
+  }
+  // SPECB200_NO_STREAM=1 keeps every call on the per-layer kernels (used to compare paths).
+  const char* no_stream = std::getenv("SPECB200_NO_STREAM");
+  if (no_stream && no_stream[0] == '1') m->stream_ok = false;
+  // Size the persistent grid now, outside any stream capture (it sets a function attribute).
+  if (m->stream_ok && stream_grid_size() <= 0) m->stream_ok = false;
   if (c.dtype == SPECB200_BF16) {
     const int qd = c.n_heads * c.head_dim;
     m->maps.resize(c.n_layers);
@@ -261,8 +376,9 @@ extern "C" int specb200_forward(void* model, const specb200_batch* batch, void* 
   if (workspace_bytes < cv.total) return specb200_set_error(SPECB200_ERR_WORKSPACE, "forward: workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (bt.status) cudaMemsetAsync(bt.status, 0, sizeof(int32_t), s);
-  int rc = m.cfg.dtype == SPECB200_BF16 ? run_forward<__nv_bfloat16>(m, bt, static_cast<char*>(workspace), cv, s)
-                                        : run_forward<float>(m, bt, static_cast<char*>(workspace), cv, s);
+  int rc = cv.stream ? run_stream(m, bt, static_cast<char*>(workspace), cv, s)
+           : m.cfg.dtype == SPECB200_BF16 ? run_forward<__nv_bfloat16>(m, bt, static_cast<char*>(workspace), cv, s)
+                                          : run_forward<float>(m, bt, static_cast<char*>(workspace), cv, s);
   if (rc != SPECB200_OK) {
     cudaError_t e = cudaGetLastError();
     return specb200_set_error(rc, e != cudaSuccess ? cudaGetErrorString(e) : "forward: launch failed");

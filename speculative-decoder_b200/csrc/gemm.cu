@@ -20,88 +20,11 @@
 #include <algorithm>
 #include <mutex>
 
+#include "epilogue.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
 
 namespace specb200 {
-
-// ------------------------------------------------------------------------------ epilogue
-SPECB200_DEVINL void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
-
-// tile: fp32 [BN][kEpiPitch] in shared memory, column j = output feature n0 + j.
-// 128 threads; thread t owns feature column t.
-template <typename T>
-__device__ void apply_epilogue(const Epilogue& e, const float* tile, int n0, int m0, int valid, int N) {
-  const int t = threadIdx.x;
-  const int n = n0 + t;
-  switch (e.op) {
-    case EPI_STORE: {
-      if (n >= N) return;
-      for (int tok = 0; tok < valid; ++tok) {
-        const float v = tile[tok * kEpiPitch + t];
-        const int64_t o = static_cast<int64_t>(m0 + tok) * e.ldo + n;
-        if (e.out_f32) static_cast<float*>(e.out)[o] = v;
-        else static_cast<T*>(e.out)[o] = from_f32<T>(v);
-      }
-      return;
-    }
-    case EPI_RESID: {
-      if (n >= N) return;
-      T* out = static_cast<T*>(e.out);
-      for (int tok = 0; tok < valid; ++tok) {
-        const int64_t o = static_cast<int64_t>(m0 + tok) * e.ldo + n;
-        const float proj = round_to<T>(tile[tok * kEpiPitch + t]);
-        out[o] = from_f32<T>(to_f32<T>(out[o]) + proj);
-      }
-      return;
-    }
-    case EPI_SILU_MUL: {
-      if (t >= 64 || n >= N) return;
-      T* out = static_cast<T*>(e.out);
-      const int f = n0 / 2 + t;
-      for (int tok = 0; tok < valid; ++tok) {
-        const float g = round_to<T>(tile[tok * kEpiPitch + t]);
-        const float u = round_to<T>(tile[tok * kEpiPitch + 64 + t]);
-        const float act = round_to<T>(g / (1.0f + expf(-g)));
-        out[static_cast<int64_t>(m0 + tok) * e.ldo + f] = from_f32<T>(act * u);
-      }
-      return;
-    }
-    case EPI_QKV: {
-      if (n >= N) return;
-      const int d = e.head_dim, half = d / 2;
-      const int qd = e.n_heads * d, kd = e.n_kv_heads * d;
-      const int region = n < qd ? 0 : (n < qd + kd ? 1 : 2);
-      const int idx = n - (region == 0 ? 0 : (region == 1 ? qd : qd + kd));
-      const int h = idx / d, i = idx % d;
-      const int partner = i < half ? t + half : t - half;
-      for (int tok = 0; tok < valid; ++tok) {
-        const int m = m0 + tok;
-        float y = round_to<T>(tile[tok * kEpiPitch + t]);
-        if (region < 2) {
-          const float xp = round_to<T>(tile[tok * kEpiPitch + partner]);
-          const float rot = i < half ? -xp : xp;
-          const int64_t p = e.pos[m];
-          const float c = round_to<T>(e.rope_cos[p * half + (i % half)]);
-          const float s = round_to<T>(e.rope_sin[p * half + (i % half)]);
-          y = round_to<T>(round_to<T>(y * c) + round_to<T>(rot * s));
-        }
-        if (region == 0) {
-          static_cast<T*>(e.out)[static_cast<int64_t>(m) * e.ldo + n] = from_f32<T>(y);
-        } else {
-          const int slot = e.slot[m];
-          if (slot >= 0) {
-            T* pool = static_cast<T*>(region == 1 ? e.k_pool : e.v_pool);
-            pool[(static_cast<int64_t>(slot) * e.n_kv_heads + h) * d + i] = from_f32<T>(y);
-          }
-        }
-      }
-      return;
-    }
-    default:
-      return;
-  }
-}
 
 // Split-K reduction (when splits > 1) followed by the epilogue. Called by 128 threads that
 // hold this CTA's partial tile in `tile`; returns early in every CTA but the last of a tile.
@@ -124,10 +47,18 @@ __device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, 
     if (!sh_last) return;
     __threadfence();
     const float* base = parts + static_cast<size_t>(tile_id) * s.splits * tile_elems;
-    for (int tok = 0; tok < valid; ++tok) {
-      float acc = 0.f;
-      for (int sp = 0; sp < s.splits; ++sp) acc += __ldcg(base + sp * tile_elems + tok * kTileN + t);
-      tile[tok * kEpiPitch + t] = acc;
+    for (int t0 = 0; t0 < valid; t0 += kEpiBatch) {
+      float acc[kEpiBatch];
+#pragma unroll
+      for (int j = 0; j < kEpiBatch; ++j) acc[j] = 0.f;
+      for (int sp = 0; sp < s.splits; ++sp) {
+#pragma unroll
+        for (int j = 0; j < kEpiBatch; ++j)
+          if (t0 + j < valid) acc[j] += __ldcg(base + sp * tile_elems + (t0 + j) * kTileN + t);
+      }
+#pragma unroll
+      for (int j = 0; j < kEpiBatch; ++j)
+        if (t0 + j < valid) tile[(t0 + j) * kEpiPitch + t] = acc[j];
     }
     if (t == 0) counters[tile_id] = 0;
     epi_bar_sync();

@@ -32,19 +32,20 @@ class ModelConfig(ctypes.Structure):
 
 class LayerWeights(ctypes.Structure):
     _fields_ = [("attn_norm", c_void_p), ("w_qkv", c_void_p), ("w_o", c_void_p), ("mlp_norm", c_void_p),
-                ("w_gate_up", c_void_p), ("w_down", c_void_p)]
+                ("w_gate_up", c_void_p), ("w_down", c_void_p), ("p_qkv", c_void_p), ("p_o", c_void_p),
+                ("p_gate_up", c_void_p), ("p_down", c_void_p)]
 
 
 class ModelWeights(ctypes.Structure):
     _fields_ = [("embed", c_void_p), ("final_norm", c_void_p), ("lm_head", c_void_p), ("rope_cos", c_void_p),
-                ("rope_sin", c_void_p), ("layers", ctypes.POINTER(LayerWeights))]
+                ("rope_sin", c_void_p), ("layers", ctypes.POINTER(LayerWeights)), ("p_lm_head", c_void_p)]
 
 
 class Batch(ctypes.Structure):
     _fields_ = [("B", c_int), ("T", c_int), ("input_ids", c_void_p), ("n_new", c_void_p), ("past_len", c_void_p),
                 ("block_table", c_void_p), ("table_stride", c_int), ("block_size", c_int), ("num_slots", c_int),
                 ("k_pool", c_void_p), ("v_pool", c_void_p), ("last_only", c_int), ("logits", c_void_p),
-                ("max_kv_len", c_int), ("status", c_void_p)]
+                ("max_kv_len", c_int), ("status", c_void_p), ("trace", c_void_p)]
 
 
 # name -> (restype, argtypes)
@@ -64,6 +65,8 @@ PROTOTYPES: dict[str, tuple] = {
     "specb200_verify_ids": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p,
                                     c_void_p, c_void_p]),
     "specb200_scatter_tokens": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "specb200_packed_tile_bytes": (c_size_t, [c_int, c_int]),
+    "specb200_pack_tiles": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "specb200_model_create": (c_int, [ctypes.POINTER(ModelConfig), ctypes.POINTER(ModelWeights),
                                       ctypes.POINTER(c_void_p)]),
     "specb200_model_destroy": (c_int, [c_void_p]),

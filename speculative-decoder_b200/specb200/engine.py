@@ -92,13 +92,23 @@ class Engine:
             self.rope_cos = (freqs.cos() * scaling).to(device).contiguous()
             self.rope_sin = (freqs.sin() * scaling).to(device).contiguous()
 
+        # bf16 models also get their matrices in the tile-packed layout the layer-stream
+        # kernel streams (decode and verify calls with at most 16 token rows).
+        self.packed = dtype == torch.bfloat16
+        with torch.cuda.device(device):
+            for L in self.layers:
+                for name in ("w_qkv", "w_o", "w_gate_up", "w_down"):
+                    L["p_" + name[2:]] = self._pack(L[name]) if self.packed else None
+            self.p_lm_head = self._pack(self.lm_head) if self.packed else None
         self._c_layers = (_ffi.LayerWeights * self.n_layers)()
         for i, L in enumerate(self.layers):
             self._c_layers[i] = _ffi.LayerWeights(ptr(L["attn_norm"]), ptr(L["w_qkv"]), ptr(L["w_o"]), ptr(L["mlp_norm"]),
-                                                  ptr(L["w_gate_up"]), ptr(L["w_down"]))
+                                                  ptr(L["w_gate_up"]), ptr(L["w_down"]), ptr(L["p_qkv"]), ptr(L["p_o"]),
+                                                  ptr(L["p_gate_up"]), ptr(L["p_down"]))
         self._c_weights = _ffi.ModelWeights(ptr(self.embed), ptr(self.final_norm), ptr(self.lm_head),
                                             ptr(self.rope_cos), ptr(self.rope_sin),
-                                            ctypes.cast(self._c_layers, ctypes.POINTER(_ffi.LayerWeights)))
+                                            ctypes.cast(self._c_layers, ctypes.POINTER(_ffi.LayerWeights)),
+                                            ptr(self.p_lm_head))
         self._c_config = _ffi.ModelConfig(self.n_layers, self.hidden, self.n_heads, self.n_kv_heads, self.head_dim,
                                           self.intermediate, self.vocab, self.eps,
                                           _ffi.BF16 if dtype == torch.bfloat16 else _ffi.F32, self.max_positions)
@@ -107,6 +117,13 @@ class Engine:
             raise_for(lib().specb200_model_create(ctypes.byref(self._c_config), ctypes.byref(self._c_weights),
                                                   ctypes.byref(handle)), "specb200_model_create")
         self.handle = handle
+
+    @staticmethod
+    def _pack(w: torch.Tensor) -> torch.Tensor:
+        n, k = w.shape
+        out = torch.empty(lib().specb200_packed_tile_bytes(n, k), dtype=torch.uint8, device=w.device)
+        raise_for(lib().specb200_pack_tiles(ptr(w), n, k, ptr(out), stream_ptr(w.device)), "specb200_pack_tiles")
+        return out
 
     def __del__(self) -> None:
         h = getattr(self, "handle", None)
@@ -119,7 +136,8 @@ class Engine:
 
     def forward_device(self, cache, ids: torch.Tensor, n_new: torch.Tensor, past: torch.Tensor,
                        table: torch.Tensor, max_kv_len: int, last_only: bool, logits: torch.Tensor,
-                       status: torch.Tensor, workspace: torch.Tensor | None = None) -> None:
+                       status: torch.Tensor, workspace: torch.Tensor | None = None,
+                       trace: torch.Tensor | None = None) -> None:
         """Launch the forward on device-resident inputs (no host synchronisation).
         ids [B, T] int32, n_new/past [B] int32, table [B, W] int32, logits fp32 out."""
         b, t = ids.shape
@@ -129,7 +147,7 @@ class Engine:
             workspace = Workspace.get("forward", self.workspace_bytes(b, t, max_kv_len), self.device)
         batch = _ffi.Batch(b, t, ptr(ids), ptr(n_new), ptr(past), ptr(table), table.shape[1], cache.block_size,
                            cache.num_slots, ptr(cache.k), ptr(cache.v), int(last_only), ptr(logits), int(max_kv_len),
-                           ptr(status))
+                           ptr(status), ptr(trace))
         raise_for(lib().specb200_forward(self.handle, ctypes.byref(batch), ptr(workspace), workspace.numel(),
                                          stream_ptr(self.device)), "specb200_forward")
 
