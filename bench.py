@@ -457,11 +457,13 @@ def main() -> None:
     achieved = vstep["bytes"] / (vstep["us"] * 1e-6) / 1e9
     acc_gbs = acc["bytes"] / (acc["us"] * 1e-6) / 1e9
     alpha = stats.accepted / max(1, stats.drafted)
-    per_forward = lambda layers: 3 + 7 * layers  # noqa: E731  (prep, 7 per layer, final norm, head)
-    launches_per_round = K * (per_forward(DRAFT["num_hidden_layers"]) + 2) + 1 + per_forward(
-        TARGET["num_hidden_layers"]) + 2
-    launches = args.steps * (per_forward(TARGET["num_hidden_layers"]) + per_forward(DRAFT["num_hidden_layers"]) + 1) \
-        + rounds * launches_per_round
+    from specb200.engine import engine_for
+
+    te, de = engine_for(target), engine_for(draft)
+    # per round: k x (draft forward + sampler + token scatter), verify ids, verify forward,
+    # accept, commit; per step: target and draft prefill forwards and the first-token sampler
+    launches_per_round = K * (de.launches(1, 2) + 2) + 1 + te.launches(1, K + 1) + 2
+    launches = args.steps * (te.launches(1, PROMPT_LEN) + de.launches(1, PROMPT_LEN) + 1) + rounds * launches_per_round
     cb = None
     if not args.no_cpu_baseline and world == 1:
         try:

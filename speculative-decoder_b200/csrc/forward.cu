@@ -24,7 +24,13 @@ struct LayerMaps {
   CUtensorMap qkv, o, gu, down;
 };
 
+int env_int(const char* name, int def) {
+  const char* v = std::getenv(name);
+  return v && *v ? std::atoi(v) : def;
+}
+
 struct Model {
+  int prefetch_ahead = 1, ring_evict_first = 1;
   specb200_model_config cfg;
   specb200_model_weights w;
   std::vector<specb200_layer_weights> layers;
@@ -168,6 +174,8 @@ int run_stream(const Model& m, const specb200_batch& bt, char* ws, const Carve& 
   a.attn_partials = reinterpret_cast<float*>(ws + cv.attn_parts);
   a.status = bt.status;
   a.trace = reinterpret_cast<unsigned long long*>(bt.trace);
+  a.prefetch_ahead = m.prefetch_ahead;
+  a.ring_evict_first = m.ring_evict_first;
   CUtensorMap map_attn{}, map_act{};
   if (!make_tmap_bf16_2d(&map_attn, a.attn, qd, M, kTileK, kStreamBN) ||
       !make_tmap_bf16_2d(&map_act, a.act, c.intermediate, M, kTileK, kStreamBN))
@@ -327,9 +335,19 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
     const specb200_layer_weights& L = weights->layers[l];
     m->stream_ok = L.p_qkv && L.p_o && L.p_gate_up && L.p_down;
   }
+  // Small models stay on the per-layer kernels: with a few MB of weights per layer the
+  // persistent kernel's per-phase latency (grid barrier, operand build, reductions) costs more
+  // than the launches it saves (measured on the 135M draft: 1.62 vs 1.17 ms per step; on the
+  // 1.7B target: 2.30 vs 2.54 ms per verify).
+  const size_t layer_bytes = 2ull * c.hidden *
+                             (static_cast<size_t>(m->qkv_n) + static_cast<size_t>(c.n_heads) * c.head_dim + 3ull * c.intermediate);
+  if (layer_bytes < (32ull << 20)) m->stream_ok = false;
   // SPECB200_NO_STREAM=1 keeps every call on the per-layer kernels (used to compare paths).
   const char* no_stream = std::getenv("SPECB200_NO_STREAM");
   if (no_stream && no_stream[0] == '1') m->stream_ok = false;
+  // Layer-stream schedule knobs (L2 prefetch distance in GEMM phases; ring eviction hint).
+  m->prefetch_ahead = env_int("SPECB200_STREAM_PREFETCH", 0);  // measured: prefetching slows it
+  m->ring_evict_first = env_int("SPECB200_STREAM_EVICT_FIRST", 1);
   // Size the persistent grid now, outside any stream capture (it sets a function attribute).
   if (m->stream_ok && stream_grid_size() <= 0) m->stream_ok = false;
   if (c.dtype == SPECB200_BF16) {
@@ -350,6 +368,12 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
   }
   *handle = m;
   return SPECB200_OK;
+}
+
+extern "C" int specb200_forward_uses_stream(void* model, int B, int T) {
+  if (!model || B <= 0 || T <= 0) return 0;
+  int grid = 0, mc = 0;
+  return use_stream(*static_cast<Model*>(model), B, T, &grid, &mc) ? 1 : 0;
 }
 
 extern "C" int specb200_model_destroy(void* handle) {

@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 4) {
     // ------------------------------------------------------------ weight stream
     if (lane == 0) {
-      const uint64_t pol = l2_policy_evict_first();
+      const uint64_t pol = a.ring_evict_first ? l2_policy_evict_first() : l2_policy_evict_normal();
       uint32_t gu = 0;
       for (int p = 0; p < n_phases && !*abort_s; ++p) {
         if (!is_gemm(phase_kind(a, p))) continue;
@@ -411,15 +411,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int U = g.n_tiles * g.kb;
         int u0, u1;
         unit_range(U, G, cta, u0, u1);
-        // Pull this CTA's share of the next GEMM phase into L2 now (up to 512 KB), so HBM keeps
-        // streaming while this phase's barrier, operand build and epilogues run.
-        for (int q = p + 1; q < n_phases; ++q) {
+        // Pull this CTA's share of the GEMM phase `prefetch_ahead` phases later into L2 now (up
+        // to 512 KB), so HBM keeps streaming while barriers, operand builds and epilogues run.
+        // (With prefetch_ahead = k, the first k phases are requested here at the start.)
+        for (int q = p + 1, seen = 0; q < n_phases && a.prefetch_ahead > 0; ++q) {
           if (!is_gemm(phase_kind(a, q))) continue;
+          ++seen;
+          const bool first_phase = (p == 1);
+          if (seen < a.prefetch_ahead && !first_phase) continue;
           const GemmInfo gn = gemm_info(a, q);
           int v0, v1;
           unit_range(gn.n_tiles * gn.kb, G, cta, v0, v1);
           for (int v = v0; v < v1 && v < v0 + 32; ++v) prefetch_l2(gn.w + static_cast<size_t>(v) * kUnitBytes, kUnitBytes);
-          break;
+          if (seen >= a.prefetch_ahead) break;
         }
         for (int u = u0; u < u1; ++u, ++gu) {
           const int st = gu % kStages;

@@ -52,6 +52,8 @@ struct StreamArgs {
   float* attn_partials;
   int32_t* status;
   unsigned long long* trace;  // optional [grid][phases][8] globaltimer stamps
+  int prefetch_ahead;         // GEMM phases whose weights are pulled into L2 ahead of use
+  int ring_evict_first;       // L2 eviction hint for the ring's weight copies
 };
 
 size_t stream_packed_bytes(int N, int K);

@@ -131,6 +131,10 @@ class Engine:
             _ffi._lib.specb200_model_destroy(h)
 
     # ------------------------------------------------------------------ device-level call
+    def launches(self, b: int, t: int) -> int:
+        """Kernel launches of one forward call of B rows x T tokens."""
+        return 1 if lib().specb200_forward_uses_stream(self.handle, b, t) else 3 + 7 * self.n_layers
+
     def workspace_bytes(self, b: int, t: int, max_kv_len: int) -> int:
         return lib().specb200_forward_workspace_bytes(self.handle, b, t, max_kv_len)
 

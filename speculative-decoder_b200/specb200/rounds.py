@@ -126,6 +126,19 @@ class FusedRound:
         acc_ws = lib().specb200_accept_workspace_bytes(B, k)
         self.acc_ws = torch.zeros(acc_ws, dtype=torch.uint8, device=dev)
         self.graph: torch.cuda.CUDAGraph | None = None
+        # numpy views of the pinned inputs: the host fills them with plain array writes
+        self.np_active = self.active_h.numpy()
+        self.np_table = self.table_h.numpy()
+        self.np_u_acc = self.u_acc_h.numpy()
+        self.np_u_res = self.u_res_h.numpy()
+        if draft is not None:
+            self.np_d_ids0 = self.d_ids0_h.numpy()
+            self.np_d_past = self.d_past_h.numpy()
+            self.np_d_n = self.d_n_h.numpy()
+            self.np_d_table = self.d_table_h.numpy()
+            self.np_d_u = self.d_u_h.numpy()
+        self.np_out = self.out_h.numpy()
+        self.np_status = self.status_h.numpy()
 
     # ------------------------------------------------------------------ the round's launches
     def _launch(self) -> None:
@@ -181,12 +194,12 @@ class FusedRound:
             self.graph = g
         self.graph.replay()
         torch.cuda.current_stream(self.dev).synchronize()
-        for code in self.status_h.tolist():
-            if code:
-                self.status.zero_()
-                _ffi.check_status(torch.tensor([code]), "fused round")
+        if self.np_status.any():
+            code = int(self.np_status[self.np_status != 0][0])
+            self.status.zero_()
+            _ffi.check_status(torch.tensor([code]), "fused round")
         B, k = self.B, self.k
-        vals = self.out_h.tolist()
+        vals = self.np_out.tolist()
         return vals[0:B], vals[B:2 * B], [vals[2 * B + b * k: 2 * B + (b + 1) * k] for b in range(B)]
 
 
@@ -234,34 +247,30 @@ def generate_fused(target, cache, drafter, prompts, max_new_tokens, k, temperatu
 
     while active:
         n_act = len(active)
-        rnd.active_h.zero_()
-        for s in active:
-            rnd.active_h[s] = 1
+        rnd.np_active[:] = 0
+        rnd.np_active[active] = 1
         # uniforms in the reference's order: draft steps (ModelDraft.propose), then accept_reject
         if draft_eng is not None:
-            d_u = [torch.rand(n_act, generator=generator, dtype=torch.float32) for _ in range(k)]
-        u_acc = torch.rand(n_act, k, generator=generator, dtype=torch.float32)
-        u_res = torch.rand(n_act, generator=generator, dtype=torch.float32)
-        idx = torch.tensor(active)
-        rnd.u_acc_h[idx] = u_acc
-        rnd.u_res_h[idx] = u_res
+            d_u = [torch.rand(n_act, generator=generator, dtype=torch.float32).numpy() for _ in range(k)]
+        rnd.np_u_acc[active] = torch.rand(n_act, k, generator=generator, dtype=torch.float32).numpy()
+        rnd.np_u_res[active] = torch.rand(n_act, generator=generator, dtype=torch.float32).numpy()
         # draft cache: the lag tokens, then one per step, grown row by row as the reference does
         if draft_eng is not None:
             dc = drafter.cache
-            rnd.d_n_h.zero_()
+            rnd.np_d_n[:] = 0
             for j in range(k):
-                rnd.d_u_h[j][idx] = d_u[j]
+                rnd.np_d_u[j, active] = d_u[j]
                 grow = [len(contexts[s]) - dc.length(s) if j == 0 else 1 for s in active]
                 before = dc.reserve(active, grow)
-                for s, g, p in zip(active, grow, before):
-                    rnd.d_past_h[j, s] = p
-                    rnd.d_n_h[j, s] = g
-                    if j == 0:
+                rnd.np_d_past[j, active] = before
+                rnd.np_d_n[j, active] = grow
+                if j == 0:
+                    for s, p in zip(active, before):
                         pend = contexts[s][p:]
-                        rnd.d_ids0_h[s, : len(pend)] = torch.tensor(pend, dtype=torch.int32)
+                        rnd.np_d_ids0[s, : len(pend)] = pend
             for s in active:
                 blocks = dc.tables[s].blocks
-                rnd.d_table_h[s, : len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+                rnd.np_d_table[s, : len(blocks)] = blocks
         # target cache: k + 1 positions past len(context) - 1 (the verify forward's append)
         for s in active:
             if cache.length(s) != len(contexts[s]) - 1:
@@ -269,7 +278,7 @@ def generate_fused(target, cache, drafter, prompts, max_new_tokens, k, temperatu
         cache.reserve(active, [k + 1] * n_act)
         for s in active:
             blocks = cache.tables[s].blocks
-            rnd.table_h[s, : len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+            rnd.np_table[s, : len(blocks)] = blocks
 
         n_acc, nxt, drafts = rnd.run()
         stats.rounds += 1
