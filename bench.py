@@ -170,6 +170,47 @@ def trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
     return out
 
 
+def chain_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
+    """The layer-chain kernel's profiling record ([C][n_layers * 5][16] in the flat trace
+    buffer; slot meanings in chain.cu): per phase kind, the median over layers of the critical
+    path (previous phase's last end to this phase's last end), and medians over CTAs and layers
+    of each stamp's offset from the CTA's phase start (us) and of the cycle counters (k cycles)."""
+    flat = trace.flatten().double().cpu()
+    per = n_layers * 5 * 16
+    C = 0
+    while (C + 1) * per <= flat.numel() and bool((flat[C * per:(C + 1) * per] > 0).any()):
+        C += 1
+    if C == 0:
+        return {}
+    t = flat[: C * per].view(C, n_layers * 5, 16)
+    ts = t / 1e3
+    ends = ts[:, :, 3].amax(0)
+    t0 = ts[:, 0, 0].amin()
+    out = {"cluster": C, "total_us": round(float(ends[-1] - t0), 1)}
+    for j, name in enumerate(["qkv", "attn", "o", "gate_up", "down"]):
+        span = [float(ends[5 * l + j] - (ends[5 * l + j - 1] if 5 * l + j > 0 else t0)) for l in range(n_layers)]
+        ph = ts[:, [5 * l + j for l in range(n_layers)], :]
+        start = ph[..., 0]
+        d = {"critical_us": round(statistics.median(span), 2)}
+        for k, key in [(12, "h_ready"), (1, "operand"), (2, "segments"), (3, "end"), (4, "mma_x"), (5, "mma_last"),
+                       (6, "copy_last")]:
+            v = ph[..., k]
+            ok = v > 0
+            if bool(ok.any()):
+                d[key] = round(float((v - start)[ok].median()), 2)
+        for k, key in [(8, "kcyc_wait"), (9, "kcyc_fma"), (10, "kcyc_release"), (11, "kcyc_mma_wait")]:
+            v = ph[..., k]
+            if bool((v > 0).any()):
+                d[key] = round(float(v.median()), 2)
+        if j == 1:
+            cyc, dur = t[:, [5 * l + 1 for l in range(n_layers)], 14], (ph[..., 3] - ph[..., 0]) * 1e3
+            okc = (cyc > 0) & (dur > 0)
+            if bool(okc.any()):
+                d["sm_mhz"] = round(float((cyc[okc] / dur[okc]).median() * 1e3), 1)
+        out[name] = d
+    return out
+
+
 def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30, trace: bool = False) -> dict:
     """The (k+1)-token target forward of one round at B=1 with `context_len` cached tokens,
     captured in a CUDA graph and replayed; CUDA events on the replay stream."""
@@ -226,7 +267,7 @@ def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30
     return r
 
 
-def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30) -> dict:
+def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30, trace: bool = False) -> dict:
     """One single-token draft-model forward (135M architecture, B=1), CUDA graph, as in each
     of the k draft steps of a round."""
     from specb200.engine import engine_for
@@ -266,9 +307,20 @@ def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30) 
     en.synchronize()
     del past
     spec = dict(DRAFT, num_hidden_layers=draft.config.num_hidden_layers)
-    return {"us": st.elapsed_time(en) / reps * 1e3,
-            "bytes": weight_bytes(spec) + kv_bytes_per_token(spec) * context_len, "context": context_len,
-            "layers": spec["num_hidden_layers"]}
+    r = {"us": st.elapsed_time(en) / reps * 1e3,
+         "bytes": weight_bytes(spec) + kv_bytes_per_token(spec) * context_len, "context": context_len,
+         "layers": spec["num_hidden_layers"]}
+    if trace:
+        n_ph = 2 + 5 * spec["num_hidden_layers"]
+        tr = torch.zeros(torch.cuda.get_device_properties(device).multi_processor_count, n_ph, 8, dtype=torch.int64,
+                         device=device)
+        eng.forward_device(cache, ids, one, pastt, table, cap, True, logits, status, ws, trace=tr)
+        torch.cuda.synchronize()
+        if eng.schedule(1, 1) == "chain":
+            r["trace"] = chain_trace_summary(tr, spec["num_hidden_layers"])
+        else:
+            r["trace"] = trace_summary(tr, spec["num_hidden_layers"])
+    return r
 
 
 def time_accept(device, reps: int = 20) -> dict:
@@ -385,7 +437,7 @@ def main() -> None:
         else:
             spec = dict(DRAFT, num_hidden_layers=args.layers or DRAFT["num_hidden_layers"])
             r = time_draft_step(make_model(spec, 1, device), KVCache, device, PROMPT_LEN + NEW_TOKENS // 2,
-                                reps=max(1, args.steps))
+                                reps=max(1, args.steps), trace=args.trace)
         r["gbs"] = r["bytes"] / (r["us"] * 1e-6) / 1e9
         r["frac"] = r["gbs"] / pk["hbm_gbs"]
         print(json.dumps({"only": args.only, **r}))

@@ -213,8 +213,10 @@ size_t specb200_packed_tile_bytes(int N, int K);
 int specb200_pack_tiles(const void* w, int N, int K, void* out, void* stream);
 
 size_t specb200_forward_workspace_bytes(void* model, int B, int T, int max_kv_len);
-/* 1 if a call with B rows of T tokens runs the persistent layer-stream kernel (one launch),
- * 0 if it runs one kernel per layer op (3 + 7 n_layers launches). */
+/* Which schedule a call with B rows of T tokens runs: 2 = the layer stack on one thread-block
+ * cluster (small models, at most 8 token rows; 3 launches with the final norm and LM head),
+ * 1 = the persistent layer-stream kernel over all SMs (one launch), 0 = one kernel per layer
+ * op (3 + 7 n_layers launches). */
 int specb200_forward_uses_stream(void* model, int B, int T);
 int specb200_forward(void* model, const specb200_batch* batch, void* workspace, size_t workspace_bytes,
                      void* stream);

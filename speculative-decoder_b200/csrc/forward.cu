@@ -15,6 +15,7 @@
 #include "attn_core.cuh"
 #include "gemm.cuh"
 #include "kernels.cuh"
+#include "chain.cuh"
 #include "stream.cuh"
 
 namespace specb200 {
@@ -38,7 +39,17 @@ struct Model {
   CUtensorMap head;
   int qkv_n;
   bool stream_ok;  // packed weights present and shapes within the layer-stream kernel's limits
+  int chain_C = 0;  // cluster size of the layer-chain kernel, 0 = not used for this model
 };
+
+// Whether a call of this shape runs the cluster layer-chain kernel (small models, decode
+// shapes); fills its plan.
+bool use_chain(const Model& m, int B, int T, ChainPhase ph[4], int* splits, ChainLayout* L) {
+  const specb200_model_config& c = m.cfg;
+  if (m.chain_C <= 0) return false;
+  return chain_plan(c.n_layers, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim, c.intermediate, B, T, m.chain_C, ph,
+                    splits, L);
+}
 
 // Whether a call of this shape runs the persistent layer-stream kernel; fills its grid size
 // and the stream-K partial slots it needs.
@@ -66,8 +77,11 @@ size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 struct Carve {
   size_t gemm_counters, attn_counters, stream_ctl, hidden, xbuf, qbuf, attn, act, pos, slot, gemm_parts, attn_parts,
       stream_parts, total;
-  bool stream;
+  bool stream, chain;
   int grid, max_contrib;
+  ChainPhase cph[4];
+  int csplits;
+  ChainLayout cl;
   GemmShape g_qkv, g_o, g_gu, g_down, g_head;
   AttnPlan ap;
 };
@@ -85,7 +99,8 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   r.g_gu = plan_gemm(M, 2 * c.intermediate, c.hidden, tc);
   r.g_down = plan_gemm(M, c.hidden, c.intermediate, tc);
   r.g_head = plan_gemm(rows_out, c.vocab, c.hidden, tc);
-  r.stream = use_stream(m, B, T, &r.grid, &r.max_contrib);
+  r.chain = use_chain(m, B, T, r.cph, &r.csplits, &r.cl);
+  r.stream = !r.chain && use_stream(m, B, T, &r.grid, &r.max_contrib);
   r.ap = r.stream ? plan_attention_decode(B, c.n_kv_heads, max_kv_len, r.grid)
                   : plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len);
   // The two ticket-counter regions sit at fixed offsets so that they stay zero across calls
@@ -183,6 +198,10 @@ int run_stream(const Model& m, const specb200_batch& bt, char* ws, const Carve& 
   cudaMemsetAsync(ws + cv.stream_ctl, 0, 128, s);  // barrier arrivals/generation and the abort flag
   return launch_stream(a, map_attn, map_act, cv.grid, s);
 }
+
+template <typename T>
+int run_head(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv, cudaStream_t s,
+             const CUtensorMap* x_final);
 
 template <typename T>
 int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv, cudaStream_t s) {
@@ -294,15 +313,87 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     if ((rc = gemm(cv.g_gu, mp ? &mp->gu : nullptr, &x_hidden, L.w_gate_up, xbuf, eg))) return rc;
     if ((rc = gemm(cv.g_down, mp ? &mp->down : nullptr, &x_act, L.w_down, act, er))) return rc;
   }
-  if ((rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(m.w.final_norm), rows_out, c.hidden, c.rms_eps, xbuf,
-                              bt.last_only ? bt.n_new : nullptr, Tt, s, pdl)))
-    return rc;
+  return run_head<T>(m, bt, ws, cv, s, tc ? &x_final : nullptr);
+}
+
+// Final RMSNorm (of each sequence's last valid row when last_only) and the LM head GEMM into
+// fp32 logits, reading the residual stream from the workspace's hidden buffer.
+template <typename T>
+int run_head(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv, cudaStream_t s,
+             const CUtensorMap* x_final) {
+  const specb200_model_config& c = m.cfg;
+  const int rows_out = bt.last_only ? bt.B : bt.B * bt.T;
+  T* hidden = reinterpret_cast<T*>(ws + cv.hidden);
+  T* xbuf = reinterpret_cast<T*>(ws + cv.xbuf);
+  GemmScratch gscr{reinterpret_cast<int*>(ws + cv.gemm_counters), reinterpret_cast<float*>(ws + cv.gemm_parts)};
+  int rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(m.w.final_norm), rows_out, c.hidden, c.rms_eps, xbuf,
+                             bt.last_only ? bt.n_new : nullptr, bt.T, s, true);
+  if (rc) return rc;
   Epilogue eh = {};
   eh.op = EPI_STORE;
   eh.out_f32 = 1;
   eh.out = bt.logits;
   eh.ldo = c.vocab;
-  return gemm(cv.g_head, &m.head, &x_final, m.w.lm_head, xbuf, eh);
+  if (c.dtype == SPECB200_BF16) return launch_gemm_tc(cv.g_head, m.head, *x_final, eh, gscr, bt.status, s, true);
+  return launch_gemm_simt<T>(cv.g_head, static_cast<const T*>(m.w.lm_head), xbuf, eh, gscr, bt.status, s, true);
+}
+
+// Decode-shaped calls of small bf16 models: the layer stack on one thread-block cluster
+// (chain.cu), then the final norm and the LM head on the whole GPU.
+int run_chain(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv, cudaStream_t s) {
+  const specb200_model_config& c = m.cfg;
+  ChainArgs a = {};
+  a.n_layers = c.n_layers;
+  a.H = c.hidden;
+  a.Hq = c.n_heads;
+  a.Hkv = c.n_kv_heads;
+  a.D = c.head_dim;
+  a.I = c.intermediate;
+  a.eps = c.rms_eps;
+  a.attn_scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
+  a.max_positions = c.max_positions;
+  a.V = c.vocab;
+  a.embed = static_cast<const __nv_bfloat16*>(m.w.embed);
+  a.rope_cos = m.w.rope_cos;
+  a.rope_sin = m.w.rope_sin;
+  for (int l = 0; l < c.n_layers; ++l) {
+    const specb200_layer_weights& L = m.layers[l];
+    a.layers[l].attn_norm = static_cast<const __nv_bfloat16*>(L.attn_norm);
+    a.layers[l].mlp_norm = static_cast<const __nv_bfloat16*>(L.mlp_norm);
+    a.layers[l].qkv = static_cast<const uint8_t*>(L.p_qkv);
+    a.layers[l].o = static_cast<const uint8_t*>(L.p_o);
+    a.layers[l].gu = static_cast<const uint8_t*>(L.p_gate_up);
+    a.layers[l].down = static_cast<const uint8_t*>(L.p_down);
+  }
+  a.B = bt.B;
+  a.T = bt.T;
+  a.M = bt.B * bt.T;
+  a.ids = bt.input_ids;
+  a.n_new = bt.n_new;
+  a.past = bt.past_len;
+  a.table = bt.block_table;
+  a.table_stride = bt.table_stride;
+  a.bs = bt.block_size;
+  a.num_slots = bt.num_slots;
+  a.k_pool = static_cast<__nv_bfloat16*>(bt.k_pool);
+  a.v_pool = static_cast<__nv_bfloat16*>(bt.v_pool);
+  a.h = reinterpret_cast<__nv_bfloat16*>(ws + cv.hidden);
+  for (int i = 0; i < 4; ++i) a.ph[i] = cv.cph[i];
+  a.splits = cv.csplits;
+  a.C = m.chain_C;
+  a.L = cv.cl;
+  a.ring_evict_first = m.ring_evict_first;
+  // GEMM units on the tensor cores by default; SPECB200_CHAIN_FMA=1 runs calls of at most
+  // kChainFmaRows rows on the CUDA cores instead (measured 1.24 vs 1.20 ms per draft step).
+  a.fma = a.M <= kChainFmaRows && env_int("SPECB200_CHAIN_FMA", 0) == 1;
+  a.status = bt.status;
+  a.trace = reinterpret_cast<unsigned long long*>(bt.trace);
+  int rc = launch_chain(a, s);
+  if (rc) return rc;
+  const int rows_out = bt.last_only ? bt.B : bt.B * bt.T;
+  CUtensorMap x_final{};
+  if (!make_tmap_bf16_2d(&x_final, ws + cv.xbuf, c.hidden, rows_out, kTileK, cv.g_head.BN)) return SPECB200_ERR_ARG;
+  return run_head<__nv_bfloat16>(m, bt, ws, cv, s, &x_final);
 }
 
 }  // namespace
@@ -341,7 +432,7 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
   // 1.7B target: 2.30 vs 2.54 ms per verify).
   const size_t layer_bytes = 2ull * c.hidden *
                              (static_cast<size_t>(m->qkv_n) + static_cast<size_t>(c.n_heads) * c.head_dim + 3ull * c.intermediate);
-  if (layer_bytes < (32ull << 20)) m->stream_ok = false;
+  if (layer_bytes < (static_cast<size_t>(env_int("SPECB200_STREAM_MIN_LAYER_MB", 32)) << 20)) m->stream_ok = false;
   // SPECB200_NO_STREAM=1 keeps every call on the per-layer kernels (used to compare paths).
   const char* no_stream = std::getenv("SPECB200_NO_STREAM");
   if (no_stream && no_stream[0] == '1') m->stream_ok = false;
@@ -350,6 +441,17 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
   m->ring_evict_first = env_int("SPECB200_STREAM_EVICT_FIRST", 1);
   // Size the persistent grid now, outside any stream capture (it sets a function attribute).
   if (m->stream_ok && stream_grid_size() <= 0) m->stream_ok = false;
+  // The cluster layer-chain kernel: same packed weights, small models (hidden <= 1024) only.
+  // Opt-in (SPECB200_CHAIN=1): on the 135M draft it is not yet faster than the per-layer
+  // kernels (measured 1.20 vs 1.17-1.29 ms per decode step).
+  const bool chain_weights = c.dtype == SPECB200_BF16 && c.head_dim == 64 && c.hidden <= 1024 &&
+                             c.n_layers <= kStreamMaxLayers && env_int("SPECB200_CHAIN", 0) == 1;
+  bool packed = chain_weights;
+  for (int l = 0; l < c.n_layers && packed; ++l) {
+    const specb200_layer_weights& L = weights->layers[l];
+    packed = L.p_qkv && L.p_o && L.p_gate_up && L.p_down;
+  }
+  m->chain_C = packed ? chain_cluster_size() : 0;
   if (c.dtype == SPECB200_BF16) {
     const int qd = c.n_heads * c.head_dim;
     m->maps.resize(c.n_layers);
@@ -372,8 +474,13 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
 
 extern "C" int specb200_forward_uses_stream(void* model, int B, int T) {
   if (!model || B <= 0 || T <= 0) return 0;
+  const Model& m = *static_cast<Model*>(model);
+  ChainPhase ph[4];
+  int splits = 0;
+  ChainLayout L;
+  if (use_chain(m, B, T, ph, &splits, &L)) return 2;
   int grid = 0, mc = 0;
-  return use_stream(*static_cast<Model*>(model), B, T, &grid, &mc) ? 1 : 0;
+  return use_stream(m, B, T, &grid, &mc) ? 1 : 0;
 }
 
 extern "C" int specb200_model_destroy(void* handle) {
@@ -400,7 +507,8 @@ extern "C" int specb200_forward(void* model, const specb200_batch* batch, void* 
   if (workspace_bytes < cv.total) return specb200_set_error(SPECB200_ERR_WORKSPACE, "forward: workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (bt.status) cudaMemsetAsync(bt.status, 0, sizeof(int32_t), s);
-  int rc = cv.stream ? run_stream(m, bt, static_cast<char*>(workspace), cv, s)
+  int rc = cv.chain  ? run_chain(m, bt, static_cast<char*>(workspace), cv, s)
+           : cv.stream ? run_stream(m, bt, static_cast<char*>(workspace), cv, s)
            : m.cfg.dtype == SPECB200_BF16 ? run_forward<__nv_bfloat16>(m, bt, static_cast<char*>(workspace), cv, s)
                                           : run_forward<float>(m, bt, static_cast<char*>(workspace), cv, s);
   if (rc != SPECB200_OK) {

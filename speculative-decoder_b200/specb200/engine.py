@@ -133,7 +133,12 @@ class Engine:
     # ------------------------------------------------------------------ device-level call
     def launches(self, b: int, t: int) -> int:
         """Kernel launches of one forward call of B rows x T tokens."""
-        return 1 if lib().specb200_forward_uses_stream(self.handle, b, t) else 3 + 7 * self.n_layers
+        return {2: 3, 1: 1}.get(lib().specb200_forward_uses_stream(self.handle, b, t), 3 + 7 * self.n_layers)
+
+    def schedule(self, b: int, t: int) -> str:
+        """The schedule a forward call of B rows x T tokens runs: "chain" (one thread-block
+        cluster), "stream" (persistent kernel over all SMs) or "layers" (a kernel per op)."""
+        return {2: "chain", 1: "stream"}.get(lib().specb200_forward_uses_stream(self.handle, b, t), "layers")
 
     def workspace_bytes(self, b: int, t: int, max_kv_len: int) -> int:
         return lib().specb200_forward_workspace_bytes(self.handle, b, t, max_kv_len)

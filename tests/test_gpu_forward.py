@@ -265,3 +265,76 @@ def test_stream_kernel_matches_per_layer_kernels(monkeypatch):
         top2 = a.topk(2, dim=-1).values
         agree = a.argmax(-1) == b.argmax(-1)
         assert bool((agree | ((top2[..., 0] - top2[..., 1]) < 1e-2 * scale)).all())
+
+
+def _decode_steps(eng, model, prompt_len: int, seqs: int = 1):
+    """Prefill `seqs` sequences of different lengths, then a 5-token verify-shaped step, a
+    1-token draft-shaped step and a ragged 2-row step (4 tokens, 3 valid in row 1); returns the
+    logits of the three decode-shaped steps and the final KV pools."""
+    from cache.kv import KVCache
+
+    cache = KVCache.for_model(model.config, num_blocks=96, block_size=16, dtype=torch.bfloat16, device=DEV)
+    outs = []
+    for s in range(2):
+        cache.add(s)
+        n = prompt_len - 37 * s
+        p = torch.randint(0, model.config.vocab_size, (1, n), generator=torch.Generator().manual_seed(40 + s))
+        eng.forward(cache, [s], p, [n], last_only=True)
+    outs.append(eng.forward(cache, [0], torch.tensor([[5, 6, 7, 8, 9]]), [5]))
+    outs.append(eng.forward(cache, [0], torch.tensor([[11]]), [1], last_only=True))
+    outs.append(eng.forward(cache, [0, 1], torch.tensor([[12, 13, 14, 15], [16, 17, 18, 0]]), [4, 3]))
+    return [x.float().cpu() for x in outs], cache
+
+
+@pytest.mark.parametrize("fma", ["0", "1"])
+def test_chain_kernel_matches_per_layer_kernels(monkeypatch, fma):
+    """The cluster layer-chain kernel (small models, at most 8 token rows) against the
+    per-layer kernels on the 135M draft architecture (2 layers): verify-, draft- and ragged
+    2-row shapes. Both sum the split-K partials in different orders, so logits agree to bf16
+    noise (1e-2 of the logit scale, argmax equal except at near ties) and the KV entries the
+    calls wrote agree to one bf16 ulp of their scale. Both GEMM back ends are covered: tcgen05
+    MMAs and (for calls of at most two rows) CUDA-core FMAs."""
+    from specb200.engine import Engine
+
+    model = _bf16_model(576, 2, 9, 3, 1536, 49152, seed=5, theta=100000.0).to(DEV)
+    per_layer = Engine(model)
+    monkeypatch.setenv("SPECB200_CHAIN", "1")
+    monkeypatch.setenv("SPECB200_CHAIN_FMA", fma)
+    chain = Engine(model)
+    assert per_layer.schedule(1, 5) == "layers"
+    assert chain.schedule(1, 5) == "chain" and chain.schedule(1, 1) == "chain" and chain.schedule(2, 4) == "chain"
+    (la, ca), (lb, cb) = _decode_steps(per_layer, model, 300), _decode_steps(chain, model, 300)
+    for a, b in zip(la, lb):
+        scale = a.abs().max().item()
+        assert (a - b).abs().max().item() <= 1e-2 * scale, ((a - b).abs().max().item(), scale)
+        top2 = a.topk(2, dim=-1).values
+        agree = a.argmax(-1) == b.argmax(-1)
+        assert bool((agree | ((top2[..., 0] - top2[..., 1]) < 1e-2 * scale)).all())
+    for pa, pb in ((ca.k, cb.k), (ca.v, cb.v)):
+        d = (pa.float() - pb.float()).abs().max().item()
+        assert d <= 2 ** -7 * pa.float().abs().max().item(), d
+
+
+def test_chain_kernel_matches_oracle(monkeypatch):
+    """The cluster layer-chain kernel against the bf16 oracle after a prefill: 5-token and
+    1-token steps of the 135M draft architecture (2 layers), logits within rtol 2e-2."""
+    from lm.forward import forward
+    from specb200.engine import engine_for
+
+    monkeypatch.setenv("SPECB200_CHAIN", "1")
+    model = _bf16_model(576, 2, 9, 3, 1536, 49152, seed=12, theta=100000.0)
+    w = ofw.weights_from_model(model)
+    prec = ofw.Precision("bf16")
+    model = model.to(DEV)
+    assert engine_for(model).schedule(1, 5) == "chain"
+    cache = new_cache(model, block_size=16)
+    ocache = ofw.Cache(w, 4096, 16, prec)
+    cache.add(0)
+    ocache.add(0)
+    prompt = torch.randint(0, 49152, (1, 70), generator=torch.Generator().manual_seed(7)).numpy()
+    for ids_np, n_new in [(prompt, [70]), (np.array([[1, 2, 3, 4, 5]]), [5]), (np.array([[6]]), [1])]:
+        got = forward(model, cache, [0], torch.from_numpy(ids_np), n_new).float().cpu().numpy()
+        want = ofw.forward(w, ocache, [0], ids_np, n_new, prec)
+        g, o = got[0, : n_new[0]], want[0, : n_new[0]]
+        scale = np.abs(o).max()
+        assert np.abs(g - o).max() <= 2e-2 * scale + 1e-3, (np.abs(g - o).max(), scale)
