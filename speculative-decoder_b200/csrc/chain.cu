@@ -215,6 +215,19 @@ __device__ bool cwait(const ChainArgs& a, const Ctx& c, uint64_t* bar, uint32_t 
   }
 }
 
+// lwait / cwait for a warp that issues with elect.sync: lane 0 waits, every lane gets the result.
+__device__ bool lwait(const ChainArgs& a, const Ctx& c, uint64_t* bar, uint32_t parity);
+__device__ bool lwait_warp(const ChainArgs& a, const Ctx& c, uint64_t* bar, uint32_t parity) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = lwait(a, c, bar, parity) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+__device__ bool cwait_warp(const ChainArgs& a, const Ctx& c, uint64_t* bar, uint32_t parity) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = cwait(a, c, bar, parity) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 // Bounded wait (acquire, CTA scope) for barriers completed by this CTA's own async units
 // (bulk copies, tcgen05.commit) or threads.
 __device__ bool lwait(const ChainArgs& a, const Ctx& c, uint64_t* bar, uint32_t parity) {
@@ -932,7 +945,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
           const Part pt = part_of(a, c, kind);
           const int u0 = pt.lo[rank], u1 = pt.lo[rank + 1];
           const bool norm_x = (kind == CK_QKV || kind == CK_GU);
-          ok = norm_x ? lwait(a, c, c.x_full, (xn_n++) & 1) : cwait(a, c, c.xp_full, (xp_n++) & 1);
+          ok = norm_x ? lwait_warp(a, c, c.x_full, (xn_n++) & 1) : cwait_warp(a, c, c.xp_full, (xp_n++) & 1);
           if (!ok) break;
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
           tc_fence_after();
@@ -948,7 +961,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
               run_first = static_cast<int>(g % S);
               run_n = run_left = min(min(kRun, u1 - u), S - run_first);
               const unsigned long long w0 = a.trace ? now_ns() : 0;
-              ok = lwait(a, c, &c.full[run_first], (g / S) & 1);
+              ok = lwait_warp(a, c, &c.full[run_first], (g / S) & 1);
               if (a.trace) waited += now_ns() - w0;
               if (!ok) break;
               tc_fence_after();
@@ -958,7 +971,7 @@ __global__ void __launch_bounds__(kThreads, 1) chain_kernel(const __grid_constan
             if (first) {
               buf = segs & 1;
               if (segs >= 2) {
-                ok = lwait(a, c, &c.acc_empty[buf], ((segs >> 1) - 1) & 1);
+                ok = lwait_warp(a, c, &c.acc_empty[buf], ((segs >> 1) - 1) & 1);
                 if (!ok) break;
               }
               tc_fence_after();

@@ -125,6 +125,14 @@ SPECB200_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int32_t* 
   }
 }
 
+// Warp-uniform bounded wait for a warp that issues tcgen05 work with elect.sync: lane 0 waits
+// (acquire) and the outcome is broadcast, so every lane takes the same branch afterwards.
+SPECB200_DEVINL bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int32_t* status, volatile int* abort) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait_bounded(bar, parity, status, abort) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 // ---------------------------------------------------------------- TMA (no multicast anywhere)
 SPECB200_DEVINL void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

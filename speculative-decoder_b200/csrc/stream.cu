@@ -441,50 +441,63 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
   } else if (warp == 5) {
-    // ------------------------------------------------------------ MMA issue
-    if (lane == 0) {
+    // ------------------------------------------------------------ MMA issue: the whole warp
+    // runs the loop and one elected lane issues (a lone issuing lane with the other lanes
+    // waiting diverged costs about a third more per instruction)
+    {
       const uint32_t idesc = umma_idesc_bf16(128, kStreamBN);
       uint32_t gu = 0, xc = 0, segs = 0;
-      for (int p = 0; p < n_phases && !*abort_s; ++p) {
+      bool ok = true;
+      for (int p = 0; p < n_phases && ok; ++p) {
+        ok = __shfl_sync(0xffffffffu, *abort_s ? 0 : 1, 0) != 0;
+        if (!ok) break;
         if (!is_gemm(phase_kind(a, p))) continue;
         const GemmInfo g = gemm_info(a, p);
         const int U = g.n_tiles * g.kb;
         int u0, u1;
         unit_range(U, G, cta, u0, u1);
         if (u0 == u1) continue;
-        if (!mbar_wait_bounded(x_full, xc & 1, a.status, abort_s)) break;
+        if (!mbar_wait_warp(x_full, xc & 1, a.status, abort_s)) {
+          ok = false;
+          break;
+        }
         ++xc;
         tc_fence_after();
-        stamp(a, n_phases, p, 4);
+        if (lane == 0) stamp(a, n_phases, p, 4);
         bool first = true;
         uint32_t buf = 0;
         for (int u = u0; u < u1; ++u, ++gu) {
           if (first) {
             buf = segs & 1;
-            if (segs >= 2 && !mbar_wait_bounded(&acc_empty[buf], ((segs >> 1) - 1) & 1, a.status, abort_s)) break;
+            if (segs >= 2 && !mbar_wait_warp(&acc_empty[buf], ((segs >> 1) - 1) & 1, a.status, abort_s)) {
+              ok = false;
+              break;
+            }
             tc_fence_after();
           }
           const int st = gu % kStages;
-          if (!mbar_wait_bounded(&full[st], (gu / kStages) & 1, a.status, abort_s)) break;
+          if (!mbar_wait_warp(&full[st], (gu / kStages) & 1, a.status, abort_s)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
-          const uint32_t wa = smem_u32(ring + st * kUnitBytes);
           const int xslot = g.per_unit ? (u - u0) : (u % g.kb);
-          const uint32_t xa = smem_u32(xreg + xslot * kXBlockBytes);
+          const uint64_t da = umma_desc_sw128(smem_u32(ring + st * kUnitBytes));
+          const uint64_t dx = umma_desc_sw128(smem_u32(xreg + xslot * kXBlockBytes));
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem_base + buf * kStreamBN, umma_desc_sw128(wa + kk * 32), umma_desc_sw128(xa + kk * 32), idesc,
-                      (first && kk == 0) ? 0u : 1u);
-          umma_commit(&empty[st]);
+            umma_bf16_elect(tmem_base + buf * kStreamBN, da + kk * 2, dx + kk * 2, idesc, (first && kk == 0) ? 0u : 1u);
+          umma_commit_elect(&empty[st]);
           const bool seg_end = (u + 1 == u1) || ((u + 1) % g.kb == 0);
           if (seg_end) {
-            umma_commit(&acc_full[buf]);
+            umma_commit_elect(&acc_full[buf]);
             ++segs;
             first = true;
           } else {
             first = false;
           }
         }
-        stamp(a, n_phases, p, 5);
+        if (lane == 0) stamp(a, n_phases, p, 5);
       }
     }
     __syncwarp();
