@@ -452,9 +452,14 @@ def main() -> None:
     from spec.draft import ModelDraft
     from spec.loop import generate
 
+    from specb200.shard import gather_results, shard_range
+
     target = make_model(TARGET, 0, device)
     draft = make_model(DRAFT, 1, device)
-    prompts = prompts_for(rank, 1)
+    # one request per GPU: the box's requests are sharded as contiguous ranges, one per rank
+    all_prompts = [prompts_for(r, 1)[0] for r in range(world)]
+    lo, hi = shard_range(len(all_prompts), rank, world)
+    prompts = all_prompts[lo:hi]
     blocks = (PROMPT_LEN + NEW_TOKENS + 2 * K + 8) // BLOCK + 2
 
     def step():
@@ -492,10 +497,9 @@ def main() -> None:
         sm = t.clone()
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         dev_s, wall, tokens_all = mx[0].item(), mx[1].item(), sm[2].item()
-        # collect outputs (kilobytes) over NCCL after the timed region
-        mine = torch.tensor(out[0] + [0] * (NEW_TOKENS - len(out[0])), dtype=torch.int32, device=device)
-        gathered = [torch.empty_like(mine) for _ in range(world)]
-        dist.all_gather(gathered, mine)
+        # the last step's outputs and statistics of every request (kilobytes), over NCCL
+        # after the timed region
+        out, stats = gather_results(out, stats, device=device)
     else:
         tokens_all = float(tokens)
     if rank != 0:
