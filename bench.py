@@ -542,7 +542,8 @@ def main() -> None:
         "roofline": {"bound": "hbm", "kernel": "verify step (one (k+1)-token target forward, CUDA graph)",
                      "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
                      "traffic": vstep["bytes"] * VERIFY_TRAFFIC_RATIO if te.launches(1, K + 1) == 1 else None,
-                     "traffic_source": "ncu capture of the 6-layer stream kernel, scaled by algorithmic bytes",
+                     "traffic_source": ("ncu capture of the 6-layer stream kernel, scaled by algorithmic bytes"
+                                        if te.launches(1, K + 1) == 1 else "per-layer kernels: see verify_launches"),
                      "peak_source": pk["source"], "verify_step_us": vstep["us"],
                      "algorithmic_bytes": vstep["bytes"], "context_tokens": vstep["context"]},
         "accept": {"us": acc["us"], "achieved": acc_gbs, "frac": acc_gbs / pk["hbm_gbs"], "unit": "GB/s",

@@ -15,8 +15,10 @@
 // merges the partial results in split order, which keeps the output independent of CTA
 // scheduling; there is no spin-wait.
 #include <algorithm>
+#include <type_traits>
 
 #include "attn_core.cuh"
+#include "attn_item_mma.cuh"
 
 namespace specb200 {
 namespace {
@@ -27,6 +29,15 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnKernelArgs 
   pdl_launch_dependents();
   pdl_wait();
   attention_item<T, D>(ka, blockIdx.z, blockIdx.y / ka.p.qtiles, blockIdx.y % ka.p.qtiles, blockIdx.x, smem);
+}
+
+// Decode / verify shapes (bf16, d = 64, T x G <= 16): one tensor-core item per (split, kv
+// head, sequence).
+__global__ void __launch_bounds__(kAttnThreads) attention_mma_kernel(AttnKernelArgs ka) {
+  __shared__ __align__(128) uint8_t smem[kAmItemSmem];
+  pdl_launch_dependents();
+  pdl_wait();
+  attention_item_mma(ka, blockIdx.z, blockIdx.y, blockIdx.x, smem);
 }
 
 template <typename T, int D>
@@ -42,7 +53,12 @@ cudaError_t launch_d(const AttnArgs& a, const AttnPlan& p, int* counters, float*
 
 }  // namespace
 
-AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len) {
+AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len, bool tensor_items) {
+  if (tensor_items && T * (Hq / Hkv) <= kAmRows) {
+    AttnPlan p = plan_attention_mma(B, Hkv, max_kv_len);
+    p.mma = 1;
+    return p;
+  }
   AttnPlan p;
   const int G = Hq / Hkv;
   p.qtiles = (T * G + kRows - 1) / kRows;
@@ -68,6 +84,17 @@ size_t attention_workspace_bytes(const AttnPlan& p, int B, int Hkv, int D) {
 template <typename T>
 int launch_attention(const AttnArgs& a, const AttnPlan& p, int* counters, float* partials, cudaStream_t s, bool pdl) {
   cudaError_t e;
+  if (p.mma) {
+    if (!std::is_same<T, __nv_bfloat16>::value || a.D != 64 || a.T * (a.Hq / a.Hkv) > kAmRows)
+      return SPECB200_ERR_UNSUPPORTED;
+    AttnKernelArgs ka;
+    ka.a = a;
+    ka.p = p;
+    ka.counters = counters;
+    ka.part = partials;
+    e = launch_kernel(attention_mma_kernel, dim3(p.splits_max, a.Hkv, a.B), dim3(kAttnThreads), 0, s, pdl, ka);
+    return e == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
+  }
   switch (a.D) {
     case 16: e = launch_d<T, 16>(a, p, counters, partials, s, pdl); break;
     case 32: e = launch_d<T, 32>(a, p, counters, partials, s, pdl); break;
@@ -87,7 +114,10 @@ extern "C" int specb200_set_error(int code, const char* msg);
 extern "C" size_t specb200_attention_workspace_bytes(int B, int T, int n_heads, int n_kv_heads, int head_dim,
                                                      int max_kv_len) {
   if (B <= 0 || T <= 0 || n_kv_heads <= 0 || n_heads % n_kv_heads) return 0;
-  return attention_workspace_bytes(plan_attention(B, T, n_heads, n_kv_heads, max_kv_len), B, n_kv_heads, head_dim);
+  // the tensor-core items apply to bf16 with d = 64; the workspace covers either plan
+  const AttnPlan a = plan_attention(B, T, n_heads, n_kv_heads, max_kv_len, false);
+  const AttnPlan b = plan_attention(B, T, n_heads, n_kv_heads, max_kv_len, head_dim == 64);
+  return std::max(attention_workspace_bytes(a, B, n_kv_heads, head_dim), attention_workspace_bytes(b, B, n_kv_heads, head_dim));
 }
 
 extern "C" int specb200_attention(int dtype, const void* q, const void* k_pool, const void* v_pool,
@@ -101,7 +131,7 @@ extern "C" int specb200_attention(int dtype, const void* q, const void* k_pool, 
     return specb200_set_error(SPECB200_ERR_UNSUPPORTED, "attention: head_dim must be 16, 32 or 64");
   if (!q || !k_pool || !v_pool || !block_table || !past_len || !n_new || !out || !workspace)
     return specb200_set_error(SPECB200_ERR_ARG, "attention: null pointer");
-  AttnPlan p = plan_attention(B, T, n_heads, n_kv_heads, max_kv_len);
+  AttnPlan p = plan_attention(B, T, n_heads, n_kv_heads, max_kv_len, dtype == SPECB200_BF16 && head_dim == 64);
   if (workspace_bytes < attention_workspace_bytes(p, B, n_kv_heads, head_dim))
     return specb200_set_error(SPECB200_ERR_WORKSPACE, "attention: workspace too small");
   AttnArgs a;

@@ -52,6 +52,13 @@ SPECB200_DEVINL void cp_async_16(void* dst, const void* src) {
 SPECB200_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
 SPECB200_DEVINL void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+// Wait until at most n (0..3) of this thread's most recent cp.async groups are pending.
+SPECB200_DEVINL void cp_async_wait_upto(int n) {
+  if (n <= 0) cp_async_wait<0>();
+  else if (n == 1) cp_async_wait<1>();
+  else if (n == 2) cp_async_wait<2>();
+  else cp_async_wait<3>();
+}
 
 // Per-warp online-softmax state for rows g = lane / 4 and g + 8 (replicated over the 4 lanes of
 // the row group; l is this lane's partial sum, reduced at the end).

@@ -724,12 +724,6 @@ __device__ void attn_prefetch(const ChainArgs& a, const Ctx& c, int l) {
   for (int j = 0; j < min(kKvBlocks, it.nblk); ++j) kv_load_block(a, c, it, l, j);
 }
 
-SPECB200_DEVINL void cp_async_wait_upto(int n) {
-  if (n <= 0) cp_async_wait<0>();
-  else if (n == 1) cp_async_wait<1>();
-  else if (n == 2) cp_async_wait<2>();
-  else cp_async_wait<3>();
-}
 static_assert(kKvBlocks <= 4, "cp_async_wait_upto covers up to 3 pending groups");
 
 __device__ bool attention_phase(const ChainArgs& a, const Ctx& c, int l, Counters& k) {

@@ -102,7 +102,7 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   r.chain = use_chain(m, B, T, r.cph, &r.csplits, &r.cl);
   r.stream = !r.chain && use_stream(m, B, T, &r.grid, &r.max_contrib);
   r.ap = r.stream ? plan_attention_decode(B, c.n_kv_heads, max_kv_len, r.grid)
-                  : plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len);
+                  : plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len, tc && c.head_dim == 64);
   // The two ticket-counter regions sit at fixed offsets so that they stay zero across calls
   // of every shape; everything after them is rewritten before it is read.
   size_t off = 0;
@@ -426,16 +426,15 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
     const specb200_layer_weights& L = weights->layers[l];
     m->stream_ok = L.p_qkv && L.p_o && L.p_gate_up && L.p_down;
   }
-  // Small models stay on the per-layer kernels: with a few MB of weights per layer the
-  // persistent kernel's per-phase latency (grid barrier, operand build, reductions) costs more
-  // than the launches it saves (measured on the 135M draft: 1.62 vs 1.17 ms per step; on the
-  // 1.7B target: 2.30 vs 2.54 ms per verify).
+  // The layer-stream schedule is opt-in (SPECB200_STREAM=1): its per-phase latency chain (grid
+  // barrier, operand build, split-K reduction, attention items) now costs more than the launch
+  // gaps it removes (1.7B verify at 644 cached tokens: 2.16 ms vs 1.90 ms per step on the
+  // per-layer kernels; 135M draft step: 1.62 vs 1.17 ms). Even when enabled, small models stay
+  // on the per-layer kernels (layers under SPECB200_STREAM_MIN_LAYER_MB, default 32 MB).
   const size_t layer_bytes = 2ull * c.hidden *
                              (static_cast<size_t>(m->qkv_n) + static_cast<size_t>(c.n_heads) * c.head_dim + 3ull * c.intermediate);
   if (layer_bytes < (static_cast<size_t>(env_int("SPECB200_STREAM_MIN_LAYER_MB", 32)) << 20)) m->stream_ok = false;
-  // SPECB200_NO_STREAM=1 keeps every call on the per-layer kernels (used to compare paths).
-  const char* no_stream = std::getenv("SPECB200_NO_STREAM");
-  if (no_stream && no_stream[0] == '1') m->stream_ok = false;
+  if (env_int("SPECB200_STREAM", 0) != 1) m->stream_ok = false;
   // Layer-stream schedule knobs (L2 prefetch distance in GEMM phases; ring eviction hint).
   m->prefetch_ahead = env_int("SPECB200_STREAM_PREFETCH", 0);  // measured: prefetching slows it
   m->ring_evict_first = env_int("SPECB200_STREAM_EVICT_FIRST", 1);

@@ -61,8 +61,11 @@ constexpr size_t kAttnCounterBytes = kAttnMaxCounters * sizeof(int);
 
 struct AttnPlan {
   int chunk, splits_max, qtiles;
+  int mma = 0;  // 1: tensor-core decode items (bf16, d = 64, at most 16 query rows per KV head)
 };
-AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len);
+// tensor_items: the call is bf16 with d = 64, so decode / verify shapes (T x G <= 16) may use
+// the tensor-core items (attn_item_mma.cuh).
+AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len, bool tensor_items);
 size_t attention_partials_bytes(const AttnPlan& p, int B, int Hkv, int D);
 size_t attention_workspace_bytes(const AttnPlan& p, int B, int Hkv, int D);  // counters + partials
 // counters: kAttnMaxCounters ints that start zero (left zero); partials: attention_partials_bytes.

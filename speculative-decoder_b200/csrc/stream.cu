@@ -26,6 +26,7 @@
 #include <mutex>
 
 #include "attn_core.cuh"
+#include "attn_item_mma.cuh"
 #include "epilogue.cuh"
 #include "stream.cuh"
 
@@ -539,9 +540,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         ka.part = a.attn_partials;
         const int per_b = a.Hkv * a.ap.splits_max;
         const int items = a.B * per_b;
+        const bool tensor_items = a.T * (a.Hq / a.Hkv) <= kAmRows;
         for (int it = cta; it < items; it += G) {
           const int b = it / per_b, r = it % per_b;
-          attention_item_decode(ka, b, r / a.ap.splits_max, r % a.ap.splits_max, xreg);
+          if (tensor_items) attention_item_mma(ka, b, r / a.ap.splits_max, r % a.ap.splits_max, xreg);
+          else attention_item_decode(ka, b, r / a.ap.splits_max, r % a.ap.splits_max, xreg);
           epi_bar_sync();
         }
         if (threadIdx.x == 0) stamp(a, n_phases, p, 3);

@@ -246,10 +246,10 @@ def test_stream_kernel_matches_per_layer_kernels(monkeypatch):
     from specb200.engine import Engine
 
     model = _bf16_model(2048, 2, 32, 32, 8192, 49152, seed=3, theta=130000.0).to(DEV)
-    monkeypatch.setenv("SPECB200_NO_STREAM", "1")
     per_layer = Engine(model)
-    monkeypatch.delenv("SPECB200_NO_STREAM")
+    monkeypatch.setenv("SPECB200_STREAM", "1")
     stream = Engine(model)
+    assert per_layer.schedule(1, 5) == "layers" and stream.schedule(1, 5) == "stream"
     prompt = torch.randint(0, 49152, (1, 300), generator=torch.Generator().manual_seed(4))
     outs = []
     for eng in (per_layer, stream):

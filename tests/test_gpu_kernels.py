@@ -269,10 +269,14 @@ def test_linear_fp32_matches_torch(m, n, k):
 
 # ---------------------------------------------------------------- paged attention (K4)
 @pytest.mark.parametrize("dtype,hq,hkv,d,T,bs", [(torch.float32, 4, 2, 16, 5, 4), (torch.bfloat16, 32, 32, 64, 5, 16),
-                                                 (torch.bfloat16, 9, 3, 64, 2, 16), (torch.float32, 4, 4, 32, 40, 3)])
+                                                 (torch.bfloat16, 9, 3, 64, 2, 16), (torch.float32, 4, 4, 32, 40, 3),
+                                                 (torch.bfloat16, 9, 3, 64, 1, 16), (torch.bfloat16, 9, 3, 64, 5, 16),
+                                                 (torch.bfloat16, 12, 3, 64, 4, 32), (torch.bfloat16, 32, 4, 64, 3, 16)])
 def test_attention_matches_dense_reference(dtype, hq, hkv, d, T, bs):
     """Paged attention over shuffled blocks vs the reference's mask (lm/forward.py:44-49) on
-    a dense fp32 copy: rows of lengths 1..700 incl. a padded row."""
+    a dense fp32 copy: rows of lengths 1..700 incl. a padded row. bf16 shapes with at most 16
+    query rows per KV head (T x G) run the tensor-core items (1, 6, 15 and 16 rows here); 24
+    rows (32 / 4 heads, T = 3) and the fp32 cases run the fp32 items."""
     g = torch.Generator().manual_seed(hq + T)
     lens_past = [0, 37, 700]
     n_new = [T, max(1, T - 2), T]
