@@ -218,6 +218,9 @@ size_t specb200_forward_workspace_bytes(void* model, int B, int T, int max_kv_le
  * 1 = the persistent layer-stream kernel over all SMs (one launch), 0 = one kernel per layer
  * op (3 + 7 n_layers launches). */
 int specb200_forward_uses_stream(void* model, int B, int T);
+/* Kernel launches one forward call with B rows of T tokens makes (no reference counterpart;
+ * used to count launches). */
+int specb200_forward_launches(void* model, int B, int T);
 int specb200_forward(void* model, const specb200_batch* batch, void* workspace, size_t workspace_bytes,
                      void* stream);
 

@@ -10,18 +10,25 @@
 //   spec/accept.py:29-35        sample_inverse_cdf(): first index whose cdf exceeds u * total,
 //                               clamped to V - 1
 //
-// Grid (R, B): one CTA per input row (R = k+1 target rows, plus k draft rows when q is a
-// real tensor). Each CTA streams its row once from HBM (128-bit loads) and leaves per-row
-// statistics (max and sum of exp for the softmax, the value at the drafted token, the
-// argmax) in the workspace. The last CTA of batch row b, found with an atomic ticket (no
-// spin-wait), makes the accept decisions and draws the residual sample from row n, which
-// it re-reads from L2. Decisions therefore cost one HBM pass over p and q.
+// Two launches, chained with programmatic dependent launch:
+//   accept_kernel, grid R x B of 256 threads (one wave of 4 CTAs per SM at config 3): one CTA
+//     per input row (R = k+1 target rows, plus k draft rows when q is a real tensor) streams
+//     its row once from HBM (128-bit loads) and leaves per-row statistics (max and sum of exp
+//     for the softmax, the value at the drafted token, the argmax) in the workspace. The last
+//     CTA of batch row b (atomic ticket, no spin-wait) makes the accept decisions: n, and for
+//     greedy rows the next token.
+//   residual_kernel (sampling only), grid C x B: chunk c of the residual row max(0, p_n - q_n)
+//     of sequence b, re-read from L2, summed in double; the last chunk CTA of b scans the chunk
+//     sums in order and then the elements of the chunk holding the crossing. Splitting the
+//     residual pass over C CTAs per sequence keeps its exp/sum work off one SM.
+// Decisions therefore cost one HBM pass over p and q.
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace specb200 {
 namespace {
 
-constexpr int kAcceptThreads = 512;
+constexpr int kAcceptThreads = 256;
 constexpr int kAcceptWarps = kAcceptThreads / 32;
 
 struct RowStat {
@@ -43,9 +50,33 @@ struct AcceptArgs {
   int64_t* n_accepted;
   int64_t* next_token;
   int32_t* status;
-  int* counters;   // [B]
+  int* counters;   // [2B]: statistics tickets, then residual tickets
   RowStat* stats;  // [B, R]
+  int* nsel;       // [B] accepted length n (the residual row)
+  double* chunk_sums;  // [B, C]
+  int C, chunk;        // residual chunks per sequence and their length (a multiple of 4 * kAcceptThreads)
 };
+
+// Workspace carve, shared by the caller-workspace and the allocation-free entry points.
+struct AcceptLayout {
+  size_t counters, stats, nsel, sums, total;
+};
+inline int residual_chunks(int V) {
+  const int per = 4 * kAcceptThreads;
+  const int blocks = (V + per - 1) / per;
+  return blocks < 16 ? blocks : 16;
+}
+inline AcceptLayout accept_layout(int B, int k, int V) {
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  const size_t R = 2 * static_cast<size_t>(k) + 1;
+  AcceptLayout l;
+  l.counters = 256;
+  l.stats = l.counters + al(2 * static_cast<size_t>(B) * sizeof(int));
+  l.nsel = l.stats + al(static_cast<size_t>(B) * R * sizeof(RowStat));
+  l.sums = l.nsel + al(static_cast<size_t>(B) * sizeof(int));
+  l.total = l.sums + al(static_cast<size_t>(B) * residual_chunks(V) * sizeof(double));
+  return l;
+}
 
 SPECB200_DEVINL const float* row_ptr(const AcceptArgs& a, int b, int r) {
   // rows 0..k: target positions; rows k+1..2k: draft positions 0..k-1
@@ -81,6 +112,8 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, RowStat* out) 
     return;
   }
   if (a.greedy) {
+    // First maximum (torch.argmax): per group of 4 values take the group's max; only a group
+    // that can win (or holds a NaN) goes through the exact tie / NaN merge.
     float best = -INFINITY;
     int bi = 0x7fffffff;
     if (vec) {
@@ -88,11 +121,15 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, RowStat* out) 
       const int n4 = a.V / 4;
 #pragma unroll 8
       for (int j = tid; j < n4; j += kAcceptThreads) {
-        float4 v = __ldg(r4 + j);
-        argmax_merge(best, bi, v.x, 4 * j);
-        argmax_merge(best, bi, v.y, 4 * j + 1);
-        argmax_merge(best, bi, v.z, 4 * j + 2);
-        argmax_merge(best, bi, v.w, 4 * j + 3);
+        const float4 v = __ldg(r4 + j);
+        const float gm = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
+        const bool nan = (v.x != v.x) || (v.y != v.y) || (v.z != v.z) || (v.w != v.w);
+        if (gm >= best || nan || best != best) {
+          argmax_merge(best, bi, v.x, 4 * j);
+          argmax_merge(best, bi, v.y, 4 * j + 1);
+          argmax_merge(best, bi, v.z, 4 * j + 2);
+          argmax_merge(best, bi, v.w, 4 * j + 3);
+        }
       }
     } else {
       for (int j = tid; j < a.V; j += kAcceptThreads) argmax_merge(best, bi, __ldg(row + j), j);
@@ -107,21 +144,23 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, RowStat* out) 
     }
     return;
   }
-  // softmax statistics of z = x / T, online per thread: 8 float4 (32 values) per chunk, one
-  // rescale per chunk; at T == 1 the division is skipped (x / 1 is exact)
+  // softmax statistics of z = x / T, online per thread: groups of kU float4 with one rescale
+  // per group, the next group's loads in flight while this one is reduced; at T == 1 the
+  // division is skipped (x / 1 is exact). The per-element exponentials of these sums use the
+  // fast intrinsic (the decisions below use expf on the few values they need).
   const float T = a.temperature;
   const bool unit_t = (T == 1.f);
   float m = -INFINITY, s = 0.f;
   if (vec) {
     const float4* r4 = reinterpret_cast<const float4*>(row);
     const int n4 = a.V / 4;
-    constexpr int kU = 8;
+    constexpr int kU = 8;  // 8 float4 per thread in flight: 32 KB per CTA, 128 KB per SM
     for (int j0 = tid; j0 < n4; j0 += kU * kAcceptThreads) {
       float z[kU * 4];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
         const int j = j0 + u * kAcceptThreads;
-        float4 v = j < n4 ? __ldg(r4 + j) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        const float4 v = j < n4 ? __ldg(r4 + j) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
         z[4 * u] = v.x; z[4 * u + 1] = v.y; z[4 * u + 2] = v.z; z[4 * u + 3] = v.w;
       }
       float mx = m;
@@ -131,9 +170,9 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, RowStat* out) 
         mx = fmaxf(mx, z[i]);
       }
       if (mx != -INFINITY) {
-        float acc = s * expf(m - mx);
+        float acc = s * __expf(m - mx);
 #pragma unroll
-        for (int i = 0; i < kU * 4; ++i) acc += expf(z[i] - mx);
+        for (int i = 0; i < kU * 4; ++i) acc += __expf(z[i] - mx);
         s = acc;
         m = mx;
       }
@@ -144,7 +183,7 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, RowStat* out) 
       if (!unit_t) z = z / T;
       float mx = fmaxf(z, m);
       if (mx != -INFINITY) {
-        s = s * expf(m - mx) + expf(z - mx);
+        s = s * __expf(m - mx) + __expf(z - mx);
         m = mx;
       }
     }
@@ -179,7 +218,7 @@ SPECB200_DEVINL float prob_at(const AcceptArgs& a, const float* row, const RowSt
 // the segment holding the crossing, then scans that segment element by element (pass B).
 // Sums accumulate in double so both passes agree except within a few ulps of a boundary.
 constexpr int kSeg = 128;
-constexpr int kMaxSegs = 4096;  // V <= 524288
+constexpr int kMaxSegs = 4096;  // V <= kMaxSegs * kSeg = 524288 (argument check)
 SPECB200_DEVINL void seg_values(const AcceptArgs& a, const float* prow, const RowStat& ps, float p_inv,
                                 const float* qrow, const RowStat& qs, float q_inv, bool q_row, bool q_hot,
                                 int64_t dn, int use_p, int x0, float (&v)[4]) {
@@ -205,12 +244,12 @@ SPECB200_DEVINL void seg_values(const AcceptArgs& a, const float* prow, const Ro
   for (int j = 0; j < 4; ++j) {
     if (x0 + j >= a.V) { v[j] = 0.f; continue; }
     float px = pv[j];
-    if (a.logits) px = expf((a.temperature == 1.f ? px : px / a.temperature) - ps.m) * p_inv;
+    if (a.logits) px = __expf((a.temperature == 1.f ? px : px / a.temperature) - ps.m) * p_inv;
     if (use_p) { v[j] = px; continue; }
     float qx = 0.f;
     if (q_row) {
       qx = qv[j];
-      if (a.logits) qx = expf((a.temperature == 1.f ? qx : qx / a.temperature) - qs.m) * q_inv;
+      if (a.logits) qx = __expf((a.temperature == 1.f ? qx : qx / a.temperature) - qs.m) * q_inv;
     } else if (q_hot) {
       qx = (x0 + j == dn) ? 1.f : 0.f;
     }
@@ -218,135 +257,205 @@ SPECB200_DEVINL void seg_values(const AcceptArgs& a, const float* prow, const Ro
   }
 }
 
-__device__ int64_t residual_sample(const AcceptArgs& a, int b, int n, const RowStat* st) {
-  __shared__ double sh_seg[kMaxSegs];
-  __shared__ double sh_part[kAcceptWarps];
-  __shared__ double sh_total;
-  __shared__ int64_t sh_token;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const float* prow = row_ptr(a, b, n);
-  const RowStat ps = st[n];
-  const float p_inv = 1.0f / ps.s;
-  // q at row n: absent (k == 0 sampler), zero (bonus row), one-hot at the draft, or a row
-  const bool bonus = n >= a.k;
-  const bool q_row = a.q_present && !a.q_onehot && !bonus;
-  const bool q_hot = a.q_present && a.q_onehot && !bonus;
-  const int64_t dn = bonus ? -1 : a.draft[static_cast<int64_t>(b) * a.k + n];
-  const float* qrow = q_row ? row_ptr(a, b, a.k + 1 + n) : nullptr;
-  const RowStat qs = q_row ? st[a.k + 1 + n] : RowStat{0.f, 1.f, 0.f, 0};
-  const float q_inv = 1.0f / qs.s;
-  const int nseg = (a.V + kSeg - 1) / kSeg;
-
-  auto segment_sums = [&](int use_p) {
-    for (int s0 = warp; s0 < nseg; s0 += 4 * kAcceptWarps) {
-      double acc[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int sg = s0 + u * kAcceptWarps;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        if (sg < nseg) seg_values(a, prow, ps, p_inv, qrow, qs, q_inv, q_row, q_hot, dn, use_p, sg * kSeg + 4 * lane, v);
-        acc[u] = static_cast<double>(v[0]) + v[1] + v[2] + v[3];
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const double t = warp_sum_d(acc[u]);
-        const int sg = s0 + u * kAcceptWarps;
-        if (lane == 0 && sg < nseg) sh_seg[sg] = t;
-      }
-    }
-    __syncthreads();
-    double t = 0.0;
-    for (int sg = tid; sg < nseg; sg += kAcceptThreads) t += sh_seg[sg];
-    t = warp_sum_d(t);
-    if (lane == 0) sh_part[warp] = t;
-    __syncthreads();
-    if (tid == 0) {
-      double tot = 0.0;
-      for (int w = 0; w < kAcceptWarps; ++w) tot += sh_part[w];
-      sh_total = tot;
-    }
-    __syncthreads();
-  };
-  segment_sums(0);
-  int use_p = 0;
-  if (!(sh_total > 0.0)) {  // residual sums to 0: residual_distribution falls back to p
-    use_p = 1;
-    segment_sums(1);
+// The residual row of sequence b at its accepted length n: row pointers, statistics and the
+// q form of row n.
+struct ResidualRow {
+  const float* prow;
+  const float* qrow;
+  RowStat ps, qs;
+  float p_inv, q_inv;
+  bool q_row, q_hot;
+  int64_t dn;
+};
+__device__ ResidualRow residual_row(const AcceptArgs& a, int b, int n) {
+  ResidualRow r;
+  const RowStat* st = a.stats + static_cast<int64_t>(b) * a.R;
+  r.prow = row_ptr(a, b, n);
+  r.ps.m = __ldcg(&st[n].m);
+  r.ps.s = __ldcg(&st[n].s);
+  r.p_inv = 1.0f / r.ps.s;
+  const bool bonus = n >= a.k;  // the bonus row uses q = 0
+  r.q_row = a.q_present && !a.q_onehot && !bonus;
+  r.q_hot = a.q_present && a.q_onehot && !bonus;
+  r.dn = bonus ? -1 : a.draft[static_cast<int64_t>(b) * a.k + n];
+  r.qrow = r.q_row ? row_ptr(a, b, a.k + 1 + n) : nullptr;
+  r.qs = RowStat{0.f, 1.f, 0.f, 0};
+  if (r.q_row) {
+    r.qs.m = __ldcg(&st[a.k + 1 + n].m);
+    r.qs.s = __ldcg(&st[a.k + 1 + n].s);
   }
-  const double target = static_cast<double>(a.u_residual[b]) * sh_total;
-  if (tid == 0) sh_token = a.V - 1;  // searchsorted past the end, clamped
-  __syncthreads();
-  if (warp == 0) {
-    // first segment whose running sum passes the target (warp scan over segment sums)
-    double base = 0.0;
-    int s_hit = nseg;
-    for (int s0 = 0; s0 < nseg && s_hit == nseg; s0 += 32) {
-      const int sg = s0 + lane;
-      double v = sg < nseg ? sh_seg[sg] : 0.0;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const double t = __shfl_up_sync(0xffffffffu, v, o);
-        if (lane >= o) v += t;
-      }
-      const unsigned hit = __ballot_sync(0xffffffffu, sg < nseg && base + v > target);
-      if (hit) {
-        const int l = __ffs(hit) - 1;
-        s_hit = s0 + l;
-        const double before = __shfl_sync(0xffffffffu, v, l) - __shfl_sync(0xffffffffu, sg < nseg ? sh_seg[sg] : 0.0, l);
-        base += before;
-      } else {
-        base += __shfl_sync(0xffffffffu, v, 31);
-      }
-    }
-    // element scan from that segment on (continues if rounding put the crossing later)
-    for (int sg = s_hit; sg < nseg; ++sg) {
-      float v4[4];
-      seg_values(a, prow, ps, p_inv, qrow, qs, q_inv, q_row, q_hot, dn, use_p, sg * kSeg + 4 * lane, v4);
-      double e[4];
-      e[0] = v4[0];
-      e[1] = e[0] + v4[1];
-      e[2] = e[1] + v4[2];
-      e[3] = e[2] + v4[3];
-      double lsum = e[3];
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const double t = __shfl_up_sync(0xffffffffu, lsum, o);
-        if (lane >= o) lsum += t;
-      }
-      const double excl = base + lsum - e[3];
-      int first = 4;
-#pragma unroll
-      for (int j = 3; j >= 0; --j)
-        if (sg * kSeg + 4 * lane + j < a.V && excl + e[j] > target) first = j;
-      const unsigned hit = __ballot_sync(0xffffffffu, first < 4);
-      if (hit) {
-        const int l = __ffs(hit) - 1;
-        const int fj = __shfl_sync(0xffffffffu, first, l);
-        if (lane == 0) sh_token = sg * kSeg + 4 * l + fj;
-        break;
-      }
-      base += __shfl_sync(0xffffffffu, lsum, 31);
-    }
-  }
-  __syncthreads();
-  return sh_token;
+  r.q_inv = 1.0f / r.qs.s;
+  return r;
 }
 
-__global__ void __launch_bounds__(kAcceptThreads) accept_kernel(AcceptArgs a) {
+// Double sum of the residual (or of p when use_p) over [x0, x1), x0 % 4 == 0; block-wide.
+// Groups of 4 elements go to threads round-robin, four groups per thread per batch so that
+// their loads are in flight together.
+__device__ double residual_block_sum(const AcceptArgs& a, const ResidualRow& r, int use_p, int x0, int x1) {
+  __shared__ double sh_part[kAcceptWarps];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  double acc = 0.0;
+  for (int xb = x0; xb < x1; xb += 16 * kAcceptThreads) {
+    float v[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int x = xb + 4 * (tid + i * kAcceptThreads);
+      v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.f;
+      if (x < x1) seg_values(a, r.prow, r.ps, r.p_inv, r.qrow, r.qs, r.q_inv, r.q_row, r.q_hot, r.dn, use_p, x, v[i]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc += static_cast<double>(v[i][0]) + v[i][1] + v[i][2] + v[i][3];
+  }
+  acc = warp_sum_d(acc);
+  if (lane == 0) sh_part[warp] = acc;
+  __syncthreads();
+  double tot = 0.0;
+  for (int w = 0; w < kAcceptWarps; ++w) tot += sh_part[w];  // fixed order
+  __syncthreads();
+  return tot;
+}
+
+// First index x in [x0, x1) (x0 % 4 == 0) where base + cumsum passes target, or -1; base is the
+// running sum before x0. Thread t takes a contiguous run of groups; their totals are scanned
+// across the block (warp shuffles, then the warp totals) to give each run its starting sum.
+__device__ int residual_block_find(const AcceptArgs& a, const ResidualRow& r, int use_p, int x0, int x1, double base,
+                                   double target) {
+  __shared__ double sh_warp[kAcceptWarps];
+  __shared__ int sh_hit;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int n4 = (x1 - x0 + 3) / 4;
+  const int per = (n4 + kAcceptThreads - 1) / kAcceptThreads;  // groups of 4 per thread
+  const int g0 = tid * per, g1 = min(n4, g0 + per);
+  // up to kKeep groups per thread stay in registers for the crossing scan below (one load
+  // round trip for the whole chunk); longer runs are recomputed there
+  constexpr int kKeep = 4;
+  float keep[kKeep][4];
+  double run = 0.0;
+#pragma unroll
+  for (int q = 0; q < kKeep; ++q) {
+    keep[q][0] = keep[q][1] = keep[q][2] = keep[q][3] = 0.f;
+    const int gi = g0 + q;
+    if (gi < g1) seg_values(a, r.prow, r.ps, r.p_inv, r.qrow, r.qs, r.q_inv, r.q_row, r.q_hot, r.dn, use_p, x0 + 4 * gi, keep[q]);
+  }
+#pragma unroll
+  for (int q = 0; q < kKeep; ++q)
+    for (int j = 0; j < 4; ++j) run += (g0 + q < g1 && x0 + 4 * (g0 + q) + j < x1) ? keep[q][j] : 0.f;
+  for (int gi = g0 + kKeep; gi < g1; ++gi) {
+    float v[4];
+    seg_values(a, r.prow, r.ps, r.p_inv, r.qrow, r.qs, r.q_inv, r.q_row, r.q_hot, r.dn, use_p, x0 + 4 * gi, v);
+    for (int j = 0; j < 4; ++j) run += (x0 + 4 * gi + j < x1) ? v[j] : 0.f;
+  }
+  double incl = run;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const double t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) sh_warp[warp] = incl;
+  if (tid == 0) sh_hit = 0x7fffffff;
+  __syncthreads();
+  double before = base;
+  for (int w = 0; w < warp; ++w) before += sh_warp[w];
+  before += incl - run;  // exclusive prefix of this thread's run
+  if (before + run > target) {
+    double c = before;
+    for (int gi = g0; gi < g1; ++gi) {
+      float v[4];
+      if (gi - g0 < kKeep) {
+#pragma unroll
+        for (int q = 0; q < kKeep; ++q)
+          if (q == gi - g0) {
+            v[0] = keep[q][0]; v[1] = keep[q][1]; v[2] = keep[q][2]; v[3] = keep[q][3];
+          }
+      } else {
+        seg_values(a, r.prow, r.ps, r.p_inv, r.qrow, r.qs, r.q_inv, r.q_row, r.q_hot, r.dn, use_p, x0 + 4 * gi, v);
+      }
+      bool found = false;
+      for (int j = 0; j < 4; ++j) {
+        const int x = x0 + 4 * gi + j;
+        if (x >= x1) break;
+        c += v[j];
+        if (c > target) {
+          atomicMin(&sh_hit, x);
+          found = true;
+          break;
+        }
+      }
+      if (found) break;
+    }
+  }
+  __syncthreads();
+  const int hit = sh_hit;
+  __syncthreads();
+  return hit == 0x7fffffff ? -1 : hit;
+}
+
+// Grid C * B (1-D, b-major): chunk sums of the residual row; the last chunk CTA of b draws
+// the sample.
+__global__ void __launch_bounds__(kAcceptThreads) residual_kernel(AcceptArgs a) {
   pdl_wait();
-  const int r = blockIdx.x % a.R, b = blockIdx.x / a.R;  // b-major: a row's CTAs run together
-  RowStat* st = a.stats + static_cast<int64_t>(b) * a.R;
-  row_statistics(a, b, r, st + r);
+  const int c = blockIdx.x % a.C, b = blockIdx.x / a.C, tid = threadIdx.x;
   __shared__ int sh_last;
+  const int n = __ldcg(a.nsel + b);
+  const ResidualRow r = residual_row(a, b, n);
+  const int x0 = c * a.chunk, x1 = min(a.V, x0 + a.chunk);
+  const double part = residual_block_sum(a, r, 0, x0, x1);
+  double* sums = a.chunk_sums + static_cast<int64_t>(b) * a.C;
+  if (tid == 0) sums[c] = part;
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) sh_last = (atomicAdd(a.counters + b, 1) == a.R - 1);
+  if (tid == 0) sh_last = (atomicAdd(a.counters + a.B + b, 1) == a.C - 1);
   __syncthreads();
   if (!sh_last) return;
   __threadfence();
-  // Last CTA of batch row b: decisions, then the residual/bonus sample.
+  if (tid == 0) a.counters[a.B + b] = 0;  // ready for the next launch
+  double total = 0.0;
+  for (int i = 0; i < a.C; ++i) total += __ldcg(sums + i);  // chunk order
+  int use_p = 0;
+  if (!(total > 0.0)) {  // residual sums to 0: residual_distribution falls back to p
+    use_p = 1;
+    total = 0.0;
+    for (int i = 0; i < a.C; ++i) total += residual_block_sum(a, r, 1, i * a.chunk, min(a.V, (i + 1) * a.chunk));
+  }
+  const double target = static_cast<double>(a.u_residual[b]) * total;
+  // the chunk whose running sum passes the target, then its elements (later chunks too, if
+  // rounding put the crossing past the chunk's end); past the end: V - 1 (searchsorted, clamped)
+  double base = 0.0;
+  int first = a.C;
+  for (int i = 0; i < a.C; ++i) {
+    const double si = use_p ? residual_block_sum(a, r, 1, i * a.chunk, min(a.V, (i + 1) * a.chunk)) : __ldcg(sums + i);
+    if (base + si > target) {
+      first = i;
+      break;
+    }
+    base += si;
+  }
+  int64_t tok = a.V - 1;
+  for (int i = first; i < a.C; ++i) {
+    const int lo = i * a.chunk, hi = min(a.V, lo + a.chunk);
+    const int x = residual_block_find(a, r, use_p, lo, hi, base, target);
+    if (x >= 0) {
+      tok = x;
+      break;
+    }
+    base += use_p ? residual_block_sum(a, r, 1, lo, hi) : __ldcg(sums + i);
+  }
+  if (tid == 0) a.next_token[b] = tok;
+}
+
+// Decisions for sequence b once all its row statistics are in the workspace (the caller is
+// the last CTA of b): n accepted drafts, then the greedy next token. All threads of the CTA
+// call it.
+__device__ void decide(const AcceptArgs& a, int b) {
   __shared__ RowStat sst[32];
-  __shared__ int sh_n;
+  __shared__ int64_t sdraft[16];
+  __shared__ float su[16];
+  const RowStat* st = a.stats + static_cast<int64_t>(b) * a.R;
+  if (threadIdx.x >= 32 && threadIdx.x < 32 + a.k) {
+    const int i = threadIdx.x - 32;
+    sdraft[i] = a.draft[static_cast<int64_t>(b) * a.k + i];
+    su[i] = a.u_accept[static_cast<int64_t>(b) * a.k + i];
+  }
   if (threadIdx.x < a.R) {
     const RowStat* src = st + threadIdx.x;
     RowStat v;
@@ -362,7 +471,7 @@ __global__ void __launch_bounds__(kAcceptThreads) accept_kernel(AcceptArgs a) {
     int n = 0;
     bool run = true;
     for (int i = 0; i < a.k; ++i) {
-      const int64_t d = a.draft[static_cast<int64_t>(b) * a.k + i];
+      const int64_t d = sdraft[i];
       if (d < 0 || d >= a.V) { set_status(a.status, SPECB200_ERR_RANGE); run = false; continue; }
       float px, qx = 1.f;
       if (a.greedy) {
@@ -379,21 +488,30 @@ __global__ void __launch_bounds__(kAcceptThreads) accept_kernel(AcceptArgs a) {
         if (a.q_present && !a.q_onehot) qx = sst[a.k + 1 + i].zx;
       }
       if (!(qx > 0.f)) set_status(a.status, SPECB200_ERR_ZERO_Q);
-      const bool acc = a.u_accept[static_cast<int64_t>(b) * a.k + i] * qx < px;
+      const bool acc = su[i] * qx < px;
       if (run && acc) ++n; else run = false;
     }
-    sh_n = n;
     a.n_accepted[b] = n;
+    a.nsel[b] = n;
+    if (a.greedy && !a.decide_only) a.next_token[b] = sst[n].amax;
   }
   __syncthreads();
-  if (a.decide_only) return;
-  const int n = sh_n;
-  if (a.greedy) {
-    if (threadIdx.x == 0) a.next_token[b] = sst[n].amax;
-    return;
-  }
-  const int64_t tok = residual_sample(a, b, n, sst);
-  if (threadIdx.x == 0) a.next_token[b] = tok;
+}
+
+__global__ void __launch_bounds__(kAcceptThreads, 4) accept_kernel(AcceptArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();  // the residual kernel may start its prologue; it waits for this grid
+  const int r = blockIdx.x % a.R, b = blockIdx.x / a.R;  // b-major: a row's CTAs run together
+  RowStat* st = a.stats + static_cast<int64_t>(b) * a.R;
+  row_statistics(a, b, r, st + r);
+  __shared__ int sh_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) sh_last = (atomicAdd(a.counters + b, 1) == a.R - 1);
+  __syncthreads();
+  if (!sh_last) return;
+  __threadfence();
+  decide(a, b);
 }
 
 // probabilities() of lm/sampling.py:13-18, materialised: one-hot of the first maximum at
@@ -454,9 +572,33 @@ __global__ void __launch_bounds__(kAcceptThreads)
 
 using namespace specb200;
 
+namespace specb200 {
+namespace {
+// Both kernels on `s`: the counters are cleared first (a call with another B may have left
+// statistics where they sit); the residual kernel follows with programmatic dependent launch.
+int launch_accept(AcceptArgs& a, char* ws, const AcceptLayout& l, cudaStream_t s) {
+  a.counters = reinterpret_cast<int*>(ws + l.counters);
+  a.stats = reinterpret_cast<RowStat*>(ws + l.stats);
+  a.nsel = reinterpret_cast<int*>(ws + l.nsel);
+  a.chunk_sums = reinterpret_cast<double*>(ws + l.sums);
+  a.C = residual_chunks(a.V);
+  const int per = 4 * kAcceptThreads;
+  a.chunk = ((a.V + a.C - 1) / a.C + per - 1) / per * per;
+  if (a.status) cudaMemsetAsync(a.status, 0, sizeof(int32_t), s);
+  cudaMemsetAsync(a.counters, 0, 2 * static_cast<size_t>(a.B) * sizeof(int), s);
+  cudaError_t e = cudaSuccess;
+  accept_kernel<<<static_cast<unsigned>(a.R) * a.B, kAcceptThreads, 0, s>>>(a);
+  e = cudaGetLastError();
+  if (e == cudaSuccess && !a.greedy && !a.decide_only)
+    e = launch_kernel(residual_kernel, dim3(static_cast<unsigned>(a.C) * a.B), dim3(kAcceptThreads), 0, s, true, a);
+  return e == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
+}
+}  // namespace
+}  // namespace specb200
+
+// Workspace for the largest V the kernels accept (the residual chunk sums depend on V).
 extern "C" size_t specb200_accept_workspace_bytes(int B, int k) {
-  const size_t R = 2 * static_cast<size_t>(k) + 1;
-  return 256 + static_cast<size_t>(B) * sizeof(int) + 256 + static_cast<size_t>(B) * R * sizeof(RowStat);
+  return accept_layout(B, k, kMaxSegs * kSeg).total;
 }
 
 extern "C" int specb200_set_error(int code, const char* msg);
@@ -494,18 +636,10 @@ extern "C" int specb200_accept(const float* p, const float* q, const int64_t* dr
   a.n_accepted = n_accepted;
   a.next_token = next_token;
   a.status = status;
-  char* ws = static_cast<char*>(workspace);
-  a.counters = reinterpret_cast<int*>(ws + 256);
-  a.stats = reinterpret_cast<RowStat*>(ws + 256 + ((static_cast<size_t>(B) * sizeof(int) + 255) / 256) * 256);
-  if (reinterpret_cast<char*>(a.stats + static_cast<size_t>(B) * a.R) > ws + workspace_bytes)
-    return specb200_set_error(SPECB200_ERR_WORKSPACE, "accept: workspace too small");
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (status) cudaMemsetAsync(status, 0, sizeof(int32_t), s);
-  // The ticket counters sit where a call with another B may have left statistics: clear them.
-  cudaMemsetAsync(a.counters, 0, static_cast<size_t>(B) * sizeof(int), s);
-  accept_kernel<<<static_cast<unsigned>(a.R) * B, kAcceptThreads, 0, s>>>(a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
+  const AcceptLayout l = accept_layout(B, k, V);
+  if (l.total > workspace_bytes) return specb200_set_error(SPECB200_ERR_WORKSPACE, "accept: workspace too small");
+  if (launch_accept(a, static_cast<char*>(workspace), l, static_cast<cudaStream_t>(stream)) != SPECB200_OK)
+    return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
   return SPECB200_OK;
 }
 
@@ -540,9 +674,12 @@ extern "C" int specb200_probabilities(const float* logits, int rows, int V, floa
 namespace {
 constexpr int kNoAllocMaxB = 512;
 constexpr int kNoAllocMaxK = 15;
-constexpr size_t kNoAllocCounterBytes = ((kNoAllocMaxB * sizeof(int) + 255) / 256) * 256;
+// accept_layout(kNoAllocMaxB, kNoAllocMaxK, V) for the largest V: counters, statistics, the
+// accepted lengths and 16 residual chunk sums per row (~331 KB)
 constexpr size_t kNoAllocScratchBytes =
-    kNoAllocCounterBytes + static_cast<size_t>(kNoAllocMaxB) * (2 * kNoAllocMaxK + 1) * sizeof(RowStat);
+    256 + ((2 * kNoAllocMaxB * sizeof(int) + 255) / 256) * 256 +
+    ((static_cast<size_t>(kNoAllocMaxB) * (2 * kNoAllocMaxK + 1) * sizeof(RowStat) + 255) / 256) * 256 +
+    ((kNoAllocMaxB * sizeof(int) + 255) / 256) * 256 + ((kNoAllocMaxB * 16 * sizeof(double) + 255) / 256) * 256;
 
 static __device__ __align__(256) unsigned char g_accept_scratch[kNoAllocScratchBytes];
 
@@ -608,13 +745,10 @@ extern "C" int specb200_accept_noalloc(const float* p, const float* q, const int
   a.n_accepted = n_accepted;
   a.next_token = next_token;
   a.status = status;
-  a.counters = static_cast<int*>(scratch);
-  a.stats = reinterpret_cast<RowStat*>(static_cast<char*>(scratch) + kNoAllocCounterBytes);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (status) cudaMemsetAsync(status, 0, sizeof(int32_t), s);
-  cudaMemsetAsync(a.counters, 0, static_cast<size_t>(B) * sizeof(int), s);  // the array keeps old tickets
-  accept_kernel<<<static_cast<unsigned>(a.R) * B, kAcceptThreads, 0, s>>>(a);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
+  const AcceptLayout l = accept_layout(B, k, V);
+  if (l.total > kNoAllocScratchBytes) return specb200_set_error(SPECB200_ERR_ARG, "accept_noalloc: scratch too small");
+  // the array keeps old tickets: launch_accept clears the counters first
+  if (launch_accept(a, static_cast<char*>(scratch), l, static_cast<cudaStream_t>(stream)) != SPECB200_OK)
+    return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
   return SPECB200_OK;
 }

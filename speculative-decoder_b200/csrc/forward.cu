@@ -471,6 +471,20 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
   return SPECB200_OK;
 }
 
+// Kernel launches of one forward call: 3 for the layer chain (chain kernel, final norm, LM head),
+// 1 for the layer stream, 3 + 7 L for the per-layer kernels (prep, 7 per layer, final norm, head).
+extern "C" int specb200_forward_launches(void* model, int B, int T) {
+  if (!model || B <= 0 || T <= 0) return 0;
+  const Model& m = *static_cast<Model*>(model);
+  ChainPhase ph[4];
+  int splits = 0;
+  ChainLayout L;
+  if (use_chain(m, B, T, ph, &splits, &L)) return 3;
+  int grid = 0, mc = 0;
+  if (use_stream(m, B, T, &grid, &mc)) return 1;
+  return 3 + 7 * m.cfg.n_layers;
+}
+
 extern "C" int specb200_forward_uses_stream(void* model, int B, int T) {
   if (!model || B <= 0 || T <= 0) return 0;
   const Model& m = *static_cast<Model*>(model);

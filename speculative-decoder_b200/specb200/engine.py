@@ -133,7 +133,7 @@ class Engine:
     # ------------------------------------------------------------------ device-level call
     def launches(self, b: int, t: int) -> int:
         """Kernel launches of one forward call of B rows x T tokens."""
-        return {2: 3, 1: 1}.get(lib().specb200_forward_uses_stream(self.handle, b, t), 3 + 7 * self.n_layers)
+        return lib().specb200_forward_launches(self.handle, b, t)
 
     def schedule(self, b: int, t: int) -> str:
         """The schedule a forward call of B rows x T tokens runs: "chain" (one thread-block
