@@ -48,11 +48,13 @@ PROMPT_LEN, NEW_TOKENS, K, BLOCK = 512, 256, 4, 16
 WEIGHT_BYTES = 3_422_752_768          # 1.7B linears + tied embedding, bf16, read once per verify
 KV_BYTES_PER_TOKEN = 196_608          # 24 layers x 2 x 32 heads x 64 x 2 B
 ACCEPT_BYTES = 113_246_208            # config 3: 64 x (5 + 4) x 49152 x 4 B
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic byte of the verify
-# kernel, from one ncu capture of the layer-stream kernel on the 6-layer case (1.0426 GB of
-# traffic for 1.0383 GB of algorithmic bytes; profiles/stream_kernel_verify_1p7b_6layers.txt);
-# traffic grows with the layers streamed, so the full-size figure scales by the same ratio.
-VERIFY_TRAFFIC_RATIO = (1_038_322_000 + 4_316_416) / 1_038_340_096
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic byte of one verify
+# forward, from ncu captures of the 6-layer case (1.0383 GB of algorithmic bytes): per-layer
+# kernels 1.0432 GB (profiles/traffic_verify_step_1p7b_6layers_perlayer.txt), layer-stream
+# kernel 1.0426 GB (profiles/stream_kernel_verify_1p7b_6layers.txt). Traffic grows with the
+# layers streamed, so the full-size figure scales by the same ratio.
+VERIFY_TRAFFIC_RATIO = {"layers": (1_042_254_080 + 901_632) / 1_038_340_096,
+                        "stream": (1_038_322_000 + 4_316_416) / 1_038_340_096}
 
 
 def weight_bytes(spec: dict) -> int:
@@ -551,9 +553,9 @@ def main() -> None:
                 "d2h_bytes_per_step": NEW_TOKENS * 8 * world},
         "roofline": {"bound": "hbm", "kernel": "verify step (one (k+1)-token target forward, CUDA graph)",
                      "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                     "traffic": vstep["bytes"] * VERIFY_TRAFFIC_RATIO if te.launches(1, K + 1) == 1 else None,
-                     "traffic_source": ("ncu capture of the 6-layer stream kernel, scaled by algorithmic bytes"
-                                        if te.launches(1, K + 1) == 1 else "per-layer kernels: see verify_launches"),
+                     "traffic": vstep["bytes"] * VERIFY_TRAFFIC_RATIO.get(te.schedule(1, K + 1), float("nan")),
+                     "traffic_source": f"ncu capture of the 6-layer verify ({te.schedule(1, K + 1)} schedule), "
+                                       "scaled by algorithmic bytes",
                      "peak_source": pk["source"], "verify_step_us": vstep["us"],
                      "algorithmic_bytes": vstep["bytes"], "context_tokens": vstep["context"]},
         "accept": {"us": acc["us"], "achieved": acc_gbs, "frac": acc_gbs / pk["hbm_gbs"], "unit": "GB/s",
