@@ -553,7 +553,8 @@ def main() -> None:
                 "d2h_bytes_per_step": NEW_TOKENS * 8 * world},
         "roofline": {"bound": "hbm", "kernel": "verify step (one (k+1)-token target forward, CUDA graph)",
                      "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                     "traffic": vstep["bytes"] * VERIFY_TRAFFIC_RATIO.get(te.schedule(1, K + 1), float("nan")),
+                     "traffic": (vstep["bytes"] * VERIFY_TRAFFIC_RATIO[te.schedule(1, K + 1)]
+                                 if te.schedule(1, K + 1) in VERIFY_TRAFFIC_RATIO else None),
                      "traffic_source": f"ncu capture of the 6-layer verify ({te.schedule(1, K + 1)} schedule), "
                                        "scaled by algorithmic bytes",
                      "peak_source": pk["source"], "verify_step_us": vstep["us"],
