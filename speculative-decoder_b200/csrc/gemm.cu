@@ -271,8 +271,20 @@ GemmShape plan_gemm(int M, int N, int K, bool tensor_core) {
   s.n_tiles = (N + kTileN - 1) / kTileN;
   s.kblocks = (K + kTileK - 1) / kTileK;
   const int ctas = s.n_tiles * s.m_tiles;
-  int splits = (148 + ctas / 2) / ctas;
-  splits = std::max(1, std::min(splits, std::min(16, s.kblocks)));
+  int splits;
+  if (tensor_core) {
+    // The fewest K-splits that let every CTA's K-range fit its ring of weight stages (so the
+    // whole share is prefetched before griddepcontrol.wait and the split-K reduction has few
+    // contributors), but never more CTAs than fill the GPU once.
+    const int per_stage = kTileN * kTileK * 2 + s.BN * kTileK * 2;
+    const int stages = std::max(2, std::min(8, (200 * 1024) / per_stage));
+    const int fit = (s.kblocks + stages - 1) / stages;
+    const int fill = std::max(1, 148 / ctas);
+    splits = std::max(1, std::min({fit, fill, 16, s.kblocks}));
+  } else {
+    splits = (148 + ctas / 2) / ctas;
+    splits = std::max(1, std::min(splits, std::min(16, s.kblocks)));
+  }
   if (ctas > kGemmMaxCounters) splits = 1;
   s.splits = splits;
   return s;
