@@ -274,6 +274,63 @@ def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30
     return r
 
 
+def gemv_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
+    """The GEMV schedule's per-CTA launch record ([4 n_layers + 1][296][8] globaltimer stamps:
+    entry, return from griddepcontrol.wait, inputs staged, first weight chunk landed, end; 4
+    linear launches per layer, then the LM head). Per linear, medians over layers (us) of:
+    `gap`, previous launch's last end to this launch's first wait return (for o it spans the
+    attention kernel); `late`, CTAs that entered after that first wait return; `staged`,
+    `landed`, `endo`: median / max over CTAs of each stamp's offset from the first wait return;
+    `wait`, `dot`: median / max over CTAs of the time spent waiting for weight chunks and in the
+    dot products. `attention`: medians over layers of the attention launch's gap after q/k/v
+    (`gap_in`) and before o (`gap_out`) and of its stamps' latest offsets from its first wait
+    return (keys landed, merged within the CTA, partial published, end of the merge)."""
+    n = 4 * n_layers + 1
+    t = trace.flatten()[: n * 296 * 8].view(n, 296, 8).cpu().to(torch.float64)
+    per = []
+    for i in range(n):
+        ok = t[i, :, 0] > 0
+        ti = t[i][ok] / 1e3
+        r0 = float(ti[:, 1].min())
+        per.append({"n": int(ok.sum()), "r0": r0, "end": float(ti[:, 4].max()),
+                    "late": int((ti[:, 0] > r0).sum()),
+                    "staged": (float((ti[:, 2] - r0).median()), float((ti[:, 2] - r0).max())),
+                    "landed": (float((ti[:, 3] - r0).median()), float((ti[:, 3] - r0).max())),
+                    "endo": (float((ti[:, 4] - r0).median()), float((ti[:, 4] - r0).max())),
+                    "wait": (float(ti[:, 5].median()), float(ti[:, 5].max())),
+                    "dot": (float(ti[:, 6].median()), float(ti[:, 6].max()))})
+    out = {"total_us": round(per[-1]["end"] - per[0]["r0"], 1)}
+    med = lambda v: round(statistics.median(v), 2)  # noqa: E731
+    for j, name in enumerate(["qkv", "o", "gate_up", "down", "head"]):
+        rows = [n - 1] if name == "head" else [4 * l + j for l in range(n_layers)]
+        d = {"ctas": per[rows[0]]["n"], "late": med([per[i]["late"] for i in rows])}
+        gaps = [per[i]["r0"] - per[i - 1]["end"] for i in rows if i > 0]
+        d["gap"] = med(gaps) if gaps else None
+        for key in ("staged", "landed", "endo", "wait", "dot"):
+            d[key] = [med([per[i][key][0] for i in rows]), med([per[i][key][1] for i in rows])]
+        out[name] = d
+    # attention launches (after the linear records): offsets from the first wait return
+    att = {"gap_in": [], "gap_out": [], "landed": [], "merged": [], "published": [], "end": [], "ctas": []}
+    for l in range(n_layers):
+        a = trace.flatten()[(n + l) * 296 * 8:(n + l + 1) * 296 * 8].view(296, 8).cpu().to(torch.float64)
+        ok = a[:, 0] > 0
+        if not bool(ok.any()):
+            continue
+        a = a[ok] / 1e3
+        r0 = float(a[:, 1].min())
+        att["ctas"].append(int(ok.sum()))
+        att["gap_in"].append(r0 - per[4 * l]["end"])
+        att["gap_out"].append(per[4 * l + 1]["r0"] - float(a[:, 5].max()))
+        for k, key in ((2, "landed"), (3, "merged"), (4, "published"), (5, "end")):
+            v = a[:, k]
+            v = v[v > 0]
+            if v.numel():
+                att[key].append(float((v - r0).max()))
+    if att["ctas"]:
+        out["attention"] = {k: med(v) for k, v in att.items() if v}
+    return out
+
+
 def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30, trace: bool = False) -> dict:
     """One single-token draft-model forward (135M architecture, B=1), CUDA graph, as in each
     of the k draft steps of a round."""
@@ -321,10 +378,15 @@ def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30, 
         n_ph = 2 + 5 * spec["num_hidden_layers"]
         tr = torch.zeros(torch.cuda.get_device_properties(device).multi_processor_count, n_ph, 8, dtype=torch.int64,
                          device=device)
+        sched = eng.schedule(1, 1)
+        if sched == "gemv":
+            tr = torch.zeros(5 * spec["num_hidden_layers"] + 1, 296, 8, dtype=torch.int64, device=device)
         eng.forward_device(cache, ids, one, pastt, table, cap, True, logits, status, ws, trace=tr)
         torch.cuda.synchronize()
-        if eng.schedule(1, 1) == "chain":
+        if sched == "chain":
             r["trace"] = chain_trace_summary(tr, spec["num_hidden_layers"])
+        elif sched == "gemv":
+            r["trace"] = gemv_trace_summary(tr, spec["num_hidden_layers"])
         else:
             r["trace"] = trace_summary(tr, spec["num_hidden_layers"])
     return r

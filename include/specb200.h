@@ -201,8 +201,11 @@ typedef struct specb200_batch {
   float* logits;                /* fp32 [B*T, V] or [B, V]                                */
   int max_kv_len;               /* >= past_len[b] + n_new[b] for every row                */
   int32_t* status;              /* device int32 status word (cleared by the call)         */
-  uint64_t* trace;              /* NULL, or [grid x phases x 8] globaltimer stamps written */
-                                /* by the layer-stream kernel (profiling only)             */
+  uint64_t* trace;              /* NULL, or globaltimer stamps (profiling only): the layer- */
+                                /* stream kernel writes [grid x phases x 8]; the GEMV       */
+                                /* schedule [4 n_layers + 1 launches][296 CTAs][8]: entry, */
+                                /* wait return, inputs staged, weights landed, end, then   */
+                                /* the attention launches [n_layers][296][8] (zeroed first) */
 } specb200_batch;
 
 /* Weight tiles for the layer-stream kernel: W [N, K] bf16 row-major is rewritten as
@@ -215,8 +218,9 @@ int specb200_pack_tiles(const void* w, int N, int K, void* out, void* stream);
 size_t specb200_forward_workspace_bytes(void* model, int B, int T, int max_kv_len);
 /* Which schedule a call with B rows of T tokens runs: 2 = the layer stack on one thread-block
  * cluster (small models, at most 8 token rows; 3 launches with the final norm and LM head),
- * 1 = the persistent layer-stream kernel over all SMs (one launch), 0 = one kernel per layer
- * op (3 + 7 n_layers launches). */
+ * 1 = the persistent layer-stream kernel over all SMs (one launch), 3 = decode steps of at
+ * most 4 token rows on the GEMV kernels with the norms folded in (2 + 5 n_layers launches),
+ * 0 = one kernel per layer op (3 + 7 n_layers launches). */
 int specb200_forward_uses_stream(void* model, int B, int T);
 /* Kernel launches one forward call with B rows of T tokens makes (no reference counterpart;
  * used to count launches). */

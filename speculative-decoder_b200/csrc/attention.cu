@@ -32,12 +32,11 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnKernelArgs 
 }
 
 // Decode / verify shapes (bf16, d = 64, T x G <= 16): one tensor-core item per (split, kv
-// head, sequence).
+// head, sequence). The item itself waits on the previous kernel, after loading the cached keys.
 __global__ void __launch_bounds__(kAttnThreads) attention_mma_kernel(AttnKernelArgs ka) {
   __shared__ __align__(128) uint8_t smem[kAmItemSmem];
   pdl_launch_dependents();
-  pdl_wait();
-  attention_item_mma(ka, blockIdx.z, blockIdx.y, blockIdx.x, smem);
+  attention_item_mma(ka, blockIdx.z, blockIdx.y, blockIdx.x, smem, true);
 }
 
 template <typename T, int D>

@@ -88,6 +88,8 @@ SPECB200_DEVINL void am_init(AmState& st, const __nv_bfloat16* q_s) {
 
 // One warp's 8 keys: rows of k_s / v_s (swizzled [.][64] bf16) key0 .. key0 + 7 hold absolute
 // keys kabs .. kabs + 7. Key kabs + j is visible to row r iff kabs + j < lim_r and j < nvalid.
+// The softmax runs in base 2: logits are scaled by scale * log2(e), so the running maxima m
+// (and every partial maximum derived from them) are in log2 units and weights are exp2f(x - m).
 SPECB200_DEVINL void am_step(AmState& st, const __nv_bfloat16* k_s, const __nv_bfloat16* v_s, int key0, int kabs,
                              int nvalid, int lim0, int lim1, float scale) {
   const int lane = threadIdx.x & 31, g = lane >> 2, tig = lane & 3;
@@ -101,10 +103,11 @@ SPECB200_DEVINL void am_step(AmState& st, const __nv_bfloat16* k_s, const __nv_b
   }
   // s[0], s[1]: row g, keys 2 tig + {0, 1}; s[2], s[3]: row g + 8
   float p[4];
+  const float sl = scale * 1.4426950408889634f;  // log2(e)
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int lim = half ? lim1 : lim0;
-    float x0 = s[2 * half] * scale, x1 = s[2 * half + 1] * scale;
+    float x0 = s[2 * half] * sl, x1 = s[2 * half + 1] * sl;
     const int j0 = 2 * tig, j1 = 2 * tig + 1;
     if (j0 >= nvalid || kabs + j0 >= lim) x0 = -INFINITY;
     if (j1 >= nvalid || kabs + j1 >= lim) x1 = -INFINITY;
@@ -112,9 +115,9 @@ SPECB200_DEVINL void am_step(AmState& st, const __nv_bfloat16* k_s, const __nv_b
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
     const float m_old = st.m[half], m_new = fmaxf(m_old, mx);
-    const float alpha = (m_new == -INFINITY) ? 1.f : expf(m_old - m_new);
-    p[2 * half] = (m_new == -INFINITY) ? 0.f : expf(x0 - m_new);
-    p[2 * half + 1] = (m_new == -INFINITY) ? 0.f : expf(x1 - m_new);
+    const float alpha = (m_new == -INFINITY) ? 1.f : exp2f(m_old - m_new);
+    p[2 * half] = (m_new == -INFINITY) ? 0.f : exp2f(x0 - m_new);
+    p[2 * half + 1] = (m_new == -INFINITY) ? 0.f : exp2f(x1 - m_new);
     st.l[half] = st.l[half] * alpha + p[2 * half] + p[2 * half + 1];
     st.m[half] = m_new;
 #pragma unroll
@@ -146,7 +149,7 @@ SPECB200_DEVINL void am_step(AmState& st, const __nv_bfloat16* k_s, const __nv_b
 }
 
 // Merge the four warps' states (fixed order) into rows 0..R-1 of out_o [R][64] (unnormalised,
-// relative to out_m) with out_m[R], out_l[R]. scratch: 4 * (16 * 64 + 32) floats. Runs on the
+// relative to out_m, a base-2 maximum) with out_m[R], out_l[R]. scratch: 4 * (16 * 64 + 32) floats. Runs on the
 // 128 threads; ends with the caller's named barrier `sync`.
 template <typename Sync>
 __device__ void am_merge(const AmState& st, float* scratch, int R, float* out_o, float* out_m, float* out_l, Sync sync) {
@@ -184,7 +187,7 @@ __device__ void am_merge(const AmState& st, float* scratch, int R, float* out_o,
     for (int w = 0; w < 4; ++w) {
       const float* b = scratch + w * (16 * 64 + 32);
       const float mw = b[16 * 64 + r];
-      const float wgt = (mw == -INFINITY) ? 0.f : expf(mw - M);
+      const float wgt = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
       O = fmaf(b[r * 64 + c], wgt, O);
       L = fmaf(b[16 * 64 + 16 + r], wgt, L);
     }

@@ -785,7 +785,7 @@ __device__ bool attention_phase(const ChainArgs& a, const Ctx& c, int l, Counter
       const float ms = sp == 0 ? om[r] : base[R * 64 + r];
       const float ls = sp == 0 ? ol[r] : base[R * 64 + R + r];
       const float ov = sp == 0 ? oo[i] : base[i];
-      const float w = (ms == -INFINITY) ? 0.f : expf(ms - Mx);
+      const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - Mx);  // base-2 maxima (am_step)
       O = fmaf(ov, w, O);
       Ls = fmaf(ls, w, Ls);
     }

@@ -14,6 +14,7 @@
 
 #include "attn_core.cuh"
 #include "gemm.cuh"
+#include "gemv.cuh"
 #include "kernels.cuh"
 #include "chain.cuh"
 #include "stream.cuh"
@@ -40,6 +41,7 @@ struct Model {
   int qkv_n;
   bool stream_ok;  // packed weights present and shapes within the layer-stream kernel's limits
   int chain_C = 0;  // cluster size of the layer-chain kernel, 0 = not used for this model
+  bool gemv_ok = false;  // bf16 weights usable by the decode-step GEMV kernels (gemv.cu)
 };
 
 // Whether a call of this shape runs the cluster layer-chain kernel (small models, decode
@@ -83,8 +85,23 @@ struct Carve {
   int csplits;
   ChainLayout cl;
   GemmShape g_qkv, g_o, g_gu, g_down, g_head;
+  bool gemv;  // decode-step schedule: the per-layer order with GEMV kernels and fused norms
+  GemvPlan v_qkv, v_o, v_gu, v_down, v_head;
   AttnPlan ap;
 };
+
+// Whether a call of this shape runs the decode-step GEMV schedule (at most kGemvMaxRows token
+// rows, bf16); fills the five plans.
+bool use_gemv(const Model& m, int M, int rows_out, GemvPlan* qkv, GemvPlan* o, GemvPlan* gu, GemvPlan* down,
+              GemvPlan* head) {
+  const specb200_model_config& c = m.cfg;
+  if (!m.gemv_ok || M > kGemvMaxRows) return false;
+  const int qd = c.n_heads * c.head_dim;
+  return plan_gemv(EPI_QKV, M, m.qkv_n, c.hidden, c.head_dim, qkv) && plan_gemv(EPI_RESID, M, c.hidden, qd, 0, o) &&
+         plan_gemv(EPI_SILU_MUL, M, 2 * c.intermediate, c.hidden, 0, gu) &&
+         plan_gemv(EPI_RESID, M, c.hidden, c.intermediate, 0, down) &&
+         plan_gemv(EPI_STORE, rows_out, c.vocab, c.hidden, 0, head);
+}
 
 Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   const specb200_model_config& c = m.cfg;
@@ -101,6 +118,7 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   r.g_head = plan_gemm(rows_out, c.vocab, c.hidden, tc);
   r.chain = use_chain(m, B, T, r.cph, &r.csplits, &r.cl);
   r.stream = !r.chain && use_stream(m, B, T, &r.grid, &r.max_contrib);
+  r.gemv = !r.chain && !r.stream && use_gemv(m, M, rows_out, &r.v_qkv, &r.v_o, &r.v_gu, &r.v_down, &r.v_head);
   r.ap = r.stream ? plan_attention_decode(B, c.n_kv_heads, max_kv_len, r.grid)
                   : plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len, tc && c.head_dim == 64);
   // The two ticket-counter regions sit at fixed offsets so that they stay zero across calls
@@ -257,12 +275,33 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     if (tc) return launch_gemm_tc(sh, *wmap, *xmap, e, gscr, status, s, pdl);
     return launch_gemm_simt<T>(sh, static_cast<const T*>(w), x, e, gscr, status, s, pdl);
   };
+  // Decode-step schedule (bf16 only): the GEMV kernels, with the two RMSNorms of each layer
+  // folded into the q/k/v and gate/up kernels. With a trace buffer, launch i of the forward
+  // (4 per layer, then the head) records its timing in trace[4 i .. 4 i + 3].
+  int gemv_slot = 0;
+  auto gemv = [&](const GemvPlan& p, const void* w, const T* x, const void* norm_w, const Epilogue& e, int N,
+                  int K) -> int {
+    GemvArgs g = {};
+    g.w = static_cast<const __nv_bfloat16*>(w);
+    g.x = reinterpret_cast<const __nv_bfloat16*>(x);
+    g.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+    g.eps = c.rms_eps;
+    g.M = M;
+    g.N = N;
+    g.K = K;
+    g.p = p;
+    g.e = e;
+    g.status = status;
+    g.trace = reinterpret_cast<unsigned long long*>(bt.trace);
+    g.trace_slot = gemv_slot++;
+    return launch_gemv(g, s, pdl);
+  };
 
   for (int l = 0; l < c.n_layers; ++l) {
     const specb200_layer_weights& L = m.layers[l];
     const LayerMaps* mp = tc ? &m.maps[l] : nullptr;
-    if ((rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.attn_norm), M, c.hidden, c.rms_eps, xbuf, nullptr, 1, s,
-                                pdl)))
+    if (!cv.gemv && (rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.attn_norm), M, c.hidden, c.rms_eps, xbuf,
+                                            nullptr, 1, s, pdl)))
       return rc;
     Epilogue eq = {};
     eq.op = EPI_QKV;
@@ -277,7 +316,9 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     eq.n_heads = c.n_heads;
     eq.n_kv_heads = c.n_kv_heads;
     eq.head_dim = c.head_dim;
-    if ((rc = gemm(cv.g_qkv, mp ? &mp->qkv : nullptr, &x_hidden, L.w_qkv, xbuf, eq))) return rc;
+    rc = cv.gemv ? gemv(cv.v_qkv, L.w_qkv, hidden, L.attn_norm, eq, m.qkv_n, c.hidden)
+                 : gemm(cv.g_qkv, mp ? &mp->qkv : nullptr, &x_hidden, L.w_qkv, xbuf, eq);
+    if (rc) return rc;
 
     AttnArgs aa;
     aa.q = qbuf;
@@ -296,22 +337,33 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     aa.scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
     aa.out = attn;
     aa.status = status;
+    if (cv.gemv && bt.trace) {  // after the GEMV launch records
+      aa.trace = reinterpret_cast<unsigned long long*>(bt.trace) +
+                 static_cast<size_t>(4 * c.n_layers + 1) * kGemvTraceCtas * kGemvTraceStamps;
+      aa.trace_slot = l;
+    }
     if ((rc = launch_attention<T>(aa, cv.ap, attn_counters, attn_parts, s, pdl))) return rc;
 
     Epilogue er = {};
     er.op = EPI_RESID;
     er.out = hidden;
     er.ldo = c.hidden;
-    if ((rc = gemm(cv.g_o, mp ? &mp->o : nullptr, &x_attn, L.w_o, attn, er))) return rc;
-    if ((rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.mlp_norm), M, c.hidden, c.rms_eps, xbuf, nullptr, 1, s,
-                                pdl)))
+    rc = cv.gemv ? gemv(cv.v_o, L.w_o, attn, nullptr, er, c.hidden, qd)
+                 : gemm(cv.g_o, mp ? &mp->o : nullptr, &x_attn, L.w_o, attn, er);
+    if (rc) return rc;
+    if (!cv.gemv && (rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.mlp_norm), M, c.hidden, c.rms_eps, xbuf,
+                                            nullptr, 1, s, pdl)))
       return rc;
     Epilogue eg = {};
     eg.op = EPI_SILU_MUL;
     eg.out = act;
     eg.ldo = c.intermediate;
-    if ((rc = gemm(cv.g_gu, mp ? &mp->gu : nullptr, &x_hidden, L.w_gate_up, xbuf, eg))) return rc;
-    if ((rc = gemm(cv.g_down, mp ? &mp->down : nullptr, &x_act, L.w_down, act, er))) return rc;
+    rc = cv.gemv ? gemv(cv.v_gu, L.w_gate_up, hidden, L.mlp_norm, eg, 2 * c.intermediate, c.hidden)
+                 : gemm(cv.g_gu, mp ? &mp->gu : nullptr, &x_hidden, L.w_gate_up, xbuf, eg);
+    if (rc) return rc;
+    rc = cv.gemv ? gemv(cv.v_down, L.w_down, act, nullptr, er, c.hidden, c.intermediate)
+                 : gemm(cv.g_down, mp ? &mp->down : nullptr, &x_act, L.w_down, act, er);
+    if (rc) return rc;
   }
   return run_head<T>(m, bt, ws, cv, s, tc ? &x_final : nullptr);
 }
@@ -326,14 +378,32 @@ int run_head(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv
   T* hidden = reinterpret_cast<T*>(ws + cv.hidden);
   T* xbuf = reinterpret_cast<T*>(ws + cv.xbuf);
   GemmScratch gscr{reinterpret_cast<int*>(ws + cv.gemm_counters), reinterpret_cast<float*>(ws + cv.gemm_parts)};
-  int rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(m.w.final_norm), rows_out, c.hidden, c.rms_eps, xbuf,
-                             bt.last_only ? bt.n_new : nullptr, bt.T, s, true);
-  if (rc) return rc;
   Epilogue eh = {};
   eh.op = EPI_STORE;
   eh.out_f32 = 1;
   eh.out = bt.logits;
   eh.ldo = c.vocab;
+  if (cv.gemv) {  // final norm (with the last-token selection) folded into the LM head
+    GemvArgs g = {};
+    g.w = static_cast<const __nv_bfloat16*>(m.w.lm_head);
+    g.x = reinterpret_cast<const __nv_bfloat16*>(hidden);
+    g.norm_w = static_cast<const __nv_bfloat16*>(m.w.final_norm);
+    g.sel_n_new = bt.last_only ? bt.n_new : nullptr;
+    g.T_tokens = bt.T;
+    g.eps = c.rms_eps;
+    g.M = rows_out;
+    g.N = c.vocab;
+    g.K = c.hidden;
+    g.p = cv.v_head;
+    g.e = eh;
+    g.status = bt.status;
+    g.trace = reinterpret_cast<unsigned long long*>(bt.trace);
+    g.trace_slot = 4 * c.n_layers;
+    return launch_gemv(g, s, true);
+  }
+  int rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(m.w.final_norm), rows_out, c.hidden, c.rms_eps, xbuf,
+                             bt.last_only ? bt.n_new : nullptr, bt.T, s, true);
+  if (rc) return rc;
   if (c.dtype == SPECB200_BF16) return launch_gemm_tc(cv.g_head, m.head, *x_final, eh, gscr, bt.status, s, true);
   return launch_gemm_simt<T>(cv.g_head, static_cast<const T*>(m.w.lm_head), xbuf, eh, gscr, bt.status, s, true);
 }
@@ -451,6 +521,15 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
     packed = L.p_qkv && L.p_o && L.p_gate_up && L.p_down;
   }
   m->chain_C = packed ? chain_cluster_size() : 0;
+  // Decode-step GEMV schedule: bf16 weights, 16-byte aligned rows (SPECB200_GEMV=0 turns it off).
+  auto al16 = [](const void* p) { return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  m->gemv_ok = c.dtype == SPECB200_BF16 && env_int("SPECB200_GEMV", 1) == 1 && al16(weights->lm_head) &&
+               al16(weights->final_norm) && gemv_prepare();
+  for (int l = 0; l < c.n_layers && m->gemv_ok; ++l) {
+    const specb200_layer_weights& L = weights->layers[l];
+    m->gemv_ok = al16(L.w_qkv) && al16(L.w_o) && al16(L.w_gate_up) && al16(L.w_down) && al16(L.attn_norm) &&
+                 al16(L.mlp_norm);
+  }
   if (c.dtype == SPECB200_BF16) {
     const int qd = c.n_heads * c.head_dim;
     m->maps.resize(c.n_layers);
@@ -472,7 +551,8 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
 }
 
 // Kernel launches of one forward call: 3 for the layer chain (chain kernel, final norm, LM head),
-// 1 for the layer stream, 3 + 7 L for the per-layer kernels (prep, 7 per layer, final norm, head).
+// 1 for the layer stream, 2 + 5 L for the GEMV schedule (prep, 5 per layer, head), 3 + 7 L for
+// the per-layer kernels (prep, 7 per layer, final norm, head).
 extern "C" int specb200_forward_launches(void* model, int B, int T) {
   if (!model || B <= 0 || T <= 0) return 0;
   const Model& m = *static_cast<Model*>(model);
@@ -482,6 +562,8 @@ extern "C" int specb200_forward_launches(void* model, int B, int T) {
   if (use_chain(m, B, T, ph, &splits, &L)) return 3;
   int grid = 0, mc = 0;
   if (use_stream(m, B, T, &grid, &mc)) return 1;
+  GemvPlan v[5];
+  if (use_gemv(m, B * T, B, &v[0], &v[1], &v[2], &v[3], &v[4])) return 2 + 5 * m.cfg.n_layers;
   return 3 + 7 * m.cfg.n_layers;
 }
 
@@ -493,7 +575,9 @@ extern "C" int specb200_forward_uses_stream(void* model, int B, int T) {
   ChainLayout L;
   if (use_chain(m, B, T, ph, &splits, &L)) return 2;
   int grid = 0, mc = 0;
-  return use_stream(m, B, T, &grid, &mc) ? 1 : 0;
+  if (use_stream(m, B, T, &grid, &mc)) return 1;
+  GemvPlan v[5];
+  return use_gemv(m, B * T, B, &v[0], &v[1], &v[2], &v[3], &v[4]) ? 3 : 0;
 }
 
 extern "C" int specb200_model_destroy(void* handle) {

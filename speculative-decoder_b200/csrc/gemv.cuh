@@ -40,8 +40,19 @@ struct GemvArgs {
   GemvPlan p;
   Epilogue e;
   int32_t* status;
+  // Optional launch record (globaltimer ns): CTA b of launch `trace_slot` writes
+  // trace[(trace_slot * kGemvTraceCtas + b) * kGemvTraceStamps + {0..7}] = entry, return from
+  // griddepcontrol.wait, inputs staged, first weight chunk landed, end, then the time spent
+  // waiting for weight chunks, the time in dot products, and the chunk count.
+  unsigned long long* trace;
+  int trace_slot;
 };
+constexpr int kGemvTraceCtas = 296;  // the largest grid plan_gemv makes
+constexpr int kGemvTraceStamps = 8;
 
 int launch_gemv(const GemvArgs& a, cudaStream_t stream, bool pdl);
+// Raises the kernels' dynamic shared-memory limit; call once outside any stream capture.
+// Returns false when the device refuses (then the schedule is not used).
+bool gemv_prepare();
 
 }  // namespace specb200

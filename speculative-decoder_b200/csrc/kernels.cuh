@@ -52,6 +52,11 @@ struct AttnArgs {
   float scale;
   void* out;            // [B*T, Hq, D]
   int32_t* status;
+  // Optional record of the tensor-core decode items (globaltimer ns): CTA c (linear block
+  // index, < 296) of launch `trace_slot` writes trace[(trace_slot * 296 + c) * 8 + {0..5}] =
+  // entry, wait return, keys landed, merged within the CTA, partial published, end.
+  unsigned long long* trace = nullptr;
+  int trace_slot = 0;
 };
 
 // Split-KV merge tickets: a fixed region at the start of the attention workspace (see the

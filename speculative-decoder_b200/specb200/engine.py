@@ -137,8 +137,10 @@ class Engine:
 
     def schedule(self, b: int, t: int) -> str:
         """The schedule a forward call of B rows x T tokens runs: "chain" (one thread-block
-        cluster), "stream" (persistent kernel over all SMs) or "layers" (a kernel per op)."""
-        return {2: "chain", 1: "stream"}.get(lib().specb200_forward_uses_stream(self.handle, b, t), "layers")
+        cluster), "stream" (persistent kernel over all SMs), "gemv" (decode steps of at most 4
+        token rows: a kernel per linear with the norms folded in) or "layers" (a kernel per op)."""
+        code = lib().specb200_forward_uses_stream(self.handle, b, t)
+        return {2: "chain", 1: "stream", 3: "gemv"}.get(code, "layers")
 
     def workspace_bytes(self, b: int, t: int, max_kv_len: int) -> int:
         return lib().specb200_forward_workspace_bytes(self.handle, b, t, max_kv_len)

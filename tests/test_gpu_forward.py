@@ -338,3 +338,81 @@ def test_chain_kernel_matches_oracle(monkeypatch):
         g, o = got[0, : n_new[0]], want[0, : n_new[0]]
         scale = np.abs(o).max()
         assert np.abs(g - o).max() <= 2e-2 * scale + 1e-3, (np.abs(g - o).max(), scale)
+
+
+def _gemv_steps(eng, model, prompt_len: int = 300):
+    """Prefill two sequences, then decode-sized calls (at most 4 token rows) of every shape the
+    GEMV schedule serves: 1 row x 1 token, 2 rows x 1 token (last rows), 2 rows x 2 tokens with
+    a ragged row, 1 row x 3 tokens. Returns their logits and the final KV pools."""
+    from cache.kv import KVCache
+
+    cache = KVCache.for_model(model.config, num_blocks=96, block_size=16, dtype=torch.bfloat16, device=DEV)
+    for s in range(2):
+        cache.add(s)
+        n = prompt_len - 37 * s
+        p = torch.randint(0, model.config.vocab_size, (1, n), generator=torch.Generator().manual_seed(50 + s))
+        eng.forward(cache, [s], p, [n], last_only=True)
+    outs = [eng.forward(cache, [0], torch.tensor([[11]]), [1], last_only=True),
+            eng.forward(cache, [0, 1], torch.tensor([[12], [13]]), [1, 1], last_only=True),
+            eng.forward(cache, [0, 1], torch.tensor([[14, 15], [16, 0]]), [2, 1]),
+            eng.forward(cache, [1], torch.tensor([[17, 18, 19]]), [3])]
+    return [x.float().cpu() for x in outs], cache
+
+
+@pytest.mark.parametrize("dims", [(576, 2, 9, 3, 1536, 49152), (2048, 2, 32, 32, 8192, 49152),
+                                  (128, 2, 4, 2, 256, 512)])
+def test_gemv_schedule_matches_per_layer_kernels(monkeypatch, dims):
+    """Decode-sized calls on the GEMV kernels (norms folded in, no split-K) against the
+    tensor-core per-layer kernels on identical inputs: the 135M draft and 1.7B widths and a
+    head_dim-32 model, 2 layers each. The two sum in different orders, so logits agree to bf16
+    noise (1e-2 of the logit scale, argmax equal except at near ties) and the KV entries the
+    calls wrote to one bf16 ulp of their scale."""
+    from specb200.engine import Engine
+
+    model = _bf16_model(*dims, seed=8, theta=100000.0).to(DEV)
+    monkeypatch.setenv("SPECB200_GEMV", "0")
+    per_layer = Engine(model)
+    monkeypatch.delenv("SPECB200_GEMV")
+    gemv = Engine(model)
+    assert per_layer.schedule(1, 1) == "layers" and per_layer.schedule(2, 2) == "layers"
+    assert gemv.schedule(1, 1) == "gemv" and gemv.schedule(2, 2) == "gemv" and gemv.schedule(1, 3) == "gemv"
+    assert gemv.schedule(1, 5) == "layers" and gemv.launches(1, 1) == 2 + 5 * 2
+    (la, ca), (lb, cb) = _gemv_steps(per_layer, model), _gemv_steps(gemv, model)
+    for a, b in zip(la, lb):
+        scale = a.abs().max().item()
+        assert (a - b).abs().max().item() <= 1e-2 * scale, ((a - b).abs().max().item(), scale)
+        top2 = a.topk(2, dim=-1).values
+        agree = a.argmax(-1) == b.argmax(-1)
+        assert bool((agree | ((top2[..., 0] - top2[..., 1]) < 1e-2 * scale)).all())
+    for pa, pb in ((ca.k, cb.k), (ca.v, cb.v)):
+        d = (pa.float() - pb.float()).abs().max().item()
+        assert d <= 2 ** -7 * pa.float().abs().max().item(), d
+
+
+@pytest.mark.parametrize("dims", [(576, 2, 9, 3, 1536, 49152), (128, 2, 4, 2, 256, 512)])
+def test_gemv_schedule_matches_oracle(dims):
+    """The GEMV schedule against the bf16 oracle: after a prefill, 1-token steps of one and of
+    two sequences and a 3-token step, logits within rtol 2e-2 of the largest logit."""
+    from lm.forward import forward
+    from specb200.engine import engine_for
+
+    model = _bf16_model(*dims, seed=13, theta=100000.0)
+    w = ofw.weights_from_model(model)
+    prec = ofw.Precision("bf16")
+    model = model.to(DEV)
+    assert engine_for(model).schedule(1, 1) == "gemv"
+    cache = new_cache(model, block_size=16)
+    ocache = ofw.Cache(w, 4096, 16, prec)
+    for s in range(2):
+        cache.add(s)
+        ocache.add(s)
+    prompts = [torch.randint(0, dims[-1], (1, n), generator=torch.Generator().manual_seed(n)).numpy() for n in (70, 33)]
+    steps = [([0], prompts[0], [70]), ([1], prompts[1], [33]), ([0], np.array([[6]]), [1]),
+             ([0, 1], np.array([[7], [8]]), [1, 1]), ([1], np.array([[9, 10, 11]]), [3])]
+    for seqs, ids_np, n_new in steps:
+        got = forward(model, cache, seqs, torch.from_numpy(ids_np), n_new).float().cpu().numpy()
+        want = ofw.forward(w, ocache, seqs, ids_np, n_new, prec)
+        for b, n in enumerate(n_new):
+            g, o = got[b, :n], want[b, :n]
+            scale = np.abs(o).max()
+            assert np.abs(g - o).max() <= 2e-2 * scale + 1e-3, (b, np.abs(g - o).max(), scale)
