@@ -15,8 +15,11 @@
 // merges the partial results in split order, which keeps the output independent of CTA
 // scheduling; there is no spin-wait.
 #include <algorithm>
+#include <cstdlib>
+#include <mutex>
 #include <type_traits>
 
+#include "attn_cluster.cuh"
 #include "attn_core.cuh"
 #include "attn_item_mma.cuh"
 
@@ -39,6 +42,42 @@ __global__ void __launch_bounds__(kAttnThreads) attention_mma_kernel(AttnKernelA
   attention_item_mma(ka, blockIdx.z, blockIdx.y, blockIdx.x, smem, true);
 }
 
+// Decode / verify shapes whose keys fit one cluster: one cluster of C CTAs per (kv head,
+// sequence); loads the cached keys before waiting on the previous kernel.
+__global__ void __launch_bounds__(kAcThreads) attention_cluster_kernel(AttnKernelArgs ka) {
+  extern __shared__ __align__(16) uint8_t ac_smem[];
+  pdl_launch_dependents();
+  attention_cluster_cta(ka, blockIdx.z, blockIdx.y, ac_smem, true);
+}
+
+constexpr int kAcSmemLimit = 200 * 1024;
+
+cudaError_t launch_cluster(const AttnArgs& a, const AttnPlan& p, cudaStream_t s, bool pdl) {
+  AttnKernelArgs ka;
+  ka.a = a;
+  ka.p = p;
+  ka.counters = nullptr;
+  ka.part = nullptr;
+  const int R = a.T * (a.Hq / a.Hkv);
+  const AcLayout lay = ac_layout(p.chunk, R, p.splits_max, a.bs);
+  if (lay.total > kAcSmemLimit) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.splits_max, a.Hkv, a.B);
+  cfg.blockDim = dim3(kAcThreads);
+  cfg.dynamicSmemBytes = lay.total;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.splits_max;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, attention_cluster_kernel, ka);
+}
+
 template <typename T, int D>
 cudaError_t launch_d(const AttnArgs& a, const AttnPlan& p, int* counters, float* partials, cudaStream_t s, bool pdl) {
   AttnKernelArgs ka;
@@ -52,7 +91,26 @@ cudaError_t launch_d(const AttnArgs& a, const AttnPlan& p, int* counters, float*
 
 }  // namespace
 
+bool attention_prepare() {
+  static std::once_flag once;
+  static bool ok = false;
+  std::call_once(once, [] {
+    ok = cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAcSmemLimit) ==
+         cudaSuccess;
+  });
+  return ok;
+}
+
 AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len, bool tensor_items) {
+  static const bool cluster_on = [] {
+    const char* v = std::getenv("SPECB200_ATTN_CLUSTER");
+    return !(v && *v == '0');
+  }();
+  if (tensor_items && T * (Hq / Hkv) <= kAmRows && cluster_on && attention_prepare()) {
+    AttnPlan p;
+    if (plan_attention_cluster(max_kv_len, &p) && ac_layout(p.chunk, T * (Hq / Hkv), p.splits_max, 1).total <= kAcSmemLimit)
+      return p;
+  }
   if (tensor_items && T * (Hq / Hkv) <= kAmRows) {
     AttnPlan p = plan_attention_mma(B, Hkv, max_kv_len);
     p.mma = 1;
@@ -72,6 +130,7 @@ AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len, bool tens
 }
 
 size_t attention_partials_bytes(const AttnPlan& p, int B, int Hkv, int D) {
+  if (p.mma == 2) return 0;  // the cluster kernel merges in distributed shared memory
   const size_t groups = static_cast<size_t>(B) * Hkv * p.qtiles;
   return p.splits_max > 1 ? groups * p.splits_max * kRows * (D + 2) * sizeof(float) : 0;
 }
@@ -83,6 +142,12 @@ size_t attention_workspace_bytes(const AttnPlan& p, int B, int Hkv, int D) {
 template <typename T>
 int launch_attention(const AttnArgs& a, const AttnPlan& p, int* counters, float* partials, cudaStream_t s, bool pdl) {
   cudaError_t e;
+  if (p.mma == 2) {
+    if (!std::is_same<T, __nv_bfloat16>::value || a.D != 64 || a.T * (a.Hq / a.Hkv) > kAcRowsMax)
+      return SPECB200_ERR_UNSUPPORTED;
+    e = launch_cluster(a, p, s, pdl);
+    return e == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
+  }
   if (p.mma) {
     if (!std::is_same<T, __nv_bfloat16>::value || a.D != 64 || a.T * (a.Hq / a.Hkv) > kAmRows)
       return SPECB200_ERR_UNSUPPORTED;

@@ -521,6 +521,7 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
     packed = L.p_qkv && L.p_o && L.p_gate_up && L.p_down;
   }
   m->chain_C = packed ? chain_cluster_size() : 0;
+  attention_prepare();  // function attributes are set here, outside any stream capture
   // Decode-step GEMV schedule: bf16 weights, 16-byte aligned rows (SPECB200_GEMV=0 turns it off).
   auto al16 = [](const void* p) { return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   m->gemv_ok = c.dtype == SPECB200_BF16 && env_int("SPECB200_GEMV", 1) == 1 && al16(weights->lm_head) &&

@@ -268,17 +268,21 @@ def test_linear_fp32_matches_torch(m, n, k):
 
 
 # ---------------------------------------------------------------- paged attention (K4)
-@pytest.mark.parametrize("dtype,hq,hkv,d,T,bs", [(torch.float32, 4, 2, 16, 5, 4), (torch.bfloat16, 32, 32, 64, 5, 16),
-                                                 (torch.bfloat16, 9, 3, 64, 2, 16), (torch.float32, 4, 4, 32, 40, 3),
-                                                 (torch.bfloat16, 9, 3, 64, 1, 16), (torch.bfloat16, 9, 3, 64, 5, 16),
-                                                 (torch.bfloat16, 12, 3, 64, 4, 32), (torch.bfloat16, 32, 4, 64, 3, 16)])
-def test_attention_matches_dense_reference(dtype, hq, hkv, d, T, bs):
+@pytest.mark.parametrize("dtype,hq,hkv,d,T,bs,long_past", [
+    (torch.float32, 4, 2, 16, 5, 4, 700), (torch.bfloat16, 32, 32, 64, 5, 16, 700),
+    (torch.bfloat16, 9, 3, 64, 2, 16, 700), (torch.float32, 4, 4, 32, 40, 3, 700),
+    (torch.bfloat16, 9, 3, 64, 1, 16, 700), (torch.bfloat16, 9, 3, 64, 5, 16, 700),
+    (torch.bfloat16, 12, 3, 64, 4, 32, 700), (torch.bfloat16, 32, 4, 64, 3, 16, 700),
+    (torch.bfloat16, 9, 3, 64, 1, 16, 4500), (torch.bfloat16, 4, 2, 64, 4, 1, 130)])
+def test_attention_matches_dense_reference(dtype, hq, hkv, d, T, bs, long_past):
     """Paged attention over shuffled blocks vs the reference's mask (lm/forward.py:44-49) on
-    a dense fp32 copy: rows of lengths 1..700 incl. a padded row. bf16 shapes with at most 16
-    query rows per KV head (T x G) run the tensor-core items (1, 6, 15 and 16 rows here); 24
-    rows (32 / 4 heads, T = 3) and the fp32 cases run the fp32 items."""
+    a dense fp32 copy: rows of lengths 1 .. long_past incl. a padded row. bf16 shapes with at
+    most 16 query rows per KV head (T x G) run the cluster kernel (1, 6, 8, 15 and 16 rows
+    here; C = 2 .. 6 CTAs per cluster, block size 1 included) or, when the keys exceed one
+    cluster (4500 cached), the tensor-core split items; 24 rows (32 / 4 heads, T = 3) and
+    the fp32 cases run the fp32 items."""
     g = torch.Generator().manual_seed(hq + T)
-    lens_past = [0, 37, 700]
+    lens_past = [0, 37, long_past]
     n_new = [T, max(1, T - 2), T]
     B = len(lens_past)
     total = [p + n for p, n in zip(lens_past, n_new)]
