@@ -290,6 +290,9 @@ def gemv_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
     per = []
     for i in range(n):
         ok = t[i, :, 0] > 0
+        if not bool(ok.any()):  # a launch that wrote no record
+            per.append(None)
+            continue
         ti = t[i][ok] / 1e3
         r0 = float(ti[:, 1].min())
         per.append({"n": int(ok.sum()), "r0": r0, "end": float(ti[:, 4].max()),
@@ -299,10 +302,14 @@ def gemv_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
                     "endo": (float((ti[:, 4] - r0).median()), float((ti[:, 4] - r0).max())),
                     "wait": (float(ti[:, 5].median()), float(ti[:, 5].max())),
                     "dot": (float(ti[:, 6].median()), float(ti[:, 6].max()))})
+    if per[0] is None or per[-1] is None:
+        return {}
     out = {"total_us": round(per[-1]["end"] - per[0]["r0"], 1)}
     med = lambda v: round(statistics.median(v), 2)  # noqa: E731
     for j, name in enumerate(["qkv", "o", "gate_up", "down", "head"]):
         rows = [n - 1] if name == "head" else [4 * l + j for l in range(n_layers)]
+        if any(per[i] is None or (i > 0 and per[i - 1] is None) for i in rows):
+            continue
         d = {"ctas": per[rows[0]]["n"], "late": med([per[i]["late"] for i in rows])}
         gaps = [per[i]["r0"] - per[i - 1]["end"] for i in rows if i > 0]
         d["gap"] = med(gaps) if gaps else None

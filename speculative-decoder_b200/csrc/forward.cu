@@ -86,21 +86,28 @@ struct Carve {
   ChainLayout cl;
   GemmShape g_qkv, g_o, g_gu, g_down, g_head;
   bool gemv;  // decode-step schedule: the per-layer order with GEMV kernels and fused norms
+  bool gemv_head;  // ... and the LM head as a GEMV with the final norm folded in
   GemvPlan v_qkv, v_o, v_gu, v_down, v_head;
   AttnPlan ap;
 };
 
-// Whether a call of this shape runs the decode-step GEMV schedule (at most kGemvMaxRows token
-// rows, bf16); fills the five plans.
+// Whether a call of this shape runs the decode-step GEMV schedule: at most kGemvMaxRows token
+// rows of a bf16 model whose every layer linear has its weights on chip at once (one chunk per
+// CTA, at most two CTAs per SM). Fills the four layer plans and, in *head, the LM head's; the
+// head runs as a GEMV (final norm folded in) only when *head_gemv, else as RMSNorm + the
+// tensor-core GEMM, which streams a large vocabulary faster than the CUDA-core dot products.
 bool use_gemv(const Model& m, int M, int rows_out, GemvPlan* qkv, GemvPlan* o, GemvPlan* gu, GemvPlan* down,
-              GemvPlan* head) {
+              GemvPlan* head, bool* head_gemv) {
   const specb200_model_config& c = m.cfg;
   if (!m.gemv_ok || M > kGemvMaxRows) return false;
   const int qd = c.n_heads * c.head_dim;
-  return plan_gemv(EPI_QKV, M, m.qkv_n, c.hidden, c.head_dim, qkv) && plan_gemv(EPI_RESID, M, c.hidden, qd, 0, o) &&
-         plan_gemv(EPI_SILU_MUL, M, 2 * c.intermediate, c.hidden, 0, gu) &&
-         plan_gemv(EPI_RESID, M, c.hidden, c.intermediate, 0, down) &&
-         plan_gemv(EPI_STORE, rows_out, c.vocab, c.hidden, 0, head);
+  const bool ok = plan_gemv(EPI_QKV, M, m.qkv_n, c.hidden, c.head_dim, qkv) && plan_gemv(EPI_RESID, M, c.hidden, qd, 0, o) &&
+                  plan_gemv(EPI_SILU_MUL, M, 2 * c.intermediate, c.hidden, 0, gu) &&
+                  plan_gemv(EPI_RESID, M, c.hidden, c.intermediate, 0, down);
+  if (!ok || qkv->stages > 1 || o->stages > 1 || gu->stages > 1 || down->stages > 1) return false;
+  static const int head_mode = env_int("SPECB200_GEMV_HEAD", 0);  // 1: GEMV head even when it streams
+  *head_gemv = plan_gemv(EPI_STORE, rows_out, c.vocab, c.hidden, 0, head) && (head->stages == 1 || head_mode == 1);
+  return true;
 }
 
 Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
@@ -118,7 +125,9 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   r.g_head = plan_gemm(rows_out, c.vocab, c.hidden, tc);
   r.chain = use_chain(m, B, T, r.cph, &r.csplits, &r.cl);
   r.stream = !r.chain && use_stream(m, B, T, &r.grid, &r.max_contrib);
-  r.gemv = !r.chain && !r.stream && use_gemv(m, M, rows_out, &r.v_qkv, &r.v_o, &r.v_gu, &r.v_down, &r.v_head);
+  r.gemv_head = false;
+  r.gemv = !r.chain && !r.stream &&
+           use_gemv(m, M, rows_out, &r.v_qkv, &r.v_o, &r.v_gu, &r.v_down, &r.v_head, &r.gemv_head);
   r.ap = r.stream ? plan_attention_decode(B, c.n_kv_heads, max_kv_len, r.grid)
                   : plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len, tc && c.head_dim == 64);
   // The two ticket-counter regions sit at fixed offsets so that they stay zero across calls
@@ -383,7 +392,7 @@ int run_head(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv
   eh.out_f32 = 1;
   eh.out = bt.logits;
   eh.ldo = c.vocab;
-  if (cv.gemv) {  // final norm (with the last-token selection) folded into the LM head
+  if (cv.gemv_head) {  // final norm (with the last-token selection) folded into the LM head
     GemvArgs g = {};
     g.w = static_cast<const __nv_bfloat16*>(m.w.lm_head);
     g.x = reinterpret_cast<const __nv_bfloat16*>(hidden);
@@ -564,7 +573,9 @@ extern "C" int specb200_forward_launches(void* model, int B, int T) {
   int grid = 0, mc = 0;
   if (use_stream(m, B, T, &grid, &mc)) return 1;
   GemvPlan v[5];
-  if (use_gemv(m, B * T, B, &v[0], &v[1], &v[2], &v[3], &v[4])) return 2 + 5 * m.cfg.n_layers;
+  bool head_gemv = false;
+  if (use_gemv(m, B * T, B, &v[0], &v[1], &v[2], &v[3], &v[4], &head_gemv))
+    return (head_gemv ? 2 : 3) + 5 * m.cfg.n_layers;
   return 3 + 7 * m.cfg.n_layers;
 }
 
@@ -578,7 +589,8 @@ extern "C" int specb200_forward_uses_stream(void* model, int B, int T) {
   int grid = 0, mc = 0;
   if (use_stream(m, B, T, &grid, &mc)) return 1;
   GemvPlan v[5];
-  return use_gemv(m, B * T, B, &v[0], &v[1], &v[2], &v[3], &v[4]) ? 3 : 0;
+  bool head_gemv = false;
+  return use_gemv(m, B * T, B, &v[0], &v[1], &v[2], &v[3], &v[4], &head_gemv) ? 3 : 0;
 }
 
 extern "C" int specb200_model_destroy(void* handle) {

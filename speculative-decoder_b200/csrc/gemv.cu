@@ -97,8 +97,9 @@ SPECB200_DEVINL void issue_chunk(const GemvArgs& a, int c, uint8_t* stage, uint6
 
 // Input rows into shared memory as bf16 [MR][K] (rows >= M zero), RMS-normalised when a norm
 // weight is given: y = round(w * round(x * rsqrt(mean(x^2) + eps))), as rmsnorm_kernel.
-template <int MR>
-SPECB200_DEVINL void stage_x(const GemvArgs& a, const uint4 (&nw)[kGvXChunks], __nv_bfloat16* xs, float (*red)[MR]) {
+template <int MR, typename Sync>
+SPECB200_DEVINL void stage_x(const GemvArgs& a, const uint4 (&nw)[kGvXChunks], __nv_bfloat16* xs, float (*red)[MR],
+                             Sync sync) {
   const int K = a.K, nch = K >> 3, tid = threadIdx.x;
   const bool norm = a.norm_w != nullptr;
   uint4 xv[kGvXChunks][MR];
@@ -131,7 +132,7 @@ SPECB200_DEVINL void stage_x(const GemvArgs& a, const uint4 (&nw)[kGvXChunks], _
       ss[m] = warp_sum(ss[m]);
       if ((tid & 31) == 0) red[tid >> 5][m] = ss[m];
     }
-    __syncthreads();
+    sync();
 #pragma unroll
     for (int m = 0; m < MR; ++m) {
       float t = 0.f;
@@ -292,65 +293,71 @@ SPECB200_DEVINL float part_sum(const float* part, int ks, int r, int m) {
   return v;
 }
 
-template <int MR>
-SPECB200_DEVINL void epilogue(const GemvArgs& a, const Chunk& k, const float* part, bool have_pre, const Pre& pre) {
+// The fused epilogue for output feature j of chunk k and token m: `lo` is the dot product of
+// the feature's (first) weight row, `hi` that of its second row (gate/up and rotary pairs).
+SPECB200_DEVINL void apply_one(const GemvArgs& a, const Chunk& k, int j, int m, float lo, float hi, const Pre& q) {
   using T = __nv_bfloat16;
   const Epilogue& e = a.e;
+  switch (e.op) {
+    case EPI_STORE: {
+      const int64_t o = static_cast<int64_t>(m) * e.ldo + k.f0 + j;
+      if (e.out_f32) static_cast<float*>(e.out)[o] = lo;
+      else static_cast<T*>(e.out)[o] = from_f32<T>(lo);
+      break;
+    }
+    case EPI_RESID: {
+      const float proj = round_to<T>(lo);
+      static_cast<T*>(e.out)[static_cast<int64_t>(m) * e.ldo + k.f0 + j] = from_f32<T>(q.h + proj);
+      break;
+    }
+    case EPI_SILU_MUL: {
+      const float g = round_to<T>(lo);
+      const float u = round_to<T>(hi);
+      const float act = round_to<T>(g / (1.0f + expf(-g)));
+      static_cast<T*>(e.out)[static_cast<int64_t>(m) * e.ldo + k.f0 + j] = from_f32<T>(act * u);
+      break;
+    }
+    case EPI_QKV: {
+      const int d = e.head_dim, half = d / 2;
+      const int qd = e.n_heads * d, kd = e.n_kv_heads * d;
+      const int n = k.row0 + j;  // the pair's low row; its partner is n + half
+      const int region = n < qd ? 0 : (n < qd + kd ? 1 : 2);
+      lo = round_to<T>(lo);
+      hi = round_to<T>(hi);
+      if (region < 2) {
+        const float lo2 = round_to<T>(round_to<T>(lo * q.c) + round_to<T>(-hi * q.s));
+        const float hi2 = round_to<T>(round_to<T>(hi * q.c) + round_to<T>(lo * q.s));
+        lo = lo2;
+        hi = hi2;
+      }
+      if (region == 0) {
+        T* out = static_cast<T*>(e.out) + static_cast<int64_t>(m) * e.ldo;
+        out[n] = from_f32<T>(lo);
+        out[n + half] = from_f32<T>(hi);
+      } else if (q.slot >= 0) {
+        const int idx = n - (region == 1 ? qd : qd + kd);
+        const int hh = idx / d, i = idx % d;
+        T* pool = static_cast<T*>(region == 1 ? e.k_pool : e.v_pool) + (static_cast<int64_t>(q.slot) * e.n_kv_heads + hh) * d;
+        pool[i] = from_f32<T>(lo);
+        pool[i + half] = from_f32<T>(hi);
+      }
+      break;
+    }
+    default:
+      break;
+  }
+}
+
+template <int MR>
+SPECB200_DEVINL void epilogue(const GemvArgs& a, const Chunk& k, const float* part, bool have_pre, const Pre& pre) {
   const int ks = a.p.ksplit, nf = k.nf;
   for (int t = threadIdx.x; t < nf * MR; t += kGvThreads) {
     const int j = t % nf, m = t / nf;
     if (m >= a.M) continue;
     const Pre q = (have_pre && t == static_cast<int>(threadIdx.x)) ? pre : load_pre(a, k, j, m);
-    switch (e.op) {
-      case EPI_STORE: {
-        const float v = part_sum<MR>(part, ks, j, m);
-        const int64_t o = static_cast<int64_t>(m) * e.ldo + k.f0 + j;
-        if (e.out_f32) static_cast<float*>(e.out)[o] = v;
-        else static_cast<T*>(e.out)[o] = from_f32<T>(v);
-        break;
-      }
-      case EPI_RESID: {
-        const float proj = round_to<T>(part_sum<MR>(part, ks, j, m));
-        static_cast<T*>(e.out)[static_cast<int64_t>(m) * e.ldo + k.f0 + j] = from_f32<T>(q.h + proj);
-        break;
-      }
-      case EPI_SILU_MUL: {
-        const float g = round_to<T>(part_sum<MR>(part, ks, j, m));
-        const float u = round_to<T>(part_sum<MR>(part, ks, nf + j, m));
-        const float act = round_to<T>(g / (1.0f + expf(-g)));
-        static_cast<T*>(e.out)[static_cast<int64_t>(m) * e.ldo + k.f0 + j] = from_f32<T>(act * u);
-        break;
-      }
-      case EPI_QKV: {
-        const int d = e.head_dim, half = d / 2;
-        const int qd = e.n_heads * d, kd = e.n_kv_heads * d;
-        const int n = k.row0 + j;  // the pair's low row; its partner is n + half
-        const int region = n < qd ? 0 : (n < qd + kd ? 1 : 2);
-        float lo = round_to<T>(part_sum<MR>(part, ks, j, m));
-        float hi = round_to<T>(part_sum<MR>(part, ks, nf + j, m));
-        if (region < 2) {
-          const float lo2 = round_to<T>(round_to<T>(lo * q.c) + round_to<T>(-hi * q.s));
-          const float hi2 = round_to<T>(round_to<T>(hi * q.c) + round_to<T>(lo * q.s));
-          lo = lo2;
-          hi = hi2;
-        }
-        if (region == 0) {
-          T* out = static_cast<T*>(e.out) + static_cast<int64_t>(m) * e.ldo;
-          out[n] = from_f32<T>(lo);
-          out[n + half] = from_f32<T>(hi);
-        } else if (q.slot >= 0) {
-          const int idx = n - (region == 1 ? qd : qd + kd);
-          const int hh = idx / d, i = idx % d;
-          T* pool = static_cast<T*>(region == 1 ? e.k_pool : e.v_pool) +
-                    (static_cast<int64_t>(q.slot) * e.n_kv_heads + hh) * d;
-          pool[i] = from_f32<T>(lo);
-          pool[i + half] = from_f32<T>(hi);
-        }
-        break;
-      }
-      default:
-        break;
-    }
+    const float lo = part_sum<MR>(part, ks, j, m);
+    const float hi = a.p.segs == 2 ? part_sum<MR>(part, ks, nf + j, m) : 0.f;
+    apply_one(a, k, j, m, lo, hi, q);
   }
 }
 
@@ -404,7 +411,7 @@ __global__ void __launch_bounds__(kGvThreads) gemv_kernel(const __grid_constant_
       have_pre = true;
     }
   }
-  stage_x<MR>(a, nw, xs, red);
+  stage_x<MR>(a, nw, xs, red, [] { __syncthreads(); });
   __syncthreads();
   if (tr && tid == 0) tr[2] = gv_now();
 
