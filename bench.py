@@ -302,9 +302,10 @@ def gemv_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
                     "endo": (float((ti[:, 4] - r0).median()), float((ti[:, 4] - r0).max())),
                     "wait": (float(ti[:, 5].median()), float(ti[:, 5].max())),
                     "dot": (float(ti[:, 6].median()), float(ti[:, 6].max()))})
-    if per[0] is None or per[-1] is None:
+    done = [x for x in per if x is not None]
+    if per[0] is None:
         return {}
-    out = {"total_us": round(per[-1]["end"] - per[0]["r0"], 1)}
+    out = {"total_us": round(done[-1]["end"] - per[0]["r0"], 1)}
     med = lambda v: round(statistics.median(v), 2)  # noqa: E731
     for j, name in enumerate(["qkv", "o", "gate_up", "down", "head"]):
         rows = [n - 1] if name == "head" else [4 * l + j for l in range(n_layers)]
@@ -338,9 +339,11 @@ def gemv_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
     return out
 
 
-def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30, trace: bool = False) -> dict:
-    """One single-token draft-model forward (135M architecture, B=1), CUDA graph, as in each
-    of the k draft steps of a round."""
+def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30, trace: bool = False,
+                    tokens: int = 1) -> dict:
+    """One draft-model forward (135M architecture, B=1) of `tokens` new tokens, CUDA graph: 1 as
+    in draft steps 1..k-1 of a round, 2 as in step 0 (the token the previous round emitted and
+    the one before it when the draft lags)."""
     from specb200.engine import engine_for
 
     eng = engine_for(draft)
@@ -352,12 +355,12 @@ def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30, 
     table = torch.zeros(1, -(-cap // BLOCK), dtype=torch.int32, device=device)
     blocks = cache.tables[0].blocks
     table[0, : len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
-    ids = torch.randint(0, DRAFT["vocab_size"], (1, 1), dtype=torch.int32, device=device)
-    one = torch.ones(1, dtype=torch.int32, device=device)
-    pastt = torch.tensor([context_len - 1], dtype=torch.int32, device=device)
+    ids = torch.randint(0, DRAFT["vocab_size"], (1, tokens), dtype=torch.int32, device=device)
+    one = torch.full((1,), tokens, dtype=torch.int32, device=device)
+    pastt = torch.tensor([context_len - tokens], dtype=torch.int32, device=device)
     logits = torch.empty(1, DRAFT["vocab_size"], dtype=torch.float32, device=device)
     status = torch.zeros(1, dtype=torch.int32, device=device)
-    ws = torch.zeros(eng.workspace_bytes(1, 1, cap), dtype=torch.uint8, device=device)
+    ws = torch.zeros(eng.workspace_bytes(1, tokens, cap), dtype=torch.uint8, device=device)
     run = lambda: eng.forward_device(cache, ids, one, pastt, table, cap, True, logits, status, ws)  # noqa: E731
     run()
     torch.cuda.synchronize()
@@ -471,6 +474,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--layers", type=int, default=0,
                     help="with --only: build the models with this many layers (smaller profiling runs)")
+    ap.add_argument("--draft-tokens", type=int, default=1,
+                    help="with --only draft: new tokens per draft forward (2 = a round's first step)")
     ap.add_argument("--trace", action="store_true",
                     help="with --only verify/draft: per-phase timings of the layer-stream kernel")
     ap.add_argument("--only", choices=["verify", "accept", "draft"],
@@ -523,7 +528,7 @@ def main() -> None:
         else:
             spec = dict(DRAFT, num_hidden_layers=args.layers or DRAFT["num_hidden_layers"])
             r = time_draft_step(make_model(spec, 1, device), KVCache, device, PROMPT_LEN + NEW_TOKENS // 2,
-                                reps=max(1, args.steps), trace=args.trace)
+                                reps=max(1, args.steps), trace=args.trace, tokens=args.draft_tokens)
         r["gbs"] = r["bytes"] / (r["us"] * 1e-6) / 1e9
         r["frac"] = r["gbs"] / pk["hbm_gbs"]
         print(json.dumps({"only": args.only, **r}))

@@ -55,26 +55,46 @@ struct AcceptArgs {
   int* nsel;       // [B] accepted length n (the residual row)
   double* chunk_sums;  // [B, C]
   int C, chunk;        // residual chunks per sequence and their length (a multiple of 4 * kAcceptThreads)
+  // Statistics of a row in nrc column chunks of rclen elements (few rows: small batches and the
+  // draft sampler), combined in chunk order by the row's last CTA (ticket in rcounters).
+  int nrc, rclen;
+  RowStat* cstats;  // [B, R, nrc]
+  int* rcounters;   // [B, R]
 };
 
 // Workspace carve, shared by the caller-workspace and the allocation-free entry points.
 struct AcceptLayout {
-  size_t counters, stats, nsel, sums, total;
+  size_t counters, stats, nsel, sums, cstats, total;
 };
-inline int residual_chunks(int V) {
+// Statistics CTAs aimed for when rows are few (one wave at 4 per SM); rows are split into at
+// most kMaxRowChunks column chunks of at least kMinRowChunk elements.
+constexpr int kStatCtas = 4 * 148;
+constexpr int kMinRowChunk = 2048;
+constexpr int kMaxRowChunks = 64;
+inline int row_chunks(int rows, int V, bool logits) {
+  if (!logits || 2 * rows >= kStatCtas) return 1;
+  int n = kStatCtas / rows;
+  const int by_len = V / kMinRowChunk;
+  n = n < by_len ? n : by_len;
+  n = n < kMaxRowChunks ? n : kMaxRowChunks;
+  return n < 1 ? 1 : n;
+}
+constexpr int residual_chunks(int V) {
   const int per = 4 * kAcceptThreads;
   const int blocks = (V + per - 1) / per;
   return blocks < 16 ? blocks : 16;
 }
-inline AcceptLayout accept_layout(int B, int k, int V) {
+constexpr AcceptLayout accept_layout(int B, int k, int V) {
   auto al = [](size_t x) { return (x + 255) / 256 * 256; };
   const size_t R = 2 * static_cast<size_t>(k) + 1;
-  AcceptLayout l;
+  AcceptLayout l{};
+  // sequence tickets [2B], then the row tickets [B R] of chunked rows (B R < kStatCtas / 2)
   l.counters = 256;
-  l.stats = l.counters + al(2 * static_cast<size_t>(B) * sizeof(int));
+  l.stats = l.counters + al((2 * static_cast<size_t>(B) + kStatCtas / 2) * sizeof(int));
   l.nsel = l.stats + al(static_cast<size_t>(B) * R * sizeof(RowStat));
   l.sums = l.nsel + al(static_cast<size_t>(B) * sizeof(int));
-  l.total = l.sums + al(static_cast<size_t>(B) * residual_chunks(V) * sizeof(double));
+  l.cstats = l.sums + al(static_cast<size_t>(B) * residual_chunks(V) * sizeof(double));
+  l.total = l.cstats + al(static_cast<size_t>(kStatCtas) * sizeof(RowStat));  // B R nrc <= kStatCtas
   return l;
 }
 
@@ -94,7 +114,10 @@ SPECB200_DEVINL void combine_ms(float& m, float& s, float m2, float s2) {
   m = mx;
 }
 
-__device__ void row_statistics(const AcceptArgs& a, int b, int r, RowStat* out) {
+// Statistics of row r of sequence b over columns [x0, x1) (x0 % 4 == 0; the whole row when
+// the row is not chunked); thread 0 writes them to *out. With `finish`, also the value at the
+// drafted token (only the CTA that sees the whole row, or the row's combining CTA, needs it).
+__device__ void row_statistics(const AcceptArgs& a, int b, int r, int x0, int x1, bool finish, RowStat* out) {
   __shared__ float sh_m[kAcceptWarps], sh_s[kAcceptWarps];
   __shared__ int sh_i[kAcceptWarps];
   const float* row = row_ptr(a, b, r);
@@ -118,9 +141,9 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, RowStat* out) 
     int bi = 0x7fffffff;
     if (vec) {
       const float4* r4 = reinterpret_cast<const float4*>(row);
-      const int n4 = a.V / 4;
+      const int n4 = x1 / 4;
 #pragma unroll 8
-      for (int j = tid; j < n4; j += kAcceptThreads) {
+      for (int j = x0 / 4 + tid; j < n4; j += kAcceptThreads) {
         const float4 v = __ldg(r4 + j);
         const float gm = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
         const bool nan = (v.x != v.x) || (v.y != v.y) || (v.z != v.z) || (v.w != v.w);
@@ -132,14 +155,14 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, RowStat* out) 
         }
       }
     } else {
-      for (int j = tid; j < a.V; j += kAcceptThreads) argmax_merge(best, bi, __ldg(row + j), j);
+      for (int j = x0 + tid; j < x1; j += kAcceptThreads) argmax_merge(best, bi, __ldg(row + j), j);
     }
     warp_argmax(best, bi);
     if (lane == 0) { sh_m[warp] = best; sh_i[warp] = bi; }
     __syncthreads();
     if (tid == 0) {
       for (int w = 1; w < kAcceptWarps; ++w) argmax_merge(best, bi, sh_m[w], sh_i[w]);
-      RowStat st{best, 1.f, 0.f, bi == 0x7fffffff ? 0 : bi};
+      RowStat st{best, 1.f, 0.f, (bi == 0x7fffffff && finish) ? 0 : bi};  // chunk partials keep "none"
       *out = st;
     }
     return;
@@ -153,9 +176,9 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, RowStat* out) 
   float m = -INFINITY, s = 0.f;
   if (vec) {
     const float4* r4 = reinterpret_cast<const float4*>(row);
-    const int n4 = a.V / 4;
+    const int n4 = x1 / 4;
     constexpr int kU = 8;  // 8 float4 per thread in flight: 32 KB per CTA, 128 KB per SM
-    for (int j0 = tid; j0 < n4; j0 += kU * kAcceptThreads) {
+    for (int j0 = x0 / 4 + tid; j0 < n4; j0 += kU * kAcceptThreads) {
       float z[kU * 4];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
@@ -178,7 +201,7 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, RowStat* out) 
       }
     }
   } else {
-    for (int j = tid; j < a.V; j += kAcceptThreads) {
+    for (int j = x0 + tid; j < x1; j += kAcceptThreads) {
       float z = __ldg(row + j);
       if (!unit_t) z = z / T;
       float mx = fmaxf(z, m);
@@ -199,7 +222,7 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, RowStat* out) 
   if (tid == 0) {
     for (int w = 1; w < kAcceptWarps; ++w) combine_ms(m, s, sh_m[w], sh_s[w]);
     RowStat st{m, s, 0.f, 0};
-    if (d >= 0 && d < a.V) st.zx = row[d] / T;
+    if (finish && d >= 0 && d < a.V) st.zx = row[d] / T;
     *out = st;
   }
 }
@@ -501,10 +524,42 @@ __device__ void decide(const AcceptArgs& a, int b) {
 __global__ void __launch_bounds__(kAcceptThreads, 4) accept_kernel(AcceptArgs a) {
   pdl_wait();
   pdl_launch_dependents();  // the residual kernel may start its prologue; it waits for this grid
-  const int r = blockIdx.x % a.R, b = blockIdx.x / a.R;  // b-major: a row's CTAs run together
+  // b-major, then row, then column chunk: a sequence's CTAs run together
+  const int c = blockIdx.x % a.nrc, rb = blockIdx.x / a.nrc;
+  const int r = rb % a.R, b = rb / a.R;
   RowStat* st = a.stats + static_cast<int64_t>(b) * a.R;
-  row_statistics(a, b, r, st + r);
   __shared__ int sh_last;
+  if (a.nrc == 1) {
+    row_statistics(a, b, r, 0, a.V, true, st + r);
+  } else {
+    // this chunk's partial, then the row's last CTA combines the chunks in column order
+    RowStat* part = a.cstats + static_cast<int64_t>(rb) * a.nrc;
+    row_statistics(a, b, r, c * a.rclen, min(a.V, (c + 1) * a.rclen), false, part + c);
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) sh_last = (atomicAdd(a.rcounters + rb, 1) == a.nrc - 1);
+    __syncthreads();
+    if (!sh_last) return;
+    __threadfence();
+    if (threadIdx.x == 0) {
+      RowStat t{__ldcg(&part[0].m), __ldcg(&part[0].s), 0.f, __ldcg(&part[0].amax)};
+      for (int j = 1; j < a.nrc; ++j) {
+        const float m2 = __ldcg(&part[j].m), s2 = __ldcg(&part[j].s);
+        if (a.greedy) argmax_merge(t.m, t.amax, m2, __ldcg(&part[j].amax));
+        else combine_ms(t.m, t.s, m2, s2);
+      }
+      if (a.greedy) {
+        t.s = 1.f;
+        t.amax = t.amax == 0x7fffffff ? 0 : t.amax;
+      } else {
+        const int i = r <= a.k ? r : r - a.k - 1;
+        const int64_t d = i < a.k ? a.draft[static_cast<int64_t>(b) * a.k + i] : -1;
+        if (d >= 0 && d < a.V) t.zx = row_ptr(a, b, r)[d] / a.temperature;
+      }
+      st[r] = t;
+      a.rcounters[rb] = 0;
+    }
+  }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) sh_last = (atomicAdd(a.counters + b, 1) == a.R - 1);
@@ -584,10 +639,15 @@ int launch_accept(AcceptArgs& a, char* ws, const AcceptLayout& l, cudaStream_t s
   a.C = residual_chunks(a.V);
   const int per = 4 * kAcceptThreads;
   a.chunk = ((a.V + a.C - 1) / a.C + per - 1) / per * per;
+  a.nrc = row_chunks(a.B * a.R, a.V, a.logits != 0);
+  a.rclen = ((a.V + a.nrc - 1) / a.nrc + 3) / 4 * 4;
+  a.rcounters = a.counters + 2 * a.B;
+  a.cstats = reinterpret_cast<RowStat*>(ws + l.cstats);
   if (a.status) cudaMemsetAsync(a.status, 0, sizeof(int32_t), s);
-  cudaMemsetAsync(a.counters, 0, 2 * static_cast<size_t>(a.B) * sizeof(int), s);
+  cudaMemsetAsync(a.counters, 0, (2 * static_cast<size_t>(a.B) + (a.nrc > 1 ? static_cast<size_t>(a.B) * a.R : 0)) * sizeof(int),
+                  s);
   cudaError_t e = cudaSuccess;
-  accept_kernel<<<static_cast<unsigned>(a.R) * a.B, kAcceptThreads, 0, s>>>(a);
+  accept_kernel<<<static_cast<unsigned>(a.R) * a.B * a.nrc, kAcceptThreads, 0, s>>>(a);
   e = cudaGetLastError();
   if (e == cudaSuccess && !a.greedy && !a.decide_only)
     e = launch_kernel(residual_kernel, dim3(static_cast<unsigned>(a.C) * a.B), dim3(kAcceptThreads), 0, s, true, a);
@@ -674,12 +734,9 @@ extern "C" int specb200_probabilities(const float* logits, int rows, int V, floa
 namespace {
 constexpr int kNoAllocMaxB = 512;
 constexpr int kNoAllocMaxK = 15;
-// accept_layout(kNoAllocMaxB, kNoAllocMaxK, V) for the largest V: counters, statistics, the
-// accepted lengths and 16 residual chunk sums per row (~331 KB)
-constexpr size_t kNoAllocScratchBytes =
-    256 + ((2 * kNoAllocMaxB * sizeof(int) + 255) / 256) * 256 +
-    ((static_cast<size_t>(kNoAllocMaxB) * (2 * kNoAllocMaxK + 1) * sizeof(RowStat) + 255) / 256) * 256 +
-    ((kNoAllocMaxB * sizeof(int) + 255) / 256) * 256 + ((kNoAllocMaxB * 16 * sizeof(double) + 255) / 256) * 256;
+// accept_layout(kNoAllocMaxB, kNoAllocMaxK, V) for the largest V: tickets, statistics, the
+// accepted lengths, 16 residual chunk sums per row and the chunked-row partials (~342 KB)
+constexpr size_t kNoAllocScratchBytes = accept_layout(kNoAllocMaxB, kNoAllocMaxK, kMaxSegs * kSeg).total;
 
 static __device__ __align__(256) unsigned char g_accept_scratch[kNoAllocScratchBytes];
 

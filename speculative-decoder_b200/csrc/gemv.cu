@@ -362,7 +362,7 @@ SPECB200_DEVINL void epilogue(const GemvArgs& a, const Chunk& k, const float* pa
 }
 
 template <int MR>
-__global__ void __launch_bounds__(kGvThreads) gemv_kernel(const __grid_constant__ GemvArgs a) {
+__global__ void __launch_bounds__(kGvThreads, 2) gemv_kernel(const __grid_constant__ GemvArgs a) {
   extern __shared__ __align__(128) uint8_t gv_smem_raw[];
   uint8_t* gv_smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gv_smem_raw) + 127) & ~uintptr_t(127));
   __shared__ float red[kGvWarps][MR];
