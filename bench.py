@@ -266,12 +266,91 @@ def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30
          "layers": spec["num_hidden_layers"]}
     if trace:
         n_ph = 2 + 5 * spec["num_hidden_layers"]
-        tr = torch.zeros(torch.cuda.get_device_properties(device).multi_processor_count, n_ph, 8, dtype=torch.int64,
-                         device=device)
+        sched = eng.schedule(1, K + 1)
+        if sched == "layers":
+            tr = torch.zeros(5 * spec["num_hidden_layers"] + 1, 512, 8, dtype=torch.int64, device=device)
+        else:
+            tr = torch.zeros(torch.cuda.get_device_properties(device).multi_processor_count, n_ph, 8,
+                             dtype=torch.int64, device=device)
         eng.forward_device(cache, ids, n_new, pastt, table, cap, False, logits, status, ws, trace=tr)
         torch.cuda.synchronize()
-        r["trace"] = trace_summary(tr, spec["num_hidden_layers"])
+        r["trace"] = (gemm_trace_summary(tr, spec["num_hidden_layers"]) if sched == "layers"
+                      else trace_summary(tr, spec["num_hidden_layers"]))
     return r
+
+
+def attention_trace(trace: torch.Tensor, base: int, n_layers: int, qkv_end: list, o_r0: list) -> dict:
+    """Per-layer attention records ([n_layers][512][8] from `base` in the flat trace): medians
+    over layers of the gap after q/k/v (`gap_in`), the gap before o (`gap_out`) and the latest
+    offset of each stamp 2..6 from the first wait return (cluster kernel: keys landed, products
+    done, warps merged, cluster merged, end; split items: keys landed, merged, published, end)."""
+    flat = trace.flatten()
+    keys = {k: [] for k in ("gap_in", "gap_out", "s2", "s3", "s4", "s5", "s6", "ctas")}
+    for l in range(n_layers):
+        a = flat[base + l * 512 * 8: base + (l + 1) * 512 * 8].view(512, 8).cpu().to(torch.float64)
+        ok = a[:, 0] > 0
+        if not bool(ok.any()):
+            continue
+        a = a[ok] / 1e3
+        r0 = float(a[:, 1][a[:, 1] > 0].min())
+        last = float(a[:, 2:7].max())
+        keys["ctas"].append(int(ok.sum()))
+        if qkv_end[l] is not None:
+            keys["gap_in"].append(r0 - qkv_end[l])
+        if l < len(o_r0) and o_r0[l] is not None:
+            keys["gap_out"].append(o_r0[l] - last)
+        for k in range(2, 7):
+            v = a[:, k][a[:, k] > 0]
+            if v.numel():
+                keys[f"s{k}"].append(float((v - r0).max()))
+    return {k: round(statistics.median(v), 2) for k, v in keys.items() if v}
+
+
+def gemm_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
+    """The per-layer schedule's tensor-core GEMM record ([4 n_layers + 1][512][8] globaltimer
+    stamps per CTA: entry, producer's wait return, first stage at the MMA warp, accumulator
+    ready, end; GEMMs q/k/v, o, gate/up, down per layer, then the LM head). Per GEMM, medians
+    over layers (us) of: `gap`, previous GEMM's last end to this one's first wait return (for
+    q/k/v it spans the RMSNorm launch, for o the attention launch, for gate/up the RMSNorm);
+    `first`, `acc`, `end`: median / max over CTAs of each stamp's offset from the first wait
+    return; `body`: first wait return to last end."""
+    n = 4 * n_layers + 1
+    t = trace.flatten()[: n * 512 * 8].view(n, 512, 8).cpu().to(torch.float64)
+    per = []
+    for i in range(n):
+        ok = t[i, :, 0] > 0
+        if not bool(ok.any()):
+            per.append(None)
+            continue
+        ti = t[i][ok] / 1e3
+        r0 = float(ti[:, 1][ti[:, 1] > 0].min())
+        rec = {"n": int(ok.sum()), "r0": r0, "end": float(ti[:, 4].max())}
+        for k, key in ((2, "first"), (3, "acc"), (4, "endo")):
+            v = ti[:, k][ti[:, k] > 0] - r0
+            rec[key] = (float(v.median()), float(v.max()))
+        per.append(rec)
+    if per[0] is None:
+        return {}
+    done = [x for x in per if x is not None]
+    out = {"total_us": round(done[-1]["end"] - per[0]["r0"], 1)}
+    med = lambda v: round(statistics.median(v), 2)  # noqa: E731
+    for j, name in enumerate(["qkv", "o", "gate_up", "down", "head"]):
+        rows = [n - 1] if name == "head" else [4 * l + j for l in range(n_layers)]
+        rows = [i for i in rows if per[i] is not None]
+        if not rows:
+            continue
+        d = {"ctas": per[rows[0]]["n"]}
+        gaps = [per[i]["r0"] - per[i - 1]["end"] for i in rows if i > 0 and per[i - 1] is not None]
+        d["gap"] = med(gaps) if gaps else None
+        d["body"] = med([per[i]["end"] - per[i]["r0"] for i in rows])
+        for key in ("first", "acc", "endo"):
+            d[key] = [med([per[i][key][0] for i in rows]), med([per[i][key][1] for i in rows])]
+        out[name] = d
+    att = attention_trace(trace, n * 512 * 8, n_layers, [p["end"] if p else None for p in per[0::4]],
+                          [p["r0"] if p else None for p in per[1::4]])
+    if att:
+        out["attention"] = att
+    return out
 
 
 def gemv_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
@@ -317,25 +396,11 @@ def gemv_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
         for key in ("staged", "landed", "endo", "wait", "dot"):
             d[key] = [med([per[i][key][0] for i in rows]), med([per[i][key][1] for i in rows])]
         out[name] = d
-    # attention launches (after the linear records): offsets from the first wait return
-    att = {"gap_in": [], "gap_out": [], "landed": [], "merged": [], "published": [], "end": [], "ctas": []}
-    for l in range(n_layers):
-        a = trace.flatten()[(n + l) * 296 * 8:(n + l + 1) * 296 * 8].view(296, 8).cpu().to(torch.float64)
-        ok = a[:, 0] > 0
-        if not bool(ok.any()):
-            continue
-        a = a[ok] / 1e3
-        r0 = float(a[:, 1].min())
-        att["ctas"].append(int(ok.sum()))
-        att["gap_in"].append(r0 - per[4 * l]["end"])
-        att["gap_out"].append(per[4 * l + 1]["r0"] - float(a[:, 5].max()))
-        for k, key in ((2, "landed"), (3, "merged"), (4, "published"), (5, "end")):
-            v = a[:, k]
-            v = v[v > 0]
-            if v.numel():
-                att[key].append(float((v - r0).max()))
-    if att["ctas"]:
-        out["attention"] = {k: med(v) for k, v in att.items() if v}
+    # attention launches (after the linear records)
+    att = attention_trace(trace, n * 296 * 8, n_layers, [p["end"] if p else None for p in per[0::4]],
+                          [p["r0"] if p else None for p in per[1::4]])
+    if att:
+        out["attention"] = att
     return out
 
 
@@ -390,7 +455,8 @@ def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30, 
                          device=device)
         sched = eng.schedule(1, 1)
         if sched == "gemv":
-            tr = torch.zeros(5 * spec["num_hidden_layers"] + 1, 296, 8, dtype=torch.int64, device=device)
+            L = spec["num_hidden_layers"]
+            tr = torch.zeros((4 * L + 1) * 296 * 8 + L * 512 * 8, dtype=torch.int64, device=device)
         eng.forward_device(cache, ids, one, pastt, table, cap, True, logits, status, ws, trace=tr)
         torch.cuda.synchronize()
         if sched == "chain":

@@ -204,8 +204,10 @@ typedef struct specb200_batch {
   uint64_t* trace;              /* NULL, or globaltimer stamps (profiling only): the layer- */
                                 /* stream kernel writes [grid x phases x 8]; the GEMV       */
                                 /* schedule [4 n_layers + 1 launches][296 CTAs][8]: entry, */
-                                /* wait return, inputs staged, weights landed, end, then   */
-                                /* the attention launches [n_layers][296][8] (zeroed first) */
+                                /* wait return, inputs staged, weights landed, end; the    */
+                                /* per-layer schedule [4 n_layers + 1 GEMMs][512][8]; both */
+                                /* followed by the attention launches [n_layers][512][8]   */
+                                /* (zeroed first)                                          */
 } specb200_batch;
 
 /* Weight tiles for the layer-stream kernel: W [N, K] bf16 row-major is rewritten as

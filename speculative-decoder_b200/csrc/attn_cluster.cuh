@@ -9,7 +9,7 @@
 //   first kernel launches without programmatic overlap), so they are loaded BEFORE
 //   griddepcontrol.wait; only the query rows and this call's new keys wait for the q/k/v
 //   projection.
-// - 16 warps each run 8-key mma.sync steps (attn_mma.cuh) over their share of the chunk. The
+// - 8 warps each run 8-key mma.sync steps (attn_mma.cuh) over their share of the chunk. The
 //   warps merge in shared memory, and the CTAs merge through distributed shared memory into
 //   the cluster's first CTA. There are no global partials, tickets or second round trips.
 #pragma once
@@ -18,7 +18,7 @@
 
 namespace specb200 {
 
-constexpr int kAcThreads = 512;
+constexpr int kAcThreads = 256;  // two CTAs per SM, so a batch-1 verify's clusters fit one wave
 constexpr int kAcWarps = kAcThreads / 32;
 constexpr int kAcMaxCluster = 8;
 constexpr int kAcMaxChunk = 512;  // keys per CTA
@@ -60,7 +60,7 @@ SPECB200_DEVINL void ac_cluster_sync() {
 SPECB200_DEVINL void ac_cluster_arrive_relaxed() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 SPECB200_DEVINL void ac_cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
 
-// Merge of the 16 warps' states into rows 0..R-1: out_o [R][64] (relative to out_m, base 2),
+// Merge of the warps' states into rows 0..R-1: out_o [R][64] (relative to out_m, base 2),
 // out_m [R], out_l [R]; scratch holds kAcWarps * (R * 64 + 32) floats. Ends with __syncthreads.
 SPECB200_DEVINL void ac_merge_warps(const AmState& st, float* scratch, int R, float* out_o, float* out_m, float* out_l) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, tig = lane & 3;
@@ -126,6 +126,19 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
   const int rank = static_cast<int>(ac_rank());
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const AcLayout lay = ac_layout(chunk, R, C, a.bs);
+  unsigned long long* tr = nullptr;  // optional record (AttnArgs::trace), thread 0
+  if (a.trace && tid == 0) {
+    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    if (cta < kAttnTraceCtas) tr = a.trace + (static_cast<size_t>(a.trace_slot) * kAttnTraceCtas + cta) * 8;
+  }
+  auto stamp = [&](int k) {
+    if (tr) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+      tr[k] = t;
+    }
+  };
+  stamp(0);
   const int past = a.past[b], nn = a.n_new[b], total = past + nn;
   if (nn <= 0) return;  // the same for every CTA of the cluster: none of them synchronises
   ac_cluster_arrive_relaxed();
@@ -163,6 +176,7 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
     *reinterpret_cast<uint4*>((isv ? v_s : k_s) + am_swz(r, cc * 8)) = make_uint4(0, 0, 0, 0);
   }
   if (pdl) pdl_wait();
+  stamp(1);
   // query rows (zero past R) and this call's keys
   const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(a.q);
   for (int i = tid; i < 16 * 8; i += kAcThreads) {
@@ -178,6 +192,7 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
   cp_async_commit();
   cp_async_wait<0>();
   __syncthreads();
+  stamp(2);
 
   AmState st;
   am_init(st, q_s);
@@ -189,6 +204,7 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
     am_step(st, k_s, v_s, 8 * j, kabs, min(8, kend - kabs), lim0, lim1, a.scale);
   }
   __syncthreads();  // K / V region becomes the merge scratch
+  stamp(3);
   float* scratch = reinterpret_cast<float*>(smem + lay.scratch);
   float* slots = reinterpret_cast<float*>(smem + lay.slots);  // [C][R * 64 + 32] in the first CTA
   // This CTA's merged partial, [R][64] o then m at R * 64 and l at R * 64 + 16: built in its
@@ -196,12 +212,14 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
   const int slot_floats = R * 64 + 32;
   float* mo = slots + rank * slot_floats;
   ac_merge_warps(st, scratch, R, mo, mo + R * 64, mo + R * 64 + 16);
+  stamp(4);
   ac_cluster_wait();
   if (rank != 0) {
     const uint32_t dst = ac_mapa(smem_u32(slots + rank * slot_floats), 0);
     for (int i = tid; i < slot_floats; i += kAcThreads) ac_st_remote(dst + 4 * i, mo[i]);
   }
   ac_cluster_sync();
+  stamp(5);
   if (rank != 0) return;
   __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
   for (int i = tid; i < R * D; i += kAcThreads) {
@@ -219,13 +237,14 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
     const int t = r / G, h = g * G + r % G;
     out[(static_cast<int64_t>(b * a.T + t) * a.Hq + h) * D + c] = __float2bfloat16_rn(O / L);
   }
+  stamp(6);
 }
 
-// Cluster plan: C = ceil(max_kv_len / 128) CTAs (at most kAcMaxCluster), chunk a multiple of 8.
+// Cluster plan: C = ceil(max_kv_len / 64) CTAs (at most kAcMaxCluster), chunk a multiple of 8.
 // Returns false when the keys do not fit C * kAcMaxChunk.
 inline bool plan_attention_cluster(int max_kv_len, AttnPlan* p) {
   const int len = max_kv_len < 1 ? 1 : max_kv_len;
-  int C = (len + 127) / 128;
+  int C = (len + 63) / 64;
   C = C > kAcMaxCluster ? kAcMaxCluster : C;
   const int chunk = ((len + C - 1) / C + 7) / 8 * 8;
   if (chunk > kAcMaxChunk) return false;

@@ -54,7 +54,7 @@ static __device__ void attention_item_mma(const AttnKernelArgs& ka, int b, int g
   unsigned long long* tr = nullptr;
   if (a.trace && tid == 0) {
     const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
-    if (cta < 296) tr = a.trace + (static_cast<size_t>(a.trace_slot) * 296 + cta) * 8;
+    if (cta < kAttnTraceCtas) tr = a.trace + (static_cast<size_t>(a.trace_slot) * kAttnTraceCtas + cta) * 8;
   }
   auto stamp = [&](int k) {
     if (tr) {

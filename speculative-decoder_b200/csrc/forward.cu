@@ -279,9 +279,17 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
 
   const bool pdl = true;
   const size_t layer_pool = static_cast<size_t>(bt.num_slots) * c.n_kv_heads * c.head_dim;
+  // With a trace buffer, tensor-core GEMM launch i (4 per layer, then the head) records its
+  // CTAs' timing (GemmScratch::trace).
+  int gemm_slot = 0;
   auto gemm = [&](const GemmShape& sh, const CUtensorMap* wmap, const CUtensorMap* xmap, const void* w, const T* x,
                   const Epilogue& e) -> int {
-    if (tc) return launch_gemm_tc(sh, *wmap, *xmap, e, gscr, status, s, pdl);
+    GemmScratch g = gscr;
+    if (bt.trace) {
+      g.trace = reinterpret_cast<unsigned long long*>(bt.trace);
+      g.trace_slot = gemm_slot++;
+    }
+    if (tc) return launch_gemm_tc(sh, *wmap, *xmap, e, g, status, s, pdl);
     return launch_gemm_simt<T>(sh, static_cast<const T*>(w), x, e, gscr, status, s, pdl);
   };
   // Decode-step schedule (bf16 only): the GEMV kernels, with the two RMSNorms of each layer
@@ -346,9 +354,9 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     aa.scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
     aa.out = attn;
     aa.status = status;
-    if (cv.gemv && bt.trace) {  // after the GEMV launch records
+    if (bt.trace) {  // after the GEMV or GEMM launch records
       aa.trace = reinterpret_cast<unsigned long long*>(bt.trace) +
-                 static_cast<size_t>(4 * c.n_layers + 1) * kGemvTraceCtas * kGemvTraceStamps;
+                 static_cast<size_t>(4 * c.n_layers + 1) * (cv.gemv ? kGemvTraceCtas * kGemvTraceStamps : kGemmTraceCtas * 8);
       aa.trace_slot = l;
     }
     if ((rc = launch_attention<T>(aa, cv.ap, attn_counters, attn_parts, s, pdl))) return rc;
@@ -413,6 +421,10 @@ int run_head(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv
   int rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(m.w.final_norm), rows_out, c.hidden, c.rms_eps, xbuf,
                              bt.last_only ? bt.n_new : nullptr, bt.T, s, true);
   if (rc) return rc;
+  if (bt.trace && !cv.gemv) {
+    gscr.trace = reinterpret_cast<unsigned long long*>(bt.trace);
+    gscr.trace_slot = 4 * c.n_layers;
+  }
   if (c.dtype == SPECB200_BF16) return launch_gemm_tc(cv.g_head, m.head, *x_final, eh, gscr, bt.status, s, true);
   return launch_gemm_simt<T>(cv.g_head, static_cast<const T*>(m.w.lm_head), xbuf, eh, gscr, bt.status, s, true);
 }

@@ -47,14 +47,25 @@ __device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, 
     if (!sh_last) return;
     __threadfence();
     const float* base = parts + static_cast<size_t>(tile_id) * s.splits * tile_elems;
+    constexpr int kSplitBatch = 4;  // splits whose partials are loaded together (summed in split order)
     for (int t0 = 0; t0 < valid; t0 += kEpiBatch) {
       float acc[kEpiBatch];
 #pragma unroll
       for (int j = 0; j < kEpiBatch; ++j) acc[j] = 0.f;
-      for (int sp = 0; sp < s.splits; ++sp) {
+      for (int sp0 = 0; sp0 < s.splits; sp0 += kSplitBatch) {
+        float v[kSplitBatch][kEpiBatch];
 #pragma unroll
-        for (int j = 0; j < kEpiBatch; ++j)
-          if (t0 + j < valid) acc[j] += __ldcg(base + sp * tile_elems + (t0 + j) * kTileN + t);
+        for (int q = 0; q < kSplitBatch; ++q)
+#pragma unroll
+          for (int j = 0; j < kEpiBatch; ++j)
+            v[q][j] = (sp0 + q < s.splits && t0 + j < valid)
+                          ? __ldcg(base + (sp0 + q) * tile_elems + (t0 + j) * kTileN + t)
+                          : 0.f;
+#pragma unroll
+        for (int q = 0; q < kSplitBatch; ++q)
+#pragma unroll
+          for (int j = 0; j < kEpiBatch; ++j)
+            if (sp0 + q < s.splits) acc[j] += v[q][j];
       }
 #pragma unroll
       for (int j = 0; j < kEpiBatch; ++j)
@@ -93,6 +104,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tile = blockIdx.x, split = blockIdx.y, m_tile = blockIdx.z;
+  unsigned long long* tr = nullptr;
+  if (scratch.trace) {
+    const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    if (cta < kGemmTraceCtas) tr = scratch.trace + (static_cast<size_t>(scratch.trace_slot) * kGemmTraceCtas + cta) * 8;
+  }
+  auto stamp = [&](int k) {
+    if (tr) {
+      unsigned long long t;
+      asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+      tr[k] = t;
+    }
+  };
+  if (threadIdx.x == 0) stamp(0);
   const int tile_id = m_tile * s.n_tiles + n_tile;
   int kb0, kb1;
   split_range(s, split, kb0, kb1);
@@ -130,6 +154,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tma_load_2d_hint(smem + i * stage_bytes, &w_map, &full[i], (kb0 + i) * kTileK, n_tile * kTileN, pol_w);
       }
       pdl_wait();
+      stamp(1);
       for (int i = 0; i < pre; ++i)
         tma_load_2d(smem + i * stage_bytes + kWTileBytes, &x_map, &full[i], (kb0 + i) * kTileK, m_tile * BN);
       for (int i = pre; i < nkb; ++i) {
@@ -152,6 +177,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     for (int i = 0; i < nkb; ++i) {
       const int st = i % stages;
       if (!mbar_wait_warp(&full[st], (i / stages) & 1, status, abort_flag)) break;
+      if (i == 0 && lane == 0) stamp(2);
       tc_fence_after();
       const uint64_t da = umma_desc_sw128(smem_u32(smem + st * stage_bytes));
       const uint64_t dx = umma_desc_sw128(smem_u32(smem + st * stage_bytes + kWTileBytes));
@@ -165,6 +191,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else {
     pdl_wait();
     const bool ok = mbar_wait_bounded(tmem_full, 0, status, abort_flag);
+    if (threadIdx.x == 0) stamp(3);
     tc_fence_after();
     float* tile = reinterpret_cast<float*>(smem);  // the pipeline stages are idle now
     if (ok) {
@@ -179,6 +206,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     epi_bar_sync();
     if (ok && !*reinterpret_cast<volatile int*>(abort_flag))
       finish_tile<__nv_bfloat16>(s, e, tile, scratch, tile_id, split, n_tile * kTileN, m_tile * BN);
+    if (threadIdx.x == 0) stamp(4);
   }
   tc_fence_before();
   __syncthreads();
@@ -325,8 +353,8 @@ int launch_gemm_tc(const GemmShape& s, const CUtensorMap& w_map, const CUtensorM
       smem_set = smem;
     }
   }
-  cudaError_t err = launch_kernel(gemm_tc_kernel, dim3(s.n_tiles, s.splits, s.m_tiles), dim3(kTcThreads), smem, stream, pdl,
-                           w_map, x_map, s, epi, scratch, status, stages);
+  cudaError_t err = launch_kernel(gemm_tc_kernel, dim3(s.n_tiles, s.splits, s.m_tiles), dim3(kTcThreads), smem, stream,
+                                  pdl, w_map, x_map, s, epi, scratch, status, stages);
   return err == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
 }
 

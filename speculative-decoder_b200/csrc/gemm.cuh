@@ -54,7 +54,13 @@ size_t gemm_workspace_bytes(const GemmShape& s);
 struct GemmScratch {
   int* counters;
   float* partials;
+  // Optional launch record (globaltimer ns): CTA c (linear block index < kGemmTraceCtas) of
+  // launch trace_slot writes trace[(trace_slot * kGemmTraceCtas + c) * 8 + {0..4}] = entry,
+  // producer's wait return, first stage at the MMA warp, accumulator ready, end.
+  unsigned long long* trace = nullptr;
+  int trace_slot = 0;
 };
+constexpr int kGemmTraceCtas = 512;
 size_t gemm_partials_bytes(const GemmShape& s);
 int launch_gemm_tc(const GemmShape& s, const CUtensorMap& w_map, const CUtensorMap& x_map, const Epilogue& epi,
                    GemmScratch scratch, int32_t* status, cudaStream_t stream, bool pdl);

@@ -52,12 +52,16 @@ struct AttnArgs {
   float scale;
   void* out;            // [B*T, Hq, D]
   int32_t* status;
-  // Optional record of the tensor-core decode items (globaltimer ns): CTA c (linear block
-  // index, < 296) of launch `trace_slot` writes trace[(trace_slot * 296 + c) * 8 + {0..5}] =
-  // entry, wait return, keys landed, merged within the CTA, partial published, end.
+  // Optional record (globaltimer ns); CTA c (linear block index, < kAttnTraceCtas) of launch
+  // `trace_slot` writes trace[(trace_slot * kAttnTraceCtas + c) * 8 + k]. Tensor-core decode
+  // items, k = 0..5: entry, wait return, keys landed, merged within the CTA, partial
+  // published, end. Cluster kernel, k = 0..6: entry, wait return, keys landed, products done,
+  // warps merged, cluster merged, end (first CTA).
   unsigned long long* trace = nullptr;
   int trace_slot = 0;
 };
+
+constexpr int kAttnTraceCtas = 512;  // CTAs per launch in an attention trace record
 
 // Split-KV merge tickets: a fixed region at the start of the attention workspace (see the
 // GEMM's kGemmMaxCounters). Split-KV is only planned when the group count fits in it.

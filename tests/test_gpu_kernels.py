@@ -278,7 +278,7 @@ def test_attention_matches_dense_reference(dtype, hq, hkv, d, T, bs, long_past):
     """Paged attention over shuffled blocks vs the reference's mask (lm/forward.py:44-49) on
     a dense fp32 copy: rows of lengths 1 .. long_past incl. a padded row. bf16 shapes with at
     most 16 query rows per KV head (T x G) run the cluster kernel (1, 6, 8, 15 and 16 rows
-    here; C = 2 .. 6 CTAs per cluster, block size 1 included) or, when the keys exceed one
+    here; C = 3 .. 8 CTAs per cluster, block size 1 included) or, when the keys exceed one
     cluster (4500 cached), the tensor-core split items; 24 rows (32 / 4 heads, T = 3) and
     the fp32 cases run the fp32 items."""
     g = torch.Generator().manual_seed(hq + T)
