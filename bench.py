@@ -285,7 +285,7 @@ def attention_trace(trace: torch.Tensor, base: int, n_layers: int, qkv_end: list
     offset of each stamp 2..6 from the first wait return (cluster kernel: keys landed, products
     done, warps merged, cluster merged, end; split items: keys landed, merged, published, end)."""
     flat = trace.flatten()
-    keys = {k: [] for k in ("gap_in", "gap_out", "s2", "s3", "s4", "s5", "s6", "ctas")}
+    keys = {k: [] for k in ("gap_in", "gap_out", "entry", "late", "s2", "s3", "s4", "s5", "s6", "ctas")}
     for l in range(n_layers):
         a = flat[base + l * 512 * 8: base + (l + 1) * 512 * 8].view(512, 8).cpu().to(torch.float64)
         ok = a[:, 0] > 0
@@ -295,6 +295,8 @@ def attention_trace(trace: torch.Tensor, base: int, n_layers: int, qkv_end: list
         r0 = float(a[:, 1][a[:, 1] > 0].min())
         last = float(a[:, 2:7].max())
         keys["ctas"].append(int(ok.sum()))
+        keys["entry"].append(float((a[:, 0] - r0).median()))
+        keys["late"].append(int((a[:, 0] > r0).sum()))
         if qkv_end[l] is not None:
             keys["gap_in"].append(r0 - qkv_end[l])
         if l < len(o_r0) and o_r0[l] is not None:
@@ -308,12 +310,13 @@ def attention_trace(trace: torch.Tensor, base: int, n_layers: int, qkv_end: list
 
 def gemm_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
     """The per-layer schedule's tensor-core GEMM record ([4 n_layers + 1][512][8] globaltimer
-    stamps per CTA: entry, producer's wait return, first stage at the MMA warp, accumulator
-    ready, end; GEMMs q/k/v, o, gate/up, down per layer, then the LM head). Per GEMM, medians
-    over layers (us) of: `gap`, previous GEMM's last end to this one's first wait return (for
-    q/k/v it spans the RMSNorm launch, for o the attention launch, for gate/up the RMSNorm);
-    `first`, `acc`, `end`: median / max over CTAs of each stamp's offset from the first wait
-    return; `body`: first wait return to last end."""
+    stamps per CTA: entry, wait return, first stage at the MMA warp, accumulator ready, end,
+    normalised operand built (GEMMs with the RMSNorm folded in); GEMMs q/k/v, o, gate/up, down
+    per layer, then the LM head). Per GEMM, medians over layers (us) of: `gap`, previous GEMM's
+    last end to this one's first wait return (it spans any RMSNorm launch, and for o the
+    attention launch); `late`, CTAs that entered after that first wait return; `entry`,
+    `first`, `xhat`, `acc`, `endo`: median / max over CTAs of each stamp's offset from the first
+    wait return; `body`: first wait return to last end."""
     n = 4 * n_layers + 1
     t = trace.flatten()[: n * 512 * 8].view(n, 512, 8).cpu().to(torch.float64)
     per = []
@@ -324,10 +327,11 @@ def gemm_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
             continue
         ti = t[i][ok] / 1e3
         r0 = float(ti[:, 1][ti[:, 1] > 0].min())
-        rec = {"n": int(ok.sum()), "r0": r0, "end": float(ti[:, 4].max())}
-        for k, key in ((2, "first"), (3, "acc"), (4, "endo")):
+        rec = {"n": int(ok.sum()), "r0": r0, "end": float(ti[:, 4].max()),
+               "late": int((ti[:, 0] > r0).sum())}
+        for k, key in ((0, "entry"), (2, "first"), (3, "acc"), (4, "endo"), (5, "xhat")):
             v = ti[:, k][ti[:, k] > 0] - r0
-            rec[key] = (float(v.median()), float(v.max()))
+            rec[key] = (float(v.median()), float(v.max())) if v.numel() else None
         per.append(rec)
     if per[0] is None:
         return {}
@@ -339,12 +343,13 @@ def gemm_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
         rows = [i for i in rows if per[i] is not None]
         if not rows:
             continue
-        d = {"ctas": per[rows[0]]["n"]}
+        d = {"ctas": per[rows[0]]["n"], "late": med([per[i]["late"] for i in rows])}
         gaps = [per[i]["r0"] - per[i - 1]["end"] for i in rows if i > 0 and per[i - 1] is not None]
         d["gap"] = med(gaps) if gaps else None
         d["body"] = med([per[i]["end"] - per[i]["r0"] for i in rows])
-        for key in ("first", "acc", "endo"):
-            d[key] = [med([per[i][key][0] for i in rows]), med([per[i][key][1] for i in rows])]
+        for key in ("entry", "first", "xhat", "acc", "endo"):
+            if all(per[i][key] is not None for i in rows):
+                d[key] = [med([per[i][key][0] for i in rows]), med([per[i][key][1] for i in rows])]
         out[name] = d
     att = attention_trace(trace, n * 512 * 8, n_layers, [p["end"] if p else None for p in per[0::4]],
                           [p["r0"] if p else None for p in per[1::4]])

@@ -97,6 +97,17 @@ bool attention_prepare() {
   std::call_once(once, [] {
     ok = cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAcSmemLimit) ==
          cudaSuccess;
+    // the largest carveout, as every kernel of a forward, so that consecutive kernels share SMs
+    for (const void* f : {reinterpret_cast<const void*>(attention_cluster_kernel),
+                          reinterpret_cast<const void*>(attention_mma_kernel),
+                          reinterpret_cast<const void*>(attention_kernel<float, 16>),
+                          reinterpret_cast<const void*>(attention_kernel<float, 32>),
+                          reinterpret_cast<const void*>(attention_kernel<float, 64>),
+                          reinterpret_cast<const void*>(attention_kernel<__nv_bfloat16, 16>),
+                          reinterpret_cast<const void*>(attention_kernel<__nv_bfloat16, 32>),
+                          reinterpret_cast<const void*>(attention_kernel<__nv_bfloat16, 64>)})
+      ok = ok && cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      cudaSharedmemCarveoutMaxShared) == cudaSuccess;
   });
   return ok;
 }

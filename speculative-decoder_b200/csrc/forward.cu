@@ -42,6 +42,7 @@ struct Model {
   bool stream_ok;  // packed weights present and shapes within the layer-stream kernel's limits
   int chain_C = 0;  // cluster size of the layer-chain kernel, 0 = not used for this model
   bool gemv_ok = false;  // bf16 weights usable by the decode-step GEMV kernels (gemv.cu)
+  bool gemm_norm = false;  // RMSNorms folded into the tensor-core GEMMs that consume them
 };
 
 // Whether a call of this shape runs the cluster layer-chain kernel (small models, decode
@@ -87,6 +88,7 @@ struct Carve {
   GemmShape g_qkv, g_o, g_gu, g_down, g_head;
   bool gemv;  // decode-step schedule: the per-layer order with GEMV kernels and fused norms
   bool gemv_head;  // ... and the LM head as a GEMV with the final norm folded in
+  bool norm_qkv, norm_gu, norm_head;  // per-layer schedule: norm folded into these GEMMs
   GemvPlan v_qkv, v_o, v_gu, v_down, v_head;
   AttnPlan ap;
 };
@@ -126,6 +128,9 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   r.chain = use_chain(m, B, T, r.cph, &r.csplits, &r.cl);
   r.stream = !r.chain && use_stream(m, B, T, &r.grid, &r.max_contrib);
   r.gemv_head = false;
+  r.norm_qkv = m.gemm_norm && gemm_norm_fits(r.g_qkv);
+  r.norm_gu = m.gemm_norm && gemm_norm_fits(r.g_gu);
+  r.norm_head = m.gemm_norm && gemm_norm_fits(r.g_head);
   r.gemv = !r.chain && !r.stream &&
            use_gemv(m, M, rows_out, &r.v_qkv, &r.v_o, &r.v_gu, &r.v_down, &r.v_head, &r.gemv_head);
   r.ap = r.stream ? plan_attention_decode(B, c.n_kv_heads, max_kv_len, r.grid)
@@ -283,11 +288,18 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
   // CTAs' timing (GemmScratch::trace).
   int gemm_slot = 0;
   auto gemm = [&](const GemmShape& sh, const CUtensorMap* wmap, const CUtensorMap* xmap, const void* w, const T* x,
-                  const Epilogue& e) -> int {
+                  const Epilogue& e, const void* norm_w = nullptr) -> int {
     GemmScratch g = gscr;
     if (bt.trace) {
       g.trace = reinterpret_cast<unsigned long long*>(bt.trace);
       g.trace_slot = gemm_slot++;
+    }
+    if (tc && norm_w) {  // X = RMSNorm(hidden) built inside the GEMM
+      GemmNorm nrm;
+      nrm.x = reinterpret_cast<const __nv_bfloat16*>(hidden);
+      nrm.w = static_cast<const __nv_bfloat16*>(norm_w);
+      nrm.eps = c.rms_eps;
+      return launch_gemm_tc(sh, *wmap, *xmap, e, g, status, s, pdl, &nrm);
     }
     if (tc) return launch_gemm_tc(sh, *wmap, *xmap, e, g, status, s, pdl);
     return launch_gemm_simt<T>(sh, static_cast<const T*>(w), x, e, gscr, status, s, pdl);
@@ -317,8 +329,9 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
   for (int l = 0; l < c.n_layers; ++l) {
     const specb200_layer_weights& L = m.layers[l];
     const LayerMaps* mp = tc ? &m.maps[l] : nullptr;
-    if (!cv.gemv && (rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.attn_norm), M, c.hidden, c.rms_eps, xbuf,
-                                            nullptr, 1, s, pdl)))
+    if (!cv.gemv && !cv.norm_qkv &&
+        (rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.attn_norm), M, c.hidden, c.rms_eps, xbuf, nullptr, 1, s,
+                                pdl)))
       return rc;
     Epilogue eq = {};
     eq.op = EPI_QKV;
@@ -334,7 +347,8 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     eq.n_kv_heads = c.n_kv_heads;
     eq.head_dim = c.head_dim;
     rc = cv.gemv ? gemv(cv.v_qkv, L.w_qkv, hidden, L.attn_norm, eq, m.qkv_n, c.hidden)
-                 : gemm(cv.g_qkv, mp ? &mp->qkv : nullptr, &x_hidden, L.w_qkv, xbuf, eq);
+                 : gemm(cv.g_qkv, mp ? &mp->qkv : nullptr, &x_hidden, L.w_qkv, xbuf, eq,
+                        cv.norm_qkv ? L.attn_norm : nullptr);
     if (rc) return rc;
 
     AttnArgs aa;
@@ -368,15 +382,16 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     rc = cv.gemv ? gemv(cv.v_o, L.w_o, attn, nullptr, er, c.hidden, qd)
                  : gemm(cv.g_o, mp ? &mp->o : nullptr, &x_attn, L.w_o, attn, er);
     if (rc) return rc;
-    if (!cv.gemv && (rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.mlp_norm), M, c.hidden, c.rms_eps, xbuf,
-                                            nullptr, 1, s, pdl)))
+    if (!cv.gemv && !cv.norm_gu &&
+        (rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.mlp_norm), M, c.hidden, c.rms_eps, xbuf, nullptr, 1, s,
+                                pdl)))
       return rc;
     Epilogue eg = {};
     eg.op = EPI_SILU_MUL;
     eg.out = act;
     eg.ldo = c.intermediate;
     rc = cv.gemv ? gemv(cv.v_gu, L.w_gate_up, hidden, L.mlp_norm, eg, 2 * c.intermediate, c.hidden)
-                 : gemm(cv.g_gu, mp ? &mp->gu : nullptr, &x_hidden, L.w_gate_up, xbuf, eg);
+                 : gemm(cv.g_gu, mp ? &mp->gu : nullptr, &x_hidden, L.w_gate_up, xbuf, eg, cv.norm_gu ? L.mlp_norm : nullptr);
     if (rc) return rc;
     rc = cv.gemv ? gemv(cv.v_down, L.w_down, act, nullptr, er, c.hidden, c.intermediate)
                  : gemm(cv.g_down, mp ? &mp->down : nullptr, &x_act, L.w_down, act, er);
@@ -418,13 +433,22 @@ int run_head(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv
     g.trace_slot = 4 * c.n_layers;
     return launch_gemv(g, s, true);
   }
-  int rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(m.w.final_norm), rows_out, c.hidden, c.rms_eps, xbuf,
-                             bt.last_only ? bt.n_new : nullptr, bt.T, s, true);
-  if (rc) return rc;
   if (bt.trace && !cv.gemv) {
     gscr.trace = reinterpret_cast<unsigned long long*>(bt.trace);
     gscr.trace_slot = 4 * c.n_layers;
   }
+  if (cv.norm_head) {  // the final norm and the last-token selection inside the LM head GEMM
+    GemmNorm nrm;
+    nrm.x = reinterpret_cast<const __nv_bfloat16*>(hidden);
+    nrm.w = static_cast<const __nv_bfloat16*>(m.w.final_norm);
+    nrm.sel_n_new = bt.last_only ? bt.n_new : nullptr;
+    nrm.T_tokens = bt.T;
+    nrm.eps = c.rms_eps;
+    return launch_gemm_tc(cv.g_head, m.head, *x_final, eh, gscr, bt.status, s, true, &nrm);
+  }
+  int rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(m.w.final_norm), rows_out, c.hidden, c.rms_eps, xbuf,
+                             bt.last_only ? bt.n_new : nullptr, bt.T, s, true);
+  if (rc) return rc;
   if (c.dtype == SPECB200_BF16) return launch_gemm_tc(cv.g_head, m.head, *x_final, eh, gscr, bt.status, s, true);
   return launch_gemm_simt<T>(cv.g_head, static_cast<const T*>(m.w.lm_head), xbuf, eh, gscr, bt.status, s, true);
 }
@@ -543,6 +567,12 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
   }
   m->chain_C = packed ? chain_cluster_size() : 0;
   attention_prepare();  // function attributes are set here, outside any stream capture
+  gemm_prepare();
+  norm_prepare();
+  // Folding the RMSNorms into the tensor-core GEMMs is opt-in (SPECB200_GEMM_NORM=1): the
+  // operand build and its 64 KB of shared memory (which keeps the attention CTAs off the SMs
+  // while the q/k/v GEMM runs) cost more than the norm launches (1.66 vs 1.58 ms per verify).
+  m->gemm_norm = c.dtype == SPECB200_BF16 && env_int("SPECB200_GEMM_NORM", 0) == 1;
   // Decode-step GEMV schedule: bf16 weights, 16-byte aligned rows (SPECB200_GEMV=0 turns it off).
   auto al16 = [](const void* p) { return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   m->gemv_ok = c.dtype == SPECB200_BF16 && env_int("SPECB200_GEMV", 1) == 1 && al16(weights->lm_head) &&
@@ -573,8 +603,9 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
 }
 
 // Kernel launches of one forward call: 3 for the layer chain (chain kernel, final norm, LM head),
-// 1 for the layer stream, 2 + 5 L for the GEMV schedule (prep, 5 per layer, head), 3 + 7 L for
-// the per-layer kernels (prep, 7 per layer, final norm, head).
+// 1 for the layer stream, 2 + 5 L for the GEMV schedule (prep, 5 per layer, head), and for the
+// per-layer kernels 2 + 5 L (prep, 5 per layer, head) plus one launch per RMSNorm that is not
+// folded into its GEMM (at most 3 + 7 L).
 extern "C" int specb200_forward_launches(void* model, int B, int T) {
   if (!model || B <= 0 || T <= 0) return 0;
   const Model& m = *static_cast<Model*>(model);
@@ -586,9 +617,14 @@ extern "C" int specb200_forward_launches(void* model, int B, int T) {
   if (use_stream(m, B, T, &grid, &mc)) return 1;
   GemvPlan v[5];
   bool head_gemv = false;
-  if (use_gemv(m, B * T, B, &v[0], &v[1], &v[2], &v[3], &v[4], &head_gemv))
-    return (head_gemv ? 2 : 3) + 5 * m.cfg.n_layers;
-  return 3 + 7 * m.cfg.n_layers;
+  const int M = B * T;
+  const bool tc = m.cfg.dtype == SPECB200_BF16;
+  const bool head_norm = m.gemm_norm && gemm_norm_fits(plan_gemm(B, m.cfg.vocab, m.cfg.hidden, tc));
+  if (use_gemv(m, M, B, &v[0], &v[1], &v[2], &v[3], &v[4], &head_gemv))
+    return (head_gemv || head_norm ? 2 : 3) + 5 * m.cfg.n_layers;
+  const int norms = (m.gemm_norm && gemm_norm_fits(plan_gemm(M, m.qkv_n, m.cfg.hidden, tc)) ? 0 : 1) +
+                    (m.gemm_norm && gemm_norm_fits(plan_gemm(M, 2 * m.cfg.intermediate, m.cfg.hidden, tc)) ? 0 : 1);
+  return 2 + (head_norm ? 0 : 1) + (5 + norms) * m.cfg.n_layers;
 }
 
 extern "C" int specb200_forward_uses_stream(void* model, int B, int T) {

@@ -464,6 +464,11 @@ bool gemv_prepare() {
     ok = cudaFuncSetAttribute(gemv_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess &&
          cudaFuncSetAttribute(gemv_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess &&
          cudaFuncSetAttribute(gemv_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) == cudaSuccess;
+    // the largest carveout, as every kernel of a forward, so that consecutive kernels share SMs
+    for (const void* f : {reinterpret_cast<const void*>(gemv_kernel<1>), reinterpret_cast<const void*>(gemv_kernel<2>),
+                          reinterpret_cast<const void*>(gemv_kernel<4>)})
+      ok = ok && cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                      cudaSharedmemCarveoutMaxShared) == cudaSuccess;
   });
   return ok;
 }

@@ -36,6 +36,8 @@ struct PrepArgs {
 
 template <typename T>
 int launch_prep_embed(const PrepArgs& a, const T* embed, T* hidden, cudaStream_t s, bool pdl);
+// Function attributes of the prep / RMSNorm kernels; call outside any stream capture.
+bool norm_prepare();
 template <typename T>
 int launch_rmsnorm(const T* x, const T* w, int rows, int H, float eps, T* y, const int32_t* sel_n_new, int T_tokens,
                    cudaStream_t s, bool pdl);

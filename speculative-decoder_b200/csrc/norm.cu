@@ -56,38 +56,131 @@ __global__ void __launch_bounds__(128)
   for (int i = threadIdx.x; i < H; i += blockDim.x) dst[i] = src[i];
 }
 
+// One CTA per output row; each thread holds up to kNormChunks 16-byte chunks of the row in
+// registers (H <= 256 * kNormChunks * 16 / sizeof(T)), so the row is read from memory once; the
+// weight chunks are loaded before griddepcontrol.wait (parameters, not produced upstream).
+constexpr int kNormThreads = 256;
+constexpr int kNormChunks = 4;
+
 template <typename T>
-__global__ void __launch_bounds__(256)
+SPECB200_DEVINL void unpack_chunk(const uint4& v, float (&f)[16 / sizeof(T)]);
+template <>
+SPECB200_DEVINL void unpack_chunk<__nv_bfloat16>(const uint4& v, float (&f)[8]) {
+  const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = __uint_as_float(u[i] << 16);
+    f[2 * i + 1] = __uint_as_float(u[i] & 0xffff0000u);
+  }
+}
+template <>
+SPECB200_DEVINL void unpack_chunk<float>(const uint4& v, float (&f)[4]) {
+  f[0] = __uint_as_float(v.x);
+  f[1] = __uint_as_float(v.y);
+  f[2] = __uint_as_float(v.z);
+  f[3] = __uint_as_float(v.w);
+}
+template <typename T>
+SPECB200_DEVINL uint4 pack_chunk(const float (&f)[16 / sizeof(T)]);
+template <>
+SPECB200_DEVINL uint4 pack_chunk<__nv_bfloat16>(const float (&f)[8]) {
+  uint32_t u[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 p = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    u[i] = *reinterpret_cast<const uint32_t*>(&p);
+  }
+  return make_uint4(u[0], u[1], u[2], u[3]);
+}
+template <>
+SPECB200_DEVINL uint4 pack_chunk<float>(const float (&f)[4]) {
+  return make_uint4(__float_as_uint(f[0]), __float_as_uint(f[1]), __float_as_uint(f[2]), __float_as_uint(f[3]));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kNormThreads)
     rmsnorm_kernel(const T* __restrict__ x, const T* __restrict__ w, int H, float eps, T* __restrict__ y,
                    const int32_t* __restrict__ sel_n_new, int T_tokens) {
+  constexpr int E = 16 / sizeof(T);  // elements per chunk
   pdl_launch_dependents();
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const int nch = H / E;
+  const bool vec = (H % E == 0) && nch <= kNormThreads * kNormChunks &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(y)) & 15) == 0;
+  uint4 wv[kNormChunks];
+  if (vec) {
+#pragma unroll
+    for (int i = 0; i < kNormChunks; ++i) {
+      const int c = tid + i * kNormThreads;
+      wv[i] = c < nch ? __ldg(reinterpret_cast<const uint4*>(w) + c) : make_uint4(0, 0, 0, 0);
+    }
+  }
   pdl_wait();
-  const int row = blockIdx.x;
   // A masked-out row (n_new == 0) selects its first token: finite, and never read back.
   const int64_t src = sel_n_new ? static_cast<int64_t>(row) * T_tokens + max(sel_n_new[row] - 1, 0) : row;
   const T* xr = x + src * H;
+  T* yr = y + static_cast<int64_t>(row) * H;
+  __shared__ float sh[kNormThreads / 32];
+  auto block_sum = [&](float v) {
+    v = warp_sum(v);
+    if ((tid & 31) == 0) sh[tid >> 5] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNormThreads / 32; ++i) t += sh[i];
+    return t;
+  };
+  if (vec) {
+    uint4 xv[kNormChunks];
+#pragma unroll
+    for (int i = 0; i < kNormChunks; ++i) {
+      const int c = tid + i * kNormThreads;
+      xv[i] = c < nch ? __ldcg(reinterpret_cast<const uint4*>(xr) + c) : make_uint4(0, 0, 0, 0);
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < kNormChunks; ++i) {
+      float f[E];
+      unpack_chunk<T>(xv[i], f);
+#pragma unroll
+      for (int e = 0; e < E; ++e) ss = fmaf(f[e], f[e], ss);
+    }
+    const float r = 1.0f / sqrtf(block_sum(ss) / static_cast<float>(H) + eps);
+#pragma unroll
+    for (int i = 0; i < kNormChunks; ++i) {
+      const int c = tid + i * kNormThreads;
+      if (c >= nch) break;
+      float f[E], g[E];
+      unpack_chunk<T>(xv[i], f);
+      unpack_chunk<T>(wv[i], g);
+#pragma unroll
+      for (int e = 0; e < E; ++e) f[e] = g[e] * round_to<T>(f[e] * r);
+      reinterpret_cast<uint4*>(yr)[c] = pack_chunk<T>(f);
+    }
+    return;
+  }
   float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+  for (int i = tid; i < H; i += kNormThreads) {
     const float v = to_f32<T>(xr[i]);
     ss = fmaf(v, v, ss);
   }
-  __shared__ float sh[8];
-  ss = warp_sum(ss);
-  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float v = threadIdx.x < (blockDim.x >> 5) ? sh[threadIdx.x] : 0.f;
-    v = warp_sum(v);
-    if (threadIdx.x == 0) sh[0] = v;
-  }
-  __syncthreads();
-  const float var = sh[0] / static_cast<float>(H);
-  const float r = 1.0f / sqrtf(var + eps);
-  T* yr = y + static_cast<int64_t>(row) * H;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+  const float r = 1.0f / sqrtf(block_sum(ss) / static_cast<float>(H) + eps);
+  for (int i = tid; i < H; i += kNormThreads) {
     const float nx = round_to<T>(to_f32<T>(xr[i]) * r);
     yr[i] = from_f32<T>(to_f32<T>(w[i]) * nx);
   }
+}
+
+bool norm_prepare() {
+  // the largest carveout, as every kernel of a forward, so that consecutive kernels share SMs
+  bool ok = true;
+  for (const void* f : {reinterpret_cast<const void*>(rmsnorm_kernel<float>),
+                        reinterpret_cast<const void*>(rmsnorm_kernel<__nv_bfloat16>),
+                        reinterpret_cast<const void*>(prep_embed_kernel<float>),
+                        reinterpret_cast<const void*>(prep_embed_kernel<__nv_bfloat16>)})
+    ok = ok && cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) ==
+                   cudaSuccess;
+  return ok;
 }
 
 template <typename T>
@@ -101,7 +194,8 @@ int launch_prep_embed(const PrepArgs& a, const T* embed, T* hidden, cudaStream_t
 template <typename T>
 int launch_rmsnorm(const T* x, const T* w, int rows, int H, float eps, T* y, const int32_t* sel_n_new, int T_tokens,
                    cudaStream_t s, bool pdl) {
-  cudaError_t e = launch_kernel(rmsnorm_kernel<T>, dim3(rows), dim3(256), 0, s, pdl, x, w, H, eps, y, sel_n_new, T_tokens);
+  cudaError_t e =
+      launch_kernel(rmsnorm_kernel<T>, dim3(rows), dim3(kNormThreads), 0, s, pdl, x, w, H, eps, y, sel_n_new, T_tokens);
   return e == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
 }
 

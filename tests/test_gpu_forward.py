@@ -377,7 +377,9 @@ def test_gemv_schedule_matches_per_layer_kernels(monkeypatch, dims):
     gemv = Engine(model)
     assert per_layer.schedule(1, 1) == "layers" and per_layer.schedule(2, 2) == "layers"
     assert gemv.schedule(1, 1) == "gemv" and gemv.schedule(2, 2) == "gemv" and gemv.schedule(1, 3) == "gemv"
-    head_launches = 1 if dims[-1] <= 4096 else 2  # GEMV head with the norm folded in, or norm + GEMM
+    # prep, 5 per layer, then the LM head: a GEMV with the final norm folded in (small vocabulary)
+    # or the final norm and the tensor-core GEMM
+    head_launches = 1 if dims[-1] <= 4096 else 2
     assert gemv.schedule(1, 5) == "layers" and gemv.launches(1, 1) == 1 + head_launches + 5 * 2
     (la, ca), (lb, cb) = _gemv_steps(per_layer, model), _gemv_steps(gemv, model)
     for a, b in zip(la, lb):
@@ -418,3 +420,38 @@ def test_gemv_schedule_matches_oracle(dims):
             g, o = got[b, :n], want[b, :n]
             scale = np.abs(o).max()
             assert np.abs(g - o).max() <= 2e-2 * scale + 1e-3, (b, np.abs(g - o).max(), scale)
+
+
+@pytest.mark.parametrize("dims", [(2048, 2, 32, 32, 8192, 49152), (576, 2, 9, 3, 1536, 49152)])
+def test_gemm_norm_matches_separate_norm(monkeypatch, dims):
+    """Verify-sized calls (5 and 2 x 4 ragged tokens, all rows and last rows only) with the
+    RMSNorms folded into the tensor-core GEMMs against the same GEMMs after separate RMSNorm
+    launches: the same roundings with the sums of squares in another order, so logits agree
+    to bf16 noise and the fused schedule makes 2 + 5 L launches."""
+    from cache.kv import KVCache
+    from specb200.engine import Engine
+
+    model = _bf16_model(*dims, seed=21, theta=130000.0).to(DEV)
+    monkeypatch.setenv("SPECB200_GEMV", "0")
+    monkeypatch.setenv("SPECB200_GEMM_NORM", "0")
+    separate = Engine(model)
+    monkeypatch.setenv("SPECB200_GEMM_NORM", "1")
+    fused = Engine(model)
+    assert separate.launches(1, 5) == 3 + 7 * 2 and fused.launches(1, 5) == 2 + 5 * 2
+    outs = []
+    for eng in (separate, fused):
+        cache = KVCache.for_model(model.config, num_blocks=96, block_size=16, dtype=torch.bfloat16, device=DEV)
+        for s in range(2):
+            cache.add(s)
+            p = torch.randint(0, dims[-1], (1, 200 - 37 * s), generator=torch.Generator().manual_seed(60 + s))
+            eng.forward(cache, [s], p, [200 - 37 * s], last_only=True)
+        steps = [eng.forward(cache, [0], torch.tensor([[5, 6, 7, 8, 9]]), [5]),
+                 eng.forward(cache, [0, 1], torch.tensor([[10, 11, 12, 13], [14, 15, 16, 0]]), [4, 3], last_only=True),
+                 eng.forward(cache, [1], torch.tensor([[17, 18, 19, 20, 21]]), [5], last_only=True)]
+        outs.append([x.float().cpu() for x in steps])
+    for a, b in zip(*outs):
+        scale = a.abs().max().item()
+        assert (a - b).abs().max().item() <= 1e-2 * scale, ((a - b).abs().max().item(), scale)
+        top2 = a.topk(2, dim=-1).values
+        agree = a.argmax(-1) == b.argmax(-1)
+        assert bool((agree | ((top2[..., 0] - top2[..., 1]) < 1e-2 * scale)).all())

@@ -231,9 +231,12 @@ def test_ngram_reference_kats():
 
 # ---------------------------------------------------------------- RMSNorm (K2)
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_rmsnorm_matches_hf_formula(dtype):
-    x = (torch.randn(7, 576, generator=torch.Generator().manual_seed(1)) * 2).to(DEV, dtype)
-    w = (1 + 0.1 * torch.randn(576, generator=torch.Generator().manual_seed(2))).to(DEV, dtype)
+@pytest.mark.parametrize("H", [576, 2048, 8200, 100])
+def test_rmsnorm_matches_hf_formula(dtype, H):
+    """Vectorised rows held in registers (576, 2048), the scalar path past the register budget
+    (8200 elements) and for rows that are not whole 16-byte chunks (100 bf16 elements)."""
+    x = (torch.randn(7, H, generator=torch.Generator().manual_seed(1)) * 2).to(DEV, dtype)
+    w = (1 + 0.1 * torch.randn(H, generator=torch.Generator().manual_seed(2))).to(DEV, dtype)
     xf = x.float()
     ref = w * (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-5)).to(dtype)
     got = _ops().rmsnorm(x, w, 1e-5)
