@@ -329,7 +329,8 @@ def gemm_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
         r0 = float(ti[:, 1][ti[:, 1] > 0].min())
         rec = {"n": int(ok.sum()), "r0": r0, "end": float(ti[:, 4].max()),
                "late": int((ti[:, 0] > r0).sum())}
-        for k, key in ((0, "entry"), (2, "first"), (3, "acc"), (4, "endo"), (5, "xhat")):
+        for k, key in ((0, "entry"), (2, "first"), (3, "acc"), (4, "endo"), (5, "fenced"), (6, "ticket"),
+                       (7, "reduced")):
             v = ti[:, k][ti[:, k] > 0] - r0
             rec[key] = (float(v.median()), float(v.max())) if v.numel() else None
         per.append(rec)
@@ -347,7 +348,7 @@ def gemm_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
         gaps = [per[i]["r0"] - per[i - 1]["end"] for i in rows if i > 0 and per[i - 1] is not None]
         d["gap"] = med(gaps) if gaps else None
         d["body"] = med([per[i]["end"] - per[i]["r0"] for i in rows])
-        for key in ("entry", "first", "xhat", "acc", "endo"):
+        for key in ("entry", "first", "acc", "fenced", "ticket", "reduced", "endo"):
             if all(per[i][key] is not None for i in rows):
                 d[key] = [med([per[i][key][0] for i in rows]), med([per[i][key][1] for i in rows])]
         out[name] = d

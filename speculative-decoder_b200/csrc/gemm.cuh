@@ -55,8 +55,9 @@ struct GemmScratch {
   int* counters;
   float* partials;
   // Optional launch record (globaltimer ns): CTA c (linear block index < kGemmTraceCtas) of
-  // launch trace_slot writes trace[(trace_slot * kGemmTraceCtas + c) * 8 + {0..4}] = entry,
-  // producer's wait return, first stage at the MMA warp, accumulator ready, end.
+  // launch trace_slot writes trace[(trace_slot * kGemmTraceCtas + c) * 8 + {0..7}] = entry,
+  // wait return, first stage at the MMA warp, accumulator ready, end, then with split-K the
+  // partial published (after the fence), the ticket taken, the partials summed.
   unsigned long long* trace = nullptr;
   int trace_slot = 0;
 };
