@@ -541,13 +541,30 @@ __global__ void __launch_bounds__(kAcceptThreads, 4) accept_kernel(AcceptArgs a)
     __syncthreads();
     if (!sh_last) return;
     __threadfence();
-    if (threadIdx.x == 0) {
-      RowStat t{__ldcg(&part[0].m), __ldcg(&part[0].s), 0.f, __ldcg(&part[0].amax)};
-      for (int j = 1; j < a.nrc; ++j) {
-        const float m2 = __ldcg(&part[j].m), s2 = __ldcg(&part[j].s);
-        if (a.greedy) argmax_merge(t.m, t.amax, m2, __ldcg(&part[j].amax));
+    RowStat t{-INFINITY, 0.f, 0.f, 0x7fffffff};
+    if (threadIdx.x < 32) {
+      // warp 0 combines the chunk partials: lane l folds chunks l, l + 32 (their loads in
+      // flight together), then a fixed xor tree across lanes (deterministic order)
+      const int lane = threadIdx.x;
+#pragma unroll
+      for (int q = 0; q < kMaxRowChunks / 32; ++q) {
+        const int j = lane + 32 * q;
+        if (j < a.nrc) {
+          const float m2 = __ldcg(&part[j].m), s2 = __ldcg(&part[j].s);
+          const int i2 = __ldcg(&part[j].amax);
+          if (a.greedy) argmax_merge(t.m, t.amax, m2, i2);
+          else combine_ms(t.m, t.s, m2, s2);
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float m2 = __shfl_xor_sync(0xffffffffu, t.m, o), s2 = __shfl_xor_sync(0xffffffffu, t.s, o);
+        const int i2 = __shfl_xor_sync(0xffffffffu, t.amax, o);
+        if (a.greedy) argmax_merge(t.m, t.amax, m2, i2);
         else combine_ms(t.m, t.s, m2, s2);
       }
+    }
+    if (threadIdx.x == 0) {
       if (a.greedy) {
         t.s = 1.f;
         t.amax = t.amax == 0x7fffffff ? 0 : t.amax;

@@ -43,6 +43,7 @@ struct Model {
   int chain_C = 0;  // cluster size of the layer-chain kernel, 0 = not used for this model
   bool gemv_ok = false;  // bf16 weights usable by the decode-step GEMV kernels (gemv.cu)
   bool gemm_norm = false;  // RMSNorms folded into the tensor-core GEMMs that consume them
+  bool defer_resid = true;  // residual adds of the o / down GEMMs deferred to the next RMSNorm
 };
 
 // Whether a call of this shape runs the cluster layer-chain kernel (small models, decode
@@ -79,7 +80,10 @@ size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 struct Carve {
   size_t gemm_counters, attn_counters, stream_ctl, hidden, xbuf, qbuf, attn, act, pos, slot, gemm_parts, attn_parts,
-      stream_parts, total;
+      stream_parts, resid_parts, total;
+  // per-layer schedule: the o and down GEMMs store split partials (EPI_PARTIAL) and the RMSNorm
+  // launch that follows each adds them to the residual stream (launch_residual_norm)
+  bool defer;
   bool stream, chain;
   int grid, max_contrib;
   ChainPhase cph[4];
@@ -131,8 +135,15 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   r.norm_qkv = m.gemm_norm && gemm_norm_fits(r.g_qkv);
   r.norm_gu = m.gemm_norm && gemm_norm_fits(r.g_gu);
   r.norm_head = m.gemm_norm && gemm_norm_fits(r.g_head);
+  r.defer = tc && m.defer_resid && !r.norm_qkv && !r.norm_gu && !r.norm_head;
+  if (r.defer) {  // the residual-norm kernel sums at most 8 partials per element
+    r.g_o.splits = std::min(r.g_o.splits, 8);
+    r.g_down.splits = std::min(r.g_down.splits, 8);
+    r.defer = residual_norm_fits(r.g_o.splits, c.hidden) && residual_norm_fits(r.g_down.splits, c.hidden);
+  }
   r.gemv = !r.chain && !r.stream &&
            use_gemv(m, M, rows_out, &r.v_qkv, &r.v_o, &r.v_gu, &r.v_down, &r.v_head, &r.gemv_head);
+  r.defer = r.defer && !r.gemv && !r.stream && !r.chain;
   r.ap = r.stream ? plan_attention_decode(B, c.n_kv_heads, max_kv_len, r.grid)
                   : plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len, tc && c.head_dim == 64);
   // The two ticket-counter regions sit at fixed offsets so that they stay zero across calls
@@ -152,6 +163,9 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   for (const GemmShape* s : {&r.g_qkv, &r.g_o, &r.g_gu, &r.g_down, &r.g_head}) gws = std::max(gws, gemm_partials_bytes(*s));
   r.gemm_parts = off; off += align256(gws);
   r.attn_parts = off; off += align256(attention_partials_bytes(r.ap, B, c.n_kv_heads, c.head_dim));
+  r.resid_parts = off;
+  if (r.defer)
+    off += align256(static_cast<size_t>(std::max(r.g_o.splits, r.g_down.splits)) * M * c.hidden * sizeof(float));
   r.stream_parts = off;
   if (r.stream) {
     const int max_tiles = std::max({(m.qkv_n + 127) / 128, (c.hidden + 127) / 128, (2 * c.intermediate + 127) / 128,
@@ -249,6 +263,7 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
   T* act = reinterpret_cast<T*>(ws + cv.act);
   int32_t* pos = reinterpret_cast<int32_t*>(ws + cv.pos);
   int32_t* slot = reinterpret_cast<int32_t*>(ws + cv.slot);
+  float* resid_parts = reinterpret_cast<float*>(ws + cv.resid_parts);
   GemmScratch gscr{reinterpret_cast<int*>(ws + cv.gemm_counters), reinterpret_cast<float*>(ws + cv.gemm_parts)};
   int* attn_counters = reinterpret_cast<int*>(ws + cv.attn_counters);
   float* attn_parts = reinterpret_cast<float*>(ws + cv.attn_parts);
@@ -329,10 +344,16 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
   for (int l = 0; l < c.n_layers; ++l) {
     const specb200_layer_weights& L = m.layers[l];
     const LayerMaps* mp = tc ? &m.maps[l] : nullptr;
-    if (!cv.gemv && !cv.norm_qkv &&
-        (rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.attn_norm), M, c.hidden, c.rms_eps, xbuf, nullptr, 1, s,
-                                pdl)))
+    if (cv.defer && l > 0) {  // the previous layer's down projection joins the residual stream here
+      rc = launch_residual_norm(reinterpret_cast<__nv_bfloat16*>(hidden), resid_parts, cv.g_down.splits, M, M, c.hidden,
+                                static_cast<const __nv_bfloat16*>(L.attn_norm), c.rms_eps,
+                                reinterpret_cast<__nv_bfloat16*>(xbuf), nullptr, 1, s, pdl);
+      if (rc) return rc;
+    } else if (!cv.gemv && !cv.norm_qkv &&
+               (rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.attn_norm), M, c.hidden, c.rms_eps, xbuf, nullptr,
+                                       1, s, pdl))) {
       return rc;
+    }
     Epilogue eq = {};
     eq.op = EPI_QKV;
     eq.out = qbuf;
@@ -379,13 +400,23 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     er.op = EPI_RESID;
     er.out = hidden;
     er.ldo = c.hidden;
+    Epilogue ep = {};  // deferred: partials for launch_residual_norm
+    ep.op = EPI_PARTIAL;
+    ep.out = resid_parts;
+    ep.ldo = c.hidden;
     rc = cv.gemv ? gemv(cv.v_o, L.w_o, attn, nullptr, er, c.hidden, qd)
-                 : gemm(cv.g_o, mp ? &mp->o : nullptr, &x_attn, L.w_o, attn, er);
+                 : gemm(cv.g_o, mp ? &mp->o : nullptr, &x_attn, L.w_o, attn, cv.defer ? ep : er);
     if (rc) return rc;
-    if (!cv.gemv && !cv.norm_gu &&
-        (rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.mlp_norm), M, c.hidden, c.rms_eps, xbuf, nullptr, 1, s,
-                                pdl)))
+    if (cv.defer) {
+      rc = launch_residual_norm(reinterpret_cast<__nv_bfloat16*>(hidden), resid_parts, cv.g_o.splits, M, M, c.hidden,
+                                static_cast<const __nv_bfloat16*>(L.mlp_norm), c.rms_eps,
+                                reinterpret_cast<__nv_bfloat16*>(xbuf), nullptr, 1, s, pdl);
+      if (rc) return rc;
+    } else if (!cv.gemv && !cv.norm_gu &&
+               (rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(L.mlp_norm), M, c.hidden, c.rms_eps, xbuf, nullptr,
+                                       1, s, pdl))) {
       return rc;
+    }
     Epilogue eg = {};
     eg.op = EPI_SILU_MUL;
     eg.out = act;
@@ -394,7 +425,7 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
                  : gemm(cv.g_gu, mp ? &mp->gu : nullptr, &x_hidden, L.w_gate_up, xbuf, eg, cv.norm_gu ? L.mlp_norm : nullptr);
     if (rc) return rc;
     rc = cv.gemv ? gemv(cv.v_down, L.w_down, act, nullptr, er, c.hidden, c.intermediate)
-                 : gemm(cv.g_down, mp ? &mp->down : nullptr, &x_act, L.w_down, act, er);
+                 : gemm(cv.g_down, mp ? &mp->down : nullptr, &x_act, L.w_down, act, cv.defer ? ep : er);
     if (rc) return rc;
   }
   return run_head<T>(m, bt, ws, cv, s, tc ? &x_final : nullptr);
@@ -446,8 +477,16 @@ int run_head(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv
     nrm.eps = c.rms_eps;
     return launch_gemm_tc(cv.g_head, m.head, *x_final, eh, gscr, bt.status, s, true, &nrm);
   }
-  int rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(m.w.final_norm), rows_out, c.hidden, c.rms_eps, xbuf,
-                             bt.last_only ? bt.n_new : nullptr, bt.T, s, true);
+  int rc;
+  if (cv.defer) {  // the last layer's down projection joins the residual stream with the final norm
+    rc = launch_residual_norm(reinterpret_cast<__nv_bfloat16*>(hidden), reinterpret_cast<const float*>(ws + cv.resid_parts),
+                              cv.g_down.splits, bt.B * bt.T, rows_out, c.hidden,
+                              static_cast<const __nv_bfloat16*>(m.w.final_norm), c.rms_eps,
+                              reinterpret_cast<__nv_bfloat16*>(xbuf), bt.last_only ? bt.n_new : nullptr, bt.T, s, true);
+  } else {
+    rc = launch_rmsnorm<T>(hidden, static_cast<const T*>(m.w.final_norm), rows_out, c.hidden, c.rms_eps, xbuf,
+                           bt.last_only ? bt.n_new : nullptr, bt.T, s, true);
+  }
   if (rc) return rc;
   if (c.dtype == SPECB200_BF16) return launch_gemm_tc(cv.g_head, m.head, *x_final, eh, gscr, bt.status, s, true);
   return launch_gemm_simt<T>(cv.g_head, static_cast<const T*>(m.w.lm_head), xbuf, eh, gscr, bt.status, s, true);
@@ -573,6 +612,7 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
   // operand build and its 64 KB of shared memory (which keeps the attention CTAs off the SMs
   // while the q/k/v GEMM runs) cost more than the norm launches (1.66 vs 1.58 ms per verify).
   m->gemm_norm = c.dtype == SPECB200_BF16 && env_int("SPECB200_GEMM_NORM", 0) == 1;
+  m->defer_resid = env_int("SPECB200_DEFER_RESID", 1) == 1;
   // Decode-step GEMV schedule: bf16 weights, 16-byte aligned rows (SPECB200_GEMV=0 turns it off).
   auto al16 = [](const void* p) { return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   m->gemv_ok = c.dtype == SPECB200_BF16 && env_int("SPECB200_GEMV", 1) == 1 && al16(weights->lm_head) &&

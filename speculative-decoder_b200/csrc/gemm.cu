@@ -41,6 +41,13 @@ __device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, 
     }
   };
   const int valid = min(s.BN, s.M - m0);
+  if (e.op == EPI_PARTIAL) {  // every split stores its own partial: no ticket, no reduction here
+    float* out = static_cast<float*>(e.out) + static_cast<size_t>(split) * s.M * s.N;
+    const int n = n0 + t;
+    if (n < s.N)
+      for (int tok = 0; tok < valid; ++tok) out[static_cast<size_t>(m0 + tok) * s.N + n] = tile[tok * kEpiPitch + t];
+    return;
+  }
   if (s.splits > 1) {
     int* counters = scratch.counters;
     float* parts = scratch.partials;

@@ -9,6 +9,8 @@ enum EpilogueOp : int {
   EPI_RESID = 1,     // out[m, n] = round(out[m, n] + round(acc)): `hidden + proj(x)` in the model dtype
   EPI_SILU_MUL = 2,  // tile rows 0-63 gate, 64-127 up: out[m, n/2 + j] = round(round(silu(round(g))) * round(u))
   EPI_QKV = 3,       // rows of q_proj | k_proj | v_proj: RoPE on q and k, q to out, k and v to the paged pool
+  EPI_PARTIAL = 4,   // out (fp32) [split][M][N] = this K split's partial sums; the residual add is
+                     // deferred to the following RMSNorm launch (launch_residual_norm)
 };
 
 struct Epilogue {

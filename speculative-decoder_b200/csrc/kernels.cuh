@@ -38,6 +38,12 @@ template <typename T>
 int launch_prep_embed(const PrepArgs& a, const T* embed, T* hidden, cudaStream_t s, bool pdl);
 // Function attributes of the prep / RMSNorm kernels; call outside any stream capture.
 bool norm_prepare();
+// Residual update of an EPI_PARTIAL GEMM (parts [splits][M][H] fp32) into h, then RMSNorm of
+// `rows` rows into y (with the last-token selection when sel_n_new is given).
+int launch_residual_norm(__nv_bfloat16* h, const float* parts, int splits, int M, int rows, int H,
+                         const __nv_bfloat16* w, float eps, __nv_bfloat16* y, const int32_t* sel_n_new, int T_tokens,
+                         cudaStream_t s, bool pdl);
+bool residual_norm_fits(int splits, int H);
 template <typename T>
 int launch_rmsnorm(const T* x, const T* w, int rows, int H, float eps, T* y, const int32_t* sel_n_new, int T_tokens,
                    cudaStream_t s, bool pdl);

@@ -171,13 +171,92 @@ __global__ void __launch_bounds__(kNormThreads)
   }
 }
 
+// The residual update deferred by an EPI_PARTIAL GEMM, then RMSNorm: for each output row
+//   h = round(h + round(sum over splits of the partials, in split order))   (EPI_RESID's rounding)
+//   y = w * round(h * rsqrt(mean(h^2) + eps))                              (rmsnorm_kernel's)
+// with h written back to the residual stream. One CTA per row, 8 elements per thread in
+// registers (H <= 8 * kNormThreads); all partial loads of a thread are in flight together.
+constexpr int kResidMaxSplits = 8;
+
+__global__ void __launch_bounds__(kNormThreads)
+    residual_norm_kernel(__nv_bfloat16* __restrict__ h, const float* __restrict__ parts, int splits, int M, int H,
+                         const __nv_bfloat16* __restrict__ w, float eps, __nv_bfloat16* __restrict__ y,
+                         const int32_t* __restrict__ sel_n_new, int T_tokens) {
+  pdl_launch_dependents();
+  const int row = blockIdx.x, tid = threadIdx.x;
+  const int c = tid;  // 8-element chunk of the row
+  const bool live = c * 8 < H;
+  uint4 wv = live ? __ldg(reinterpret_cast<const uint4*>(w) + c) : make_uint4(0, 0, 0, 0);
+  pdl_wait();
+  const int64_t src = sel_n_new ? static_cast<int64_t>(row) * T_tokens + max(sel_n_new[row] - 1, 0) : row;
+  float hv[8];
+  float ss = 0.f;
+  if (live) {
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.f;
+    float4 pv[kResidMaxSplits][2];
+#pragma unroll
+    for (int sp = 0; sp < kResidMaxSplits; ++sp) {
+      if (sp < splits) {
+        const float4* p = reinterpret_cast<const float4*>(parts + (static_cast<size_t>(sp) * M + src) * H) + 2 * c;
+        pv[sp][0] = __ldcg(p);
+        pv[sp][1] = __ldcg(p + 1);
+      }
+    }
+    const uint4 hb = __ldcg(reinterpret_cast<const uint4*>(h + src * H) + c);
+#pragma unroll
+    for (int sp = 0; sp < kResidMaxSplits; ++sp) {
+      if (sp < splits) {
+        acc[0] += pv[sp][0].x; acc[1] += pv[sp][0].y; acc[2] += pv[sp][0].z; acc[3] += pv[sp][0].w;
+        acc[4] += pv[sp][1].x; acc[5] += pv[sp][1].y; acc[6] += pv[sp][1].z; acc[7] += pv[sp][1].w;
+      }
+    }
+    float hf[8];
+    unpack_chunk<__nv_bfloat16>(hb, hf);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      hv[e] = round_to<__nv_bfloat16>(hf[e] + round_to<__nv_bfloat16>(acc[e]));
+      ss = fmaf(hv[e], hv[e], ss);
+    }
+    reinterpret_cast<uint4*>(h + src * H)[c] = pack_chunk<__nv_bfloat16>(hv);
+  }
+  __shared__ float sh[kNormThreads / 32];
+  ss = warp_sum(ss);
+  if ((tid & 31) == 0) sh[tid >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int i = 0; i < kNormThreads / 32; ++i) t += sh[i];
+  const float r = 1.0f / sqrtf(t / static_cast<float>(H) + eps);
+  if (live) {
+    float g[8];
+    unpack_chunk<__nv_bfloat16>(wv, g);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) hv[e] = g[e] * round_to<__nv_bfloat16>(hv[e] * r);
+    reinterpret_cast<uint4*>(y + static_cast<int64_t>(row) * H)[c] = pack_chunk<__nv_bfloat16>(hv);
+  }
+}
+
+int launch_residual_norm(__nv_bfloat16* h, const float* parts, int splits, int M, int rows, int H,
+                         const __nv_bfloat16* w, float eps, __nv_bfloat16* y, const int32_t* sel_n_new, int T_tokens,
+                         cudaStream_t s, bool pdl) {
+  if (splits < 1 || splits > kResidMaxSplits || H % 8 != 0 || H > 8 * kNormThreads) return SPECB200_ERR_UNSUPPORTED;
+  const cudaError_t e = launch_kernel(residual_norm_kernel, dim3(rows), dim3(kNormThreads), 0, s, pdl, h, parts, splits, M,
+                                      H, w, eps, y, sel_n_new, T_tokens);
+  return e == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
+}
+
+bool residual_norm_fits(int splits, int H) { return splits >= 1 && splits <= kResidMaxSplits && H % 8 == 0 && H <= 8 * kNormThreads; }
+
 bool norm_prepare() {
   // the largest carveout, as every kernel of a forward, so that consecutive kernels share SMs
   bool ok = true;
   for (const void* f : {reinterpret_cast<const void*>(rmsnorm_kernel<float>),
                         reinterpret_cast<const void*>(rmsnorm_kernel<__nv_bfloat16>),
                         reinterpret_cast<const void*>(prep_embed_kernel<float>),
-                        reinterpret_cast<const void*>(prep_embed_kernel<__nv_bfloat16>)})
+                        reinterpret_cast<const void*>(prep_embed_kernel<__nv_bfloat16>),
+                        reinterpret_cast<const void*>(residual_norm_kernel)})
     ok = ok && cudaFuncSetAttribute(f, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared) ==
                    cudaSuccess;
   return ok;
