@@ -50,7 +50,16 @@ __global__ void __launch_bounds__(kAcThreads) attention_cluster_kernel(AttnKerne
   attention_cluster_cta(ka, blockIdx.z, blockIdx.y, ac_smem, true);
 }
 
+// Decode steps of small models: attention of every KV head of a sequence in one cluster
+// (P CTAs per head), then the o projection with the residual add (FuseO).
+__global__ void __launch_bounds__(kAcThreads) attention_o_kernel(AttnKernelArgs ka, FuseO fo) {
+  extern __shared__ __align__(16) uint8_t ac_smem[];
+  pdl_launch_dependents();
+  attention_cluster_cta(ka, blockIdx.y, 0, ac_smem, true, &fo);
+}
+
 constexpr int kAcSmemLimit = 200 * 1024;
+constexpr int kAoMaxCluster = 16;  // non-portable cluster size
 
 cudaError_t launch_cluster(const AttnArgs& a, const AttnPlan& p, cudaStream_t s, bool pdl) {
   AttnKernelArgs ka;
@@ -96,9 +105,13 @@ bool attention_prepare() {
   static bool ok = false;
   std::call_once(once, [] {
     ok = cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAcSmemLimit) ==
-         cudaSuccess;
+             cudaSuccess &&
+         cudaFuncSetAttribute(attention_o_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAcSmemLimit) ==
+             cudaSuccess &&
+         cudaFuncSetAttribute(attention_o_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
     // the largest carveout, as every kernel of a forward, so that consecutive kernels share SMs
     for (const void* f : {reinterpret_cast<const void*>(attention_cluster_kernel),
+                          reinterpret_cast<const void*>(attention_o_kernel),
                           reinterpret_cast<const void*>(attention_mma_kernel),
                           reinterpret_cast<const void*>(attention_kernel<float, 16>),
                           reinterpret_cast<const void*>(attention_kernel<float, 32>),
@@ -140,8 +153,62 @@ AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len, bool tens
   return p;
 }
 
+bool plan_attention_o(int B, int T, int Hq, int Hkv, int D, int H, int max_kv_len, AttnPlan* p, int* P, int* rows) {
+  if (D != 64 || Hq % Hkv || T * (Hq / Hkv) > kAcRowsMax || Hkv > kAoMaxCluster || !attention_prepare()) return false;
+  // Opt-in (SPECB200_ATTN_O=1): the 15-CTA clusters cannot be placed while the q/k/v GEMV
+  // holds the SMs, so they lose the early key and weight loads: 0.605 vs 0.573 ms per draft step.
+  static const bool on = [] {
+    const char* v = std::getenv("SPECB200_ATTN_O");
+    return v && *v == '1';
+  }();
+  if (!on) return false;
+  const int len = std::max(1, max_kv_len);
+  const int per = std::max(1, std::min(kAoMaxCluster / Hkv, (len + 63) / 64));
+  const int chunk = ((len + per - 1) / per + 7) / 8 * 8;
+  if (chunk > kAcMaxChunk) return false;
+  const int C = Hkv * per;
+  const int r = (H + C - 1) / C;
+  if (ac_layout(chunk, T * (Hq / Hkv), per, 1, T, Hq, r).total > kAcSmemLimit || (Hq * D * 2) % 16) return false;
+  p->qtiles = 1;
+  p->splits_max = C;
+  p->chunk = chunk;
+  p->mma = 3;
+  *P = per;
+  *rows = r;
+  return true;
+}
+
+int launch_attention_o(const AttnArgs& a, const AttnPlan& p, int P, int rows, const __nv_bfloat16* w_o,
+                       __nv_bfloat16* hidden, int H, cudaStream_t s, bool pdl) {
+  if (p.mma != 3 || a.D != 64 || (reinterpret_cast<uintptr_t>(w_o) & 15)) return SPECB200_ERR_UNSUPPORTED;
+  AttnKernelArgs ka;
+  ka.a = a;
+  ka.p = p;
+  ka.counters = nullptr;
+  ka.part = nullptr;
+  FuseO fo{w_o, hidden, H, P, rows};
+  const int R = a.T * (a.Hq / a.Hkv);
+  const AcLayout lay = ac_layout(p.chunk, R, P, a.bs, a.T, a.Hq, rows);
+  if (lay.total > kAcSmemLimit) return SPECB200_ERR_UNSUPPORTED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.splits_max, a.B, 1);
+  cfg.blockDim = dim3(kAcThreads);
+  cfg.dynamicSmemBytes = lay.total;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.splits_max;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, attention_o_kernel, ka, fo) == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
+}
+
 size_t attention_partials_bytes(const AttnPlan& p, int B, int Hkv, int D) {
-  if (p.mma == 2) return 0;  // the cluster kernel merges in distributed shared memory
+  if (p.mma >= 2) return 0;  // the cluster kernels merge in distributed shared memory
   const size_t groups = static_cast<size_t>(B) * Hkv * p.qtiles;
   return p.splits_max > 1 ? groups * p.splits_max * kRows * (D + 2) * sizeof(float) : 0;
 }

@@ -24,18 +24,33 @@ constexpr int kAcMaxCluster = 8;
 constexpr int kAcMaxChunk = 512;  // keys per CTA
 constexpr int kAcRowsMax = 16;
 
-// Dynamic shared memory of the cluster kernel for chunk keys per CTA, R query rows and C CTAs.
-struct AcLayout {
-  int kv, scratch, slots, tab, total;  // byte offsets (q rows at 0), total size
+// The o projection fused behind the attention (decode steps of small models): one cluster per
+// sequence covers every KV head (P CTAs per head); after the heads' merges every CTA holds the
+// whole attention output and computes `rows` rows of o = W_o attn with the residual add.
+struct FuseO {
+  const __nv_bfloat16* w;  // [H, Hq d] row-major
+  __nv_bfloat16* hidden;   // residual stream [B T, H]
+  int H;
+  int P;     // CTAs per KV head
+  int rows;  // o rows per CTA
 };
-__host__ __device__ inline AcLayout ac_layout(int chunk, int R, int C, int bs) {
+
+// Dynamic shared memory of the cluster kernel for chunk keys per CTA, R query rows, S merge
+// slots (CTAs per head) and, when fused, T tokens of Hq heads and `orows` o rows of K = Hq d.
+struct AcLayout {
+  int kv, scratch, slots, tab, attn, wo, bar, total;  // byte offsets (q rows at 0), total size
+};
+__host__ __device__ inline AcLayout ac_layout(int chunk, int R, int S, int bs, int T = 0, int Hq = 0, int orows = 0) {
   AcLayout L;
   const int region = chunk * 256 > kAcWarps * (R * 64 + 32) * 4 ? chunk * 256 : kAcWarps * (R * 64 + 32) * 4;
   L.kv = 2048;
   L.scratch = L.kv;  // the K / V region is reused by the warp merge once the products are done
   L.slots = L.kv + ((region + 127) / 128) * 128;
-  L.tab = L.slots + C * (R * 64 + 32) * 4;
-  L.total = L.tab + ((chunk + bs - 1) / bs + 2) * 4 + 128;
+  L.tab = L.slots + S * (R * 64 + 32) * 4;
+  L.attn = L.tab + (((chunk + bs - 1) / bs + 2) * 4 + 127) / 128 * 128;
+  L.wo = L.attn + (T * Hq * 64 * 2 + 127) / 128 * 128;
+  L.bar = L.wo + orows * Hq * 64 * 2;
+  L.total = L.bar + 16 + 128;
   return L;
 }
 
@@ -115,17 +130,26 @@ SPECB200_DEVINL void ac_merge_warps(const AmState& st, float* scratch, int R, fl
   __syncthreads();
 }
 
-// One CTA of the cluster for (sequence b, KV head g): keys [rank * chunk, ...) of the row.
-// With `pdl` the cached keys are loaded before griddepcontrol.wait.
-static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, int g, uint8_t* smem, bool pdl) {
+// One CTA of the cluster for (sequence b, KV head g): keys [part * chunk, ...) of the row. Without
+// `fo` the cluster is one KV head (part = rank) and its first CTA writes the output; with `fo`
+// the cluster is every KV head of the sequence (g = rank / P, part = rank % P), each head's first
+// CTA sends the head's output to every CTA, and each CTA computes its o rows.
+// With `pdl` the cached keys (and the o weights) are loaded before griddepcontrol.wait.
+static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, int g, uint8_t* smem, bool pdl,
+                                             const FuseO* fo = nullptr) {
   const AttnArgs& a = ka.a;
   constexpr int D = 64;
-  const int C = ka.p.splits_max, chunk = ka.p.chunk;
+  const int chunk = ka.p.chunk;
   const int G = a.Hq / a.Hkv;
   const int R = a.T * G;
   const int rank = static_cast<int>(ac_rank());
+  const int P = fo ? fo->P : ka.p.splits_max;  // CTAs per KV head
+  if (fo) g = rank / P;
+  const int part = fo ? rank % P : rank;
+  const int lead = rank - part;  // the head's first CTA
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const AcLayout lay = ac_layout(chunk, R, C, a.bs);
+  const int K = a.Hq * D;  // o projection inputs
+  const AcLayout lay = fo ? ac_layout(chunk, R, P, a.bs, a.T, a.Hq, fo->rows) : ac_layout(chunk, R, P, a.bs);
   unsigned long long* tr = nullptr;  // optional record (AttnArgs::trace), thread 0
   if (a.trace && tid == 0) {
     const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
@@ -143,8 +167,27 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
   if (nn <= 0) return;  // the same for every CTA of the cluster: none of them synchronises
   ac_cluster_arrive_relaxed();
   const int kmax = min(total, past + (R - 1) / G + 1);
-  const int kbeg = min(kmax, rank * chunk);
+  const int kbeg = min(kmax, part * chunk);
   const int kend = min(kmax, kbeg + chunk);
+  // fused o projection: this CTA's weight rows [o0, o1) by one bulk copy, before the wait
+  const int o0 = fo ? min(fo->H, rank * fo->rows) : 0, o1 = fo ? min(fo->H, o0 + fo->rows) : 0;
+  uint64_t* obar = reinterpret_cast<uint64_t*>(smem + lay.bar);
+  __nv_bfloat16* wo_s = reinterpret_cast<__nv_bfloat16*>(smem + lay.wo);
+  __nv_bfloat16* attn_s = reinterpret_cast<__nv_bfloat16*>(smem + lay.attn);  // [T][Hq d]
+  if (fo && tid == 0) {
+    mbar_init(obar, 1);
+    fence_mbar_init();
+    if (o1 > o0) {
+      const uint32_t bytes = static_cast<uint32_t>(o1 - o0) * K * 2;
+      mbar_arrive_expect_tx(obar, bytes);
+      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       smem_u32(wo_s)),
+                   "l"(reinterpret_cast<uint64_t>(fo->w + static_cast<int64_t>(o0) * K)), "r"(bytes), "r"(smem_u32(obar))
+                   : "memory");
+    } else {
+      mbar_arrive(obar);
+    }
+  }
   __nv_bfloat16* q_s = reinterpret_cast<__nv_bfloat16*>(smem);
   __nv_bfloat16* k_s = reinterpret_cast<__nv_bfloat16*>(smem + lay.kv);
   __nv_bfloat16* v_s = k_s + chunk * 64;
@@ -208,34 +251,81 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
   float* scratch = reinterpret_cast<float*>(smem + lay.scratch);
   float* slots = reinterpret_cast<float*>(smem + lay.slots);  // [C][R * 64 + 32] in the first CTA
   // This CTA's merged partial, [R][64] o then m at R * 64 and l at R * 64 + 16: built in its
-  // own slot `rank`, then (other CTAs) copied to the same slot of the first CTA.
+  // own slot `part`, then (other CTAs) copied to the same slot of the head's first CTA.
   const int slot_floats = R * 64 + 32;
-  float* mo = slots + rank * slot_floats;
+  float* mo = slots + part * slot_floats;
   ac_merge_warps(st, scratch, R, mo, mo + R * 64, mo + R * 64 + 16);
   stamp(4);
   ac_cluster_wait();
-  if (rank != 0) {
-    const uint32_t dst = ac_mapa(smem_u32(slots + rank * slot_floats), 0);
+  if (part != 0) {
+    const uint32_t dst = ac_mapa(smem_u32(slots + part * slot_floats), lead);
     for (int i = tid; i < slot_floats; i += kAcThreads) ac_st_remote(dst + 4 * i, mo[i]);
   }
   ac_cluster_sync();
   stamp(5);
-  if (rank != 0) return;
-  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
-  for (int i = tid; i < R * D; i += kAcThreads) {
-    const int r = i >> 6, c = i & 63;
-    float M = -INFINITY;
-    for (int cr = 0; cr < C; ++cr) M = fmaxf(M, slots[cr * slot_floats + R * 64 + r]);
-    float O = 0.f, L = 0.f;
-    for (int cr = 0; cr < C; ++cr) {
-      const float* sp = slots + cr * slot_floats;
-      const float ms = sp[R * 64 + r];
-      const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
-      O = fmaf(sp[i], w, O);
-      L = fmaf(sp[R * 64 + 16 + r], w, L);
+  if (part == 0) {
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
+    const int nc = fo ? static_cast<int>(gridDim.x) : 1;  // CTAs that receive the head's output
+    for (int i = tid; i < R * D; i += kAcThreads) {
+      const int r = i >> 6, c = i & 63;
+      float M = -INFINITY;
+      for (int cr = 0; cr < P; ++cr) M = fmaxf(M, slots[cr * slot_floats + R * 64 + r]);
+      float O = 0.f, L = 0.f;
+      for (int cr = 0; cr < P; ++cr) {
+        const float* sp = slots + cr * slot_floats;
+        const float ms = sp[R * 64 + r];
+        const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - M);
+        O = fmaf(sp[i], w, O);
+        L = fmaf(sp[R * 64 + 16 + r], w, L);
+      }
+      const int t = r / G, h = g * G + r % G;
+      const __nv_bfloat16 v = __float2bfloat16_rn(O / L);
+      if (!fo) {
+        out[(static_cast<int64_t>(b * a.T + t) * a.Hq + h) * D + c] = v;
+      } else {
+        const uint32_t off = smem_u32(attn_s + t * K + h * D + c);
+        for (int cr = 0; cr < nc; ++cr)
+          asm volatile("st.shared::cluster.u16 [%0], %1;" ::"r"(ac_mapa(off, cr)), "h"(__bfloat16_as_ushort(v)) : "memory");
+      }
     }
-    const int t = r / G, h = g * G + r % G;
-    out[(static_cast<int64_t>(b * a.T + t) * a.Hq + h) * D + c] = __float2bfloat16_rn(O / L);
+  }
+  if (!fo) {
+    stamp(6);
+    return;
+  }
+  ac_cluster_sync();  // every CTA holds the attention output of all heads
+  // o = W_o attn for rows [o0, o1) and the residual add (the GEMM's EPI_RESID rounding)
+  if (!mbar_wait_bounded(obar, 0, a.status, nullptr)) return;
+  const uint4* a4 = reinterpret_cast<const uint4*>(attn_s);
+  const int nch = K >> 3;
+  for (int n = o0 + warp; n < o1; n += kAcWarps) {
+    const uint4* wr = reinterpret_cast<const uint4*>(wo_s + static_cast<int64_t>(n - o0) * K);
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int ch = lane; ch < nch; ch += 32) {
+      const uint4 wv = wr[ch];
+      const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        if (t >= a.T) break;
+        const uint4 xv = a4[t * nch + ch];
+        const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          acc[t] = fmaf(__uint_as_float(wu[q] << 16), __uint_as_float(xu[q] << 16), acc[t]);
+          acc[t] = fmaf(__uint_as_float(wu[q] & 0xffff0000u), __uint_as_float(xu[q] & 0xffff0000u), acc[t]);
+        }
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < 4; ++t) acc[t] = warp_sum(acc[t]);
+    if (lane < a.T) {
+      float v = acc[0];
+#pragma unroll
+      for (int t = 1; t < 4; ++t)
+        if (lane == t) v = acc[t];
+      __nv_bfloat16* hp = fo->hidden + static_cast<int64_t>(b * a.T + lane) * fo->H + n;
+      *hp = __float2bfloat16_rn(__bfloat162float(*hp) + round_to<__nv_bfloat16>(v));
+    }
   }
   stamp(6);
 }

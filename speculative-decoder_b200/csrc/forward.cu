@@ -92,6 +92,9 @@ struct Carve {
   GemmShape g_qkv, g_o, g_gu, g_down, g_head;
   bool gemv;  // decode-step schedule: the per-layer order with GEMV kernels and fused norms
   bool gemv_head;  // ... and the LM head as a GEMV with the final norm folded in
+  bool attn_o;     // ... and attention + o projection as one cluster kernel per sequence
+  AttnPlan ap_o;
+  int ao_P, ao_rows;
   bool norm_qkv, norm_gu, norm_head;  // per-layer schedule: norm folded into these GEMMs
   GemvPlan v_qkv, v_o, v_gu, v_down, v_head;
   AttnPlan ap;
@@ -144,6 +147,8 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   r.gemv = !r.chain && !r.stream &&
            use_gemv(m, M, rows_out, &r.v_qkv, &r.v_o, &r.v_gu, &r.v_down, &r.v_head, &r.gemv_head);
   r.defer = r.defer && !r.gemv && !r.stream && !r.chain;
+  r.attn_o = r.gemv && plan_attention_o(B, T, c.n_heads, c.n_kv_heads, c.head_dim, c.hidden, max_kv_len, &r.ap_o,
+                                        &r.ao_P, &r.ao_rows);
   r.ap = r.stream ? plan_attention_decode(B, c.n_kv_heads, max_kv_len, r.grid)
                   : plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len, tc && c.head_dim == 64);
   // The two ticket-counter regions sit at fixed offsets so that they stay zero across calls
@@ -394,7 +399,13 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
                  static_cast<size_t>(4 * c.n_layers + 1) * (cv.gemv ? kGemvTraceCtas * kGemvTraceStamps : kGemmTraceCtas * 8);
       aa.trace_slot = l;
     }
-    if ((rc = launch_attention<T>(aa, cv.ap, attn_counters, attn_parts, s, pdl))) return rc;
+    if (cv.attn_o) {  // attention and the o projection with the residual add, one launch
+      rc = launch_attention_o(aa, cv.ap_o, cv.ao_P, cv.ao_rows, static_cast<const __nv_bfloat16*>(L.w_o),
+                              reinterpret_cast<__nv_bfloat16*>(hidden), c.hidden, s, pdl);
+      if (rc) return rc;
+    } else if ((rc = launch_attention<T>(aa, cv.ap, attn_counters, attn_parts, s, pdl))) {
+      return rc;
+    }
 
     Epilogue er = {};
     er.op = EPI_RESID;
@@ -404,9 +415,13 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     ep.op = EPI_PARTIAL;
     ep.out = resid_parts;
     ep.ldo = c.hidden;
-    rc = cv.gemv ? gemv(cv.v_o, L.w_o, attn, nullptr, er, c.hidden, qd)
-                 : gemm(cv.g_o, mp ? &mp->o : nullptr, &x_attn, L.w_o, attn, cv.defer ? ep : er);
-    if (rc) return rc;
+    if (!cv.attn_o) {
+      rc = cv.gemv ? gemv(cv.v_o, L.w_o, attn, nullptr, er, c.hidden, qd)
+                   : gemm(cv.g_o, mp ? &mp->o : nullptr, &x_attn, L.w_o, attn, cv.defer ? ep : er);
+      if (rc) return rc;
+    } else {
+      ++gemv_slot;  // keep the trace slots of the remaining launches in place
+    }
     if (cv.defer) {
       rc = launch_residual_norm(reinterpret_cast<__nv_bfloat16*>(hidden), resid_parts, cv.g_o.splits, M, M, c.hidden,
                                 static_cast<const __nv_bfloat16*>(L.mlp_norm), c.rms_eps,
@@ -660,8 +675,13 @@ extern "C" int specb200_forward_launches(void* model, int B, int T) {
   const int M = B * T;
   const bool tc = m.cfg.dtype == SPECB200_BF16;
   const bool head_norm = m.gemm_norm && gemm_norm_fits(plan_gemm(B, m.cfg.vocab, m.cfg.hidden, tc));
-  if (use_gemv(m, M, B, &v[0], &v[1], &v[2], &v[3], &v[4], &head_gemv))
-    return (head_gemv || head_norm ? 2 : 3) + 5 * m.cfg.n_layers;
+  if (use_gemv(m, M, B, &v[0], &v[1], &v[2], &v[3], &v[4], &head_gemv)) {
+    AttnPlan ap;
+    int P = 0, rows = 0;  // counted for contexts up to 1024 keys
+    const specb200_model_config& c = m.cfg;
+    const bool ao = plan_attention_o(B, T, c.n_heads, c.n_kv_heads, c.head_dim, c.hidden, 1024, &ap, &P, &rows);
+    return (head_gemv || head_norm ? 2 : 3) + (ao ? 4 : 5) * m.cfg.n_layers;
+  }
   const int norms = (m.gemm_norm && gemm_norm_fits(plan_gemm(M, m.qkv_n, m.cfg.hidden, tc)) ? 0 : 1) +
                     (m.gemm_norm && gemm_norm_fits(plan_gemm(M, 2 * m.cfg.intermediate, m.cfg.hidden, tc)) ? 0 : 1);
   return 2 + (head_norm ? 0 : 1) + (5 + norms) * m.cfg.n_layers;

@@ -84,6 +84,12 @@ struct AttnPlan {
 };
 // Sets the cluster kernel's shared-memory limit; call outside any stream capture.
 bool attention_prepare();
+// Attention of every KV head of a sequence in one cluster followed by the o projection and the
+// residual add into hidden (decode steps of small bf16 models, d = 64). Plans P CTAs per KV
+// head and `rows` o rows per CTA; false when the shape does not fit.
+bool plan_attention_o(int B, int T, int Hq, int Hkv, int D, int H, int max_kv_len, AttnPlan* p, int* P, int* rows);
+int launch_attention_o(const AttnArgs& a, const AttnPlan& p, int P, int rows, const __nv_bfloat16* w_o,
+                       __nv_bfloat16* hidden, int H, cudaStream_t s, bool pdl);
 // tensor_items: the call is bf16 with d = 64, so decode / verify shapes (T x G <= 16) may use
 // the tensor-core items (attn_item_mma.cuh).
 AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len, bool tensor_items);

@@ -422,6 +422,38 @@ def test_gemv_schedule_matches_oracle(dims):
             assert np.abs(g - o).max() <= 2e-2 * scale + 1e-3, (b, np.abs(g - o).max(), scale)
 
 
+def test_attention_o_kernel_matches_separate_launches():
+    """The opt-in fused attention + o projection (one cluster of P CTAs per KV head per
+    sequence, SPECB200_ATTN_O=1, read once per process) against the separate cluster attention
+    and o GEMV, in a child process: 1- and 2-token steps of the 135M draft width."""
+    import subprocess
+    import sys
+    import textwrap
+    code = textwrap.dedent('''
+        import os, sys, torch
+        sys.path[:0] = ["tests", "speculative-decoder_b200", "."]
+        from test_gpu_forward import _bf16_model, _gemv_steps
+        from specb200.engine import Engine
+        model = _bf16_model(576, 2, 9, 3, 1536, 49152, seed=31, theta=100000.0).to("cuda")
+        fused = Engine(model)
+        assert fused.launches(1, 1) == 3 + 4 * 2, fused.launches(1, 1)
+        (la, ca) = _gemv_steps(fused, model)
+        os.environ["SPECB200_GEMV"] = "0"
+        ref = Engine(model)
+        (lb, cb) = _gemv_steps(ref, model)
+        for a, b in zip(la, lb):
+            scale = a.abs().max().item()
+            assert (a - b).abs().max().item() <= 1e-2 * scale, ((a - b).abs().max().item(), scale)
+        for pa, pb in ((ca.k, cb.k), (ca.v, cb.v)):
+            d = (pa.float() - pb.float()).abs().max().item()
+            assert d <= 2 ** -7 * pa.float().abs().max().item(), d
+        print("ok")
+    ''')
+    env = dict(__import__("os").environ, SPECB200_ATTN_O="1")
+    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=600)
+    assert res.returncode == 0 and "ok" in res.stdout, res.stdout + res.stderr
+
+
 @pytest.mark.parametrize("dims", [(2048, 2, 32, 32, 8192, 49152), (576, 2, 9, 3, 1536, 49152)])
 def test_gemm_norm_matches_separate_norm(monkeypatch, dims):
     """Verify-sized calls (5 and 2 x 4 ragged tokens, all rows and last rows only) on three
