@@ -23,6 +23,7 @@ constexpr int kAcWarps = kAcThreads / 32;
 constexpr int kAcMaxCluster = 8;
 constexpr int kAcMaxChunk = 512;  // keys per CTA
 constexpr int kAcRowsMax = 16;
+constexpr int kQkvMaxSplits = 4;  // q/k/v partials summed by the attention (AttnArgs::qkv_parts)
 
 // The o projection fused behind the attention (decode steps of small models): one cluster per
 // sequence covers every KV head (P CTAs per head); after the heads' merges every CTA holds the
@@ -220,19 +221,108 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
   }
   if (pdl) pdl_wait();
   stamp(1);
-  // query rows (zero past R) and this call's keys
-  const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(a.q);
-  for (int i = tid; i < 16 * 8; i += kAcThreads) {
-    const int r = i >> 3, c8 = i & 7;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < R) {
-      const int t = r / G, h = g * G + r % G;
-      v = *reinterpret_cast<const uint4*>(q + (static_cast<int64_t>(b * a.T + t) * a.Hq + h) * D + c8 * 8);
+  if (a.qkv_parts) {
+    // q rows and the new keys / values from the q/k/v GEMM's partials: pair (c, c + 32) of a
+    // head, summed over splits in order, rounded, rotated (q and k) as EPI_QKV does. Two pairs
+    // per thread per pass with every partial load of the pass in flight together.
+    using T16 = __nv_bfloat16;
+    const int qd = a.Hq * D, kd = a.Hkv * D;
+    const int nq = R * 32;        // (query row, pair)
+    const int nkv = a.T * 2 * 32;  // (new token, k or v, pair)
+    for (int i = tid; i < (16 - R) * 64; i += kAcThreads)  // query rows past R are zero
+      q_s[am_swz(R + i / 64, i % 64)] = __float2bfloat16_rn(0.f);
+    for (int i0 = 0; i0 < nq + nkv; i0 += 2 * kAcThreads) {
+      int col[2], t[2], c[2], r[2];
+      bool live[2], isq[2], isv[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int i = i0 + u * kAcThreads + tid;
+        live[u] = i < nq + nkv;
+        isq[u] = i < nq;
+        isv[u] = false;
+        r[u] = 0;
+        if (isq[u]) {
+          r[u] = i >> 5;
+          c[u] = i & 31;
+          t[u] = r[u] / G;
+          col[u] = (g * G + r[u] % G) * D + c[u];
+        } else {
+          const int k = i - nq;
+          t[u] = k >> 6;
+          isv[u] = (k >> 5) & 1;
+          c[u] = k & 31;
+          col[u] = (isv[u] ? qd + kd : qd) + g * D + c[u];
+          live[u] = live[u] && t[u] < nn;  // padding tokens have no key
+        }
+      }
+      float v[kQkvMaxSplits][2][2];
+#pragma unroll
+      for (int sp = 0; sp < kQkvMaxSplits; ++sp)
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          v[sp][u][0] = v[sp][u][1] = 0.f;
+          if (sp < a.qkv_splits && live[u]) {
+            const float* row =
+                a.qkv_parts + (static_cast<int64_t>(sp) * a.B * a.T + static_cast<int64_t>(b) * a.T + t[u]) * a.qkv_n;
+            v[sp][u][0] = __ldcg(row + col[u]);
+            v[sp][u][1] = __ldcg(row + col[u] + 32);
+          }
+        }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (!live[u]) continue;
+        float lo = 0.f, hi = 0.f;
+#pragma unroll
+        for (int sp = 0; sp < kQkvMaxSplits; ++sp)
+          if (sp < a.qkv_splits) {
+            lo += v[sp][u][0];
+            hi += v[sp][u][1];
+          }
+        lo = round_to<T16>(lo);
+        hi = round_to<T16>(hi);
+        if (!isv[u]) {  // q and k rotate
+          const int pos = min(past + t[u], a.max_positions - 1);
+          const float cs = round_to<T16>(a.rope_cos[static_cast<int64_t>(pos) * 32 + c[u]]);
+          const float sn = round_to<T16>(a.rope_sin[static_cast<int64_t>(pos) * 32 + c[u]]);
+          const float lo2 = round_to<T16>(round_to<T16>(lo * cs) + round_to<T16>(-hi * sn));
+          const float hi2 = round_to<T16>(round_to<T16>(hi * cs) + round_to<T16>(lo * sn));
+          lo = lo2;
+          hi = hi2;
+        }
+        if (isq[u]) {
+          q_s[am_swz(r[u], c[u])] = __float2bfloat16_rn(lo);
+          q_s[am_swz(r[u], c[u] + 32)] = __float2bfloat16_rn(hi);
+          continue;
+        }
+        const int kk = past + t[u];  // key index of the new token
+        if (kk >= kbeg && kk < kend) {
+          __nv_bfloat16* dst = isv[u] ? v_s : k_s;
+          dst[am_swz(kk - kbeg, c[u])] = __float2bfloat16_rn(lo);
+          dst[am_swz(kk - kbeg, c[u] + 32)] = __float2bfloat16_rn(hi);
+        }
+        if (part == 0) {  // the new key / value into the pool, once per cluster
+          const int64_t sl = static_cast<int64_t>(table[kk / a.bs]) * a.bs + kk % a.bs;
+          __nv_bfloat16* pool = const_cast<__nv_bfloat16*>(isv[u] ? vp : kp) + (sl * a.Hkv + g) * D;
+          pool[c[u]] = __float2bfloat16_rn(lo);
+          pool[c[u] + 32] = __float2bfloat16_rn(hi);
+        }
+      }
     }
-    *reinterpret_cast<uint4*>(q_s + am_swz(r, c8 * 8)) = v;
+  } else {
+    // query rows (zero past R) and this call's keys
+    const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(a.q);
+    for (int i = tid; i < 16 * 8; i += kAcThreads) {
+      const int r = i >> 3, c8 = i & 7;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (r < R) {
+        const int t = r / G, h = g * G + r % G;
+        v = *reinterpret_cast<const uint4*>(q + (static_cast<int64_t>(b * a.T + t) * a.Hq + h) * D + c8 * 8);
+      }
+      *reinterpret_cast<uint4*>(q_s + am_swz(r, c8 * 8)) = v;
+    }
+    load_keys(split_at, kend);
+    cp_async_commit();
   }
-  load_keys(split_at, kend);
-  cp_async_commit();
   cp_async_wait<0>();
   __syncthreads();
   stamp(2);

@@ -12,6 +12,7 @@
 #include <cstdlib>
 #include <vector>
 
+#include "attn_cluster.cuh"
 #include "attn_core.cuh"
 #include "gemm.cuh"
 #include "gemv.cuh"
@@ -44,6 +45,7 @@ struct Model {
   bool gemv_ok = false;  // bf16 weights usable by the decode-step GEMV kernels (gemv.cu)
   bool gemm_norm = false;  // RMSNorms folded into the tensor-core GEMMs that consume them
   bool defer_resid = true;  // residual adds of the o / down GEMMs deferred to the next RMSNorm
+  bool defer_qkv = true;    // q/k/v GEMM partials summed by the cluster attention
 };
 
 // Whether a call of this shape runs the cluster layer-chain kernel (small models, decode
@@ -80,10 +82,13 @@ size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 struct Carve {
   size_t gemm_counters, attn_counters, stream_ctl, hidden, xbuf, qbuf, attn, act, pos, slot, gemm_parts, attn_parts,
-      stream_parts, resid_parts, total;
+      stream_parts, resid_parts, qkv_parts, total;
   // per-layer schedule: the o and down GEMMs store split partials (EPI_PARTIAL) and the RMSNorm
   // launch that follows each adds them to the residual stream (launch_residual_norm)
   bool defer;
+  // ... and the q/k/v GEMM stores split partials that the cluster attention sums, rotates and
+  // writes to the pool itself (no ticket, no epilogue tail in the GEMM)
+  bool defer_qkv;
   bool stream, chain;
   int grid, max_contrib;
   ChainPhase cph[4];
@@ -151,6 +156,7 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
                                         &r.ao_P, &r.ao_rows);
   r.ap = r.stream ? plan_attention_decode(B, c.n_kv_heads, max_kv_len, r.grid)
                   : plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len, tc && c.head_dim == 64);
+  r.defer_qkv = r.defer && r.ap.mma == 2 && c.head_dim == 64 && m.defer_qkv && r.g_qkv.splits <= kQkvMaxSplits;
   // The two ticket-counter regions sit at fixed offsets so that they stay zero across calls
   // of every shape; everything after them is rewritten before it is read.
   size_t off = 0;
@@ -171,6 +177,8 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   r.resid_parts = off;
   if (r.defer)
     off += align256(static_cast<size_t>(std::max(r.g_o.splits, r.g_down.splits)) * M * c.hidden * sizeof(float));
+  r.qkv_parts = off;
+  if (r.defer_qkv) off += align256(static_cast<size_t>(r.g_qkv.splits) * M * m.qkv_n * sizeof(float));
   r.stream_parts = off;
   if (r.stream) {
     const int max_tiles = std::max({(m.qkv_n + 127) / 128, (c.hidden + 127) / 128, (2 * c.intermediate + 127) / 128,
@@ -372,8 +380,12 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     eq.n_heads = c.n_heads;
     eq.n_kv_heads = c.n_kv_heads;
     eq.head_dim = c.head_dim;
+    Epilogue eqp = {};  // deferred: partials for the cluster attention
+    eqp.op = EPI_PARTIAL;
+    eqp.out = ws + cv.qkv_parts;
+    eqp.ldo = m.qkv_n;
     rc = cv.gemv ? gemv(cv.v_qkv, L.w_qkv, hidden, L.attn_norm, eq, m.qkv_n, c.hidden)
-                 : gemm(cv.g_qkv, mp ? &mp->qkv : nullptr, &x_hidden, L.w_qkv, xbuf, eq,
+                 : gemm(cv.g_qkv, mp ? &mp->qkv : nullptr, &x_hidden, L.w_qkv, xbuf, cv.defer_qkv ? eqp : eq,
                         cv.norm_qkv ? L.attn_norm : nullptr);
     if (rc) return rc;
 
@@ -394,6 +406,14 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     aa.scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
     aa.out = attn;
     aa.status = status;
+    if (cv.defer_qkv) {
+      aa.qkv_parts = reinterpret_cast<const float*>(ws + cv.qkv_parts);
+      aa.qkv_splits = cv.g_qkv.splits;
+      aa.qkv_n = m.qkv_n;
+      aa.rope_cos = m.w.rope_cos;
+      aa.rope_sin = m.w.rope_sin;
+      aa.max_positions = c.max_positions;
+    }
     if (bt.trace) {  // after the GEMV or GEMM launch records
       aa.trace = reinterpret_cast<unsigned long long*>(bt.trace) +
                  static_cast<size_t>(4 * c.n_layers + 1) * (cv.gemv ? kGemvTraceCtas * kGemvTraceStamps : kGemmTraceCtas * 8);
@@ -628,6 +648,7 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
   // while the q/k/v GEMM runs) cost more than the norm launches (1.66 vs 1.58 ms per verify).
   m->gemm_norm = c.dtype == SPECB200_BF16 && env_int("SPECB200_GEMM_NORM", 0) == 1;
   m->defer_resid = env_int("SPECB200_DEFER_RESID", 1) == 1;
+  m->defer_qkv = env_int("SPECB200_DEFER_QKV", 1) == 1;
   // Decode-step GEMV schedule: bf16 weights, 16-byte aligned rows (SPECB200_GEMV=0 turns it off).
   auto al16 = [](const void* p) { return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   m->gemv_ok = c.dtype == SPECB200_BF16 && env_int("SPECB200_GEMV", 1) == 1 && al16(weights->lm_head) &&

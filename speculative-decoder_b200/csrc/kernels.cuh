@@ -67,6 +67,15 @@ struct AttnArgs {
   // warps merged, cluster merged, end (first CTA).
   unsigned long long* trace = nullptr;
   int trace_slot = 0;
+  // Optional (cluster kernel): q and the new keys / values come from the q/k/v GEMM's split
+  // partials [qkv_splits][B T][qkv_n] (EPI_PARTIAL) instead of q and the pool; the kernel sums
+  // them in split order, applies the EPI_QKV rounding and RoPE, and the first CTA of each
+  // cluster writes the new keys and values to the pool.
+  const float* qkv_parts = nullptr;
+  int qkv_splits = 0, qkv_n = 0;
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
+  int max_positions = 0;
 };
 
 constexpr int kAttnTraceCtas = 512;  // CTAs per launch in an attention trace record

@@ -456,11 +456,13 @@ def test_attention_o_kernel_matches_separate_launches():
 
 @pytest.mark.parametrize("dims", [(2048, 2, 32, 32, 8192, 49152), (576, 2, 9, 3, 1536, 49152)])
 def test_gemm_norm_matches_separate_norm(monkeypatch, dims):
-    """Verify-sized calls (5 and 2 x 4 ragged tokens, all rows and last rows only) on three
+    """Verify-sized calls (5 and 2 x 4 ragged tokens, all rows and last rows only) on four
     per-layer variants: separate RMSNorm launches after residual-add epilogues; the o and down
-    GEMMs storing split partials that the next RMSNorm launch adds to the residual stream (the
-    default); and the RMSNorms folded into the GEMMs. Same roundings, sums in other orders, so
-    logits agree to bf16 noise; the folded schedule makes 2 + 5 L launches."""
+    GEMMs storing split partials that the next RMSNorm launch adds to the residual stream; that
+    plus the q/k/v GEMM storing partials that the cluster attention sums, rotates and writes to
+    the pool (the default); and the RMSNorms folded into the GEMMs. Same roundings, sums in
+    other orders, so logits and the pools agree to bf16 noise; the folded schedule makes
+    2 + 5 L launches."""
     from cache.kv import KVCache
     from specb200.engine import Engine
 
@@ -470,13 +472,16 @@ def test_gemm_norm_matches_separate_norm(monkeypatch, dims):
     monkeypatch.setenv("SPECB200_DEFER_RESID", "0")
     separate = Engine(model)
     monkeypatch.setenv("SPECB200_DEFER_RESID", "1")
+    monkeypatch.setenv("SPECB200_DEFER_QKV", "0")
     deferred = Engine(model)  # o / down partials summed into the residual by the next norm launch
+    monkeypatch.setenv("SPECB200_DEFER_QKV", "1")
+    deferred_qkv = Engine(model)  # ... and q/k/v partials summed, rotated and stored by the attention
     monkeypatch.setenv("SPECB200_GEMM_NORM", "1")
     fused = Engine(model)
     assert separate.launches(1, 5) == 3 + 7 * 2 and fused.launches(1, 5) == 2 + 5 * 2
-    assert deferred.launches(1, 5) == 3 + 7 * 2
-    outs = []
-    for eng in (separate, deferred, fused):
+    assert deferred.launches(1, 5) == 3 + 7 * 2 and deferred_qkv.launches(1, 5) == 3 + 7 * 2
+    outs, caches = [], []
+    for eng in (separate, deferred, deferred_qkv, fused):
         cache = KVCache.for_model(model.config, num_blocks=96, block_size=16, dtype=torch.bfloat16, device=DEV)
         for s in range(2):
             cache.add(s)
@@ -486,6 +491,7 @@ def test_gemm_norm_matches_separate_norm(monkeypatch, dims):
                  eng.forward(cache, [0, 1], torch.tensor([[10, 11, 12, 13], [14, 15, 16, 0]]), [4, 3], last_only=True),
                  eng.forward(cache, [1], torch.tensor([[17, 18, 19, 20, 21]]), [5], last_only=True)]
         outs.append([x.float().cpu() for x in steps])
+        caches.append(cache)
     for other in outs[1:]:
         for a, b in zip(outs[0], other):
             scale = a.abs().max().item()
@@ -493,3 +499,7 @@ def test_gemm_norm_matches_separate_norm(monkeypatch, dims):
             top2 = a.topk(2, dim=-1).values
             agree = a.argmax(-1) == b.argmax(-1)
             assert bool((agree | ((top2[..., 0] - top2[..., 1]) < 1e-2 * scale)).all())
+    for other in caches[1:]:  # the keys and values every variant wrote to the pool
+        for pa, pb in ((caches[0].k, other.k), (caches[0].v, other.v)):
+            d = (pa.float() - pb.float()).abs().max().item()
+            assert d <= 2 ** -7 * pa.float().abs().max().item(), d
