@@ -53,7 +53,7 @@ ACCEPT_BYTES = 113_246_208            # config 3: 64 x (5 + 4) x 49152 x 4 B
 # kernels 1.0427 GB (profiles/traffic_verify_step_1p7b_6layers_perlayer.txt), layer-stream
 # kernel 1.0426 GB (profiles/stream_kernel_verify_1p7b_6layers.txt). Traffic grows with the
 # layers streamed, so the full-size figure scales by the same ratio.
-VERIFY_TRAFFIC_RATIO = {"layers": (1_042_289_664 + 449_536) / 1_038_340_096,
+VERIFY_TRAFFIC_RATIO = {"layers": (1_046_855_168 + 181_760) / 1_038_340_096,
                         "stream": (1_038_322_000 + 4_316_416) / 1_038_340_096}
 
 
