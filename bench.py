@@ -35,7 +35,8 @@ import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
-sys.path[:0] = [str(ROOT), str(ROOT / "speculative-decoder_b200")]
+# the package directory first: its `bench` package (the latency harness) must win over this file
+sys.path[:0] = [str(ROOT / "speculative-decoder_b200"), str(ROOT)]
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
@@ -511,6 +512,33 @@ def time_accept(device, reps: int = 20) -> dict:
     return {"us": statistics.median(times) * 1e3, "bytes": ACCEPT_BYTES}
 
 
+def request_latency(target, draft, prompts, device, blocks: int, repeats: int = 3) -> dict:
+    """TTFT / TPOT / end-to-end of whole generate() requests through the latency harness
+    (bench.harness.measure with CUDA syncs at the loop's events, bench.latency.summarize): p50
+    over `repeats` requests, after the timed region."""
+    from bench.harness import measure, synchronizer
+    from bench.latency import summarize
+    from cache.kv import KVCache
+    from spec.draft import ModelDraft
+    from spec.loop import generate
+
+    def request(watch) -> int:
+        cache = KVCache.for_model(target.config, num_blocks=blocks, block_size=BLOCK, dtype=torch.bfloat16, device=device)
+        dcache = KVCache.for_model(draft.config, num_blocks=blocks, block_size=BLOCK, dtype=torch.bfloat16,
+                                   device=device)
+        out, _ = generate(target, cache, ModelDraft(draft, dcache), prompts, NEW_TOKENS, k=K, on_event=watch.mark)
+        return sum(len(o) for o in out)
+
+    s = summarize(measure({"spec_draft": request}, warmup=0, repeats=repeats, sync=synchronizer(device), seed=0))
+    s = s["spec_draft"]
+    p50 = lambda d: d["p50"] if d else None  # noqa: E731
+    return {"requests": s["n"], "tokens_per_request": p50(s["tokens"]), "ttft_ms": p50(s["ttft_ms"]),
+            "ttft_first_round_ms": p50(s["ttft_first_round_ms"]), "draft_prefill_ms": p50(s["draft_prefill_ms"]),
+            "tpot_ms": p50(s["tpot_ms"]), "tpot_first_round_ms": p50(s["tpot_first_round_ms"]),
+            "e2e_ms": p50(s["e2e_ms"]),
+            "source": "bench.harness.measure + bench.latency.summarize (p50; device synced at each event)"}
+
+
 def cpu_baseline(target, draft, prompt: list[int], engine_rounds: int | None, max_rounds: int = 2) -> dict:
     """The CPU oracle (numpy restatement of the reference path, oracle/) on this host: target
     and draft prefill, first token and `max_rounds` rounds of config 2; tokens/s is then
@@ -672,6 +700,7 @@ def main() -> None:
 
     vstep = time_verify_step(target, KVCache, device, PROMPT_LEN + NEW_TOKENS // 2)
     acc = time_accept(device)
+    latency = request_latency(target, draft, prompts, device, blocks)
     pk = peaks()
     achieved = vstep["bytes"] / (vstep["us"] * 1e-6) / 1e9
     acc_gbs = acc["bytes"] / (acc["us"] * 1e-6) / 1e9
@@ -707,6 +736,7 @@ def main() -> None:
                      "algorithmic_bytes": vstep["bytes"], "context_tokens": vstep["context"]},
         "accept": {"us": acc["us"], "achieved": acc_gbs, "frac": acc_gbs / pk["hbm_gbs"], "unit": "GB/s",
                    "algorithmic_bytes": acc["bytes"], "config": "B=64, k=4, V=49152 fp32 logits, T=1"},
+        "latency": latency,
         "acceptance": alpha, "rounds_per_step": rounds / args.steps,
         "gpu_launches": launches,
         "clocks": clocks.summary(),
