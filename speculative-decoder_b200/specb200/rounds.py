@@ -185,12 +185,22 @@ class FusedRound:
 
     def run(self) -> tuple[list[int], list[int], list[list[int]]]:
         if self.graph is None:
+            main = torch.cuda.current_stream(self.dev)
             side = torch.cuda.Stream(self.dev)
-            side.wait_stream(torch.cuda.current_stream(self.dev))
+            side.wait_stream(main)
             g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=side):
-                self._launch()
-            torch.cuda.current_stream(self.dev).wait_stream(side)
+            # Captured with capture_begin/capture_end rather than the torch.cuda.graph() context:
+            # that context first returns every cached device block and every cached pinned host
+            # block to the driver, so each generate() call would re-allocate its KV pools and
+            # pinned round buffers through cudaMalloc / cudaHostAlloc, which on B200 hosts
+            # sporadically stalls a request for 60-570 ms.
+            with torch.cuda.stream(side):
+                g.capture_begin()
+                try:
+                    self._launch()
+                finally:
+                    g.capture_end()
+            main.wait_stream(side)
             self.graph = g
         self.graph.replay()
         torch.cuda.current_stream(self.dev).synchronize()
