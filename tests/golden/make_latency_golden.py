@@ -95,4 +95,6 @@ def main(ref: str) -> None:
 
 
 if __name__ == "__main__":
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_latency_golden.py /path/to/speculative-decoder")
     main(sys.argv[1])
