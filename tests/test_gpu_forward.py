@@ -148,6 +148,22 @@ def test_fused_path_is_taken_for_engine_drafters(tiny, monkeypatch):
     assert calls == [1] and len(out[0]) == 8
 
 
+def test_fused_round_keeps_the_allocator_caches(tiny, monkeypatch):
+    """Capturing the round's graph must not return cached device or pinned host blocks to the
+    driver: re-allocating them for every request stalled requests for hundreds of ms."""
+    from spec.loop import generate
+    from spec.ngram import NGramDraft
+
+    calls = []
+    dev_empty, host_empty = torch.cuda.empty_cache, torch._C._host_emptyCache
+    monkeypatch.setattr(torch.cuda, "empty_cache", lambda: calls.append("device") or dev_empty())
+    monkeypatch.setattr(torch._C, "_host_emptyCache", lambda: calls.append("host") or host_empty())
+    for _ in range(2):
+        out, _ = generate(tiny, new_cache(tiny), NGramDraft(256), [[4, 8, 15, 16, 23, 42, 4, 8]], 10, k=3)
+        assert len(out[0]) == 10
+    assert calls == []
+
+
 def test_plain_decode_matches_reference(tiny, golden_generate):
     from baselines import cached_autoregressive
 
