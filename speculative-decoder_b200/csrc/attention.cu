@@ -58,6 +58,14 @@ __global__ void __launch_bounds__(kAcThreads) attention_o_kernel(AttnKernelArgs 
   attention_cluster_cta(ka, blockIdx.y, 0, ac_smem, true, &fo);
 }
 
+// Decode steps of small models: each KV head's q/k/v projection computed by its own cluster in
+// front of the attention (FuseQKV).
+__global__ void __launch_bounds__(kAcThreads) attention_qkv_kernel(AttnKernelArgs ka, FuseQKV fq) {
+  extern __shared__ __align__(16) uint8_t ac_smem[];
+  pdl_launch_dependents();
+  attention_cluster_cta(ka, blockIdx.z, blockIdx.y, ac_smem, true, nullptr, &fq);
+}
+
 constexpr int kAcSmemLimit = 200 * 1024;
 constexpr int kAoMaxCluster = 16;  // non-portable cluster size
 
@@ -108,10 +116,13 @@ bool attention_prepare() {
              cudaSuccess &&
          cudaFuncSetAttribute(attention_o_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAcSmemLimit) ==
              cudaSuccess &&
-         cudaFuncSetAttribute(attention_o_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
+         cudaFuncSetAttribute(attention_o_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
+         cudaFuncSetAttribute(attention_qkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAcSmemLimit) ==
+             cudaSuccess;
     // the largest carveout, as every kernel of a forward, so that consecutive kernels share SMs
     for (const void* f : {reinterpret_cast<const void*>(attention_cluster_kernel),
                           reinterpret_cast<const void*>(attention_o_kernel),
+                          reinterpret_cast<const void*>(attention_qkv_kernel),
                           reinterpret_cast<const void*>(attention_mma_kernel),
                           reinterpret_cast<const void*>(attention_kernel<float, 16>),
                           reinterpret_cast<const void*>(attention_kernel<float, 32>),
@@ -205,6 +216,58 @@ int launch_attention_o(const AttnArgs& a, const AttnPlan& p, int P, int rows, co
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, attention_o_kernel, ka, fo) == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
+}
+
+bool plan_attention_qkv(int T, int Hq, int Hkv, int D, int H, int max_kv_len, AttnPlan* p, int* pairs) {
+  if (D != 64 || Hkv <= 0 || Hq % Hkv || T < 1 || T > kAcQkvMaxT || T * (Hq / Hkv) > kAcRowsMax || H % 8 ||
+      H > kAcThreads * 8 * kAcQkvChunks || !attention_prepare())
+    return false;
+  // Always the largest cluster: the head's weight rows spread over 8 CTAs (46 KB each for the
+  // 135M draft) and 8 warps per CTA share the products; CTAs past the keys only compute rows.
+  const int G = Hq / Hkv, C = kAcMaxCluster, len = std::max(1, max_kv_len);
+  const int chunk = ((len + C - 1) / C + 7) / 8 * 8;
+  if (chunk > kAcMaxChunk) return false;
+  const int pr = ((G + 2) * 32 + C - 1) / C;
+  if (ac_qkv_layout(ac_layout(chunk, T * G, C, 1).total, T, H, pr).total > kAcSmemLimit) return false;
+  p->qtiles = 1;
+  p->splits_max = C;
+  p->chunk = chunk;
+  p->mma = 4;
+  *pairs = pr;
+  return true;
+}
+
+int launch_attention_qkv(const AttnArgs& a, const AttnPlan& p, int pairs, const __nv_bfloat16* w_qkv,
+                         const __nv_bfloat16* x, const __nv_bfloat16* norm_w, const int32_t* slot, float eps, int H,
+                         cudaStream_t s, bool pdl) {
+  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
+  if (p.mma != 4 || a.D != 64 || a.T > kAcQkvMaxT || H % 8 || !al16(w_qkv) || !al16(x) || !al16(norm_w) || !slot ||
+      !a.rope_cos || !a.rope_sin || a.max_positions <= 0 || pairs * p.splits_max < (a.Hq / a.Hkv + 2) * 32)
+    return SPECB200_ERR_UNSUPPORTED;
+  AttnKernelArgs ka;
+  ka.a = a;
+  ka.p = p;
+  ka.counters = nullptr;
+  ka.part = nullptr;
+  FuseQKV fq{w_qkv, x, norm_w, slot, eps, H, pairs};
+  const int R = a.T * (a.Hq / a.Hkv);
+  const AcQkvLayout ql = ac_qkv_layout(ac_layout(p.chunk, R, p.splits_max, a.bs).total, a.T, H, pairs);
+  if (ql.total > kAcSmemLimit) return SPECB200_ERR_UNSUPPORTED;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.splits_max, a.Hkv, a.B);
+  cfg.blockDim = dim3(kAcThreads);
+  cfg.dynamicSmemBytes = ql.total;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.splits_max;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, attention_qkv_kernel, ka, fq) == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
 }
 
 size_t attention_partials_bytes(const AttnPlan& p, int B, int Hkv, int D) {

@@ -46,6 +46,7 @@ struct Model {
   bool gemm_norm = false;  // RMSNorms folded into the tensor-core GEMMs that consume them
   bool defer_resid = true;  // residual adds of the o / down GEMMs deferred to the next RMSNorm
   bool defer_qkv = true;    // q/k/v GEMM partials summed by the cluster attention
+  bool qkv_attn = false;    // GEMV schedule: each KV head's q/k/v projection inside its attention cluster
 };
 
 // Whether a call of this shape runs the cluster layer-chain kernel (small models, decode
@@ -100,6 +101,9 @@ struct Carve {
   bool attn_o;     // ... and attention + o projection as one cluster kernel per sequence
   AttnPlan ap_o;
   int ao_P, ao_rows;
+  bool qkv_attn;   // ... or the q/k/v projection inside the attention clusters
+  AttnPlan ap_qkv;
+  int qkv_pairs;
   bool norm_qkv, norm_gu, norm_head;  // per-layer schedule: norm folded into these GEMMs
   GemvPlan v_qkv, v_o, v_gu, v_down, v_head;
   AttnPlan ap;
@@ -154,6 +158,8 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   r.defer = r.defer && !r.gemv && !r.stream && !r.chain;
   r.attn_o = r.gemv && plan_attention_o(B, T, c.n_heads, c.n_kv_heads, c.head_dim, c.hidden, max_kv_len, &r.ap_o,
                                         &r.ao_P, &r.ao_rows);
+  r.qkv_attn = r.gemv && !r.attn_o && m.qkv_attn &&
+               plan_attention_qkv(T, c.n_heads, c.n_kv_heads, c.head_dim, c.hidden, max_kv_len, &r.ap_qkv, &r.qkv_pairs);
   r.ap = r.stream ? plan_attention_decode(B, c.n_kv_heads, max_kv_len, r.grid)
                   : plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len, tc && c.head_dim == 64);
   r.defer_qkv = r.defer && r.ap.mma == 2 && c.head_dim == 64 && m.defer_qkv && r.g_qkv.splits <= kQkvMaxSplits;
@@ -384,10 +390,14 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     eqp.op = EPI_PARTIAL;
     eqp.out = ws + cv.qkv_parts;
     eqp.ldo = m.qkv_n;
-    rc = cv.gemv ? gemv(cv.v_qkv, L.w_qkv, hidden, L.attn_norm, eq, m.qkv_n, c.hidden)
-                 : gemm(cv.g_qkv, mp ? &mp->qkv : nullptr, &x_hidden, L.w_qkv, xbuf, cv.defer_qkv ? eqp : eq,
-                        cv.norm_qkv ? L.attn_norm : nullptr);
-    if (rc) return rc;
+    if (cv.qkv_attn) {
+      ++gemv_slot;  // computed by the attention clusters; keep the trace slots in place
+    } else {
+      rc = cv.gemv ? gemv(cv.v_qkv, L.w_qkv, hidden, L.attn_norm, eq, m.qkv_n, c.hidden)
+                   : gemm(cv.g_qkv, mp ? &mp->qkv : nullptr, &x_hidden, L.w_qkv, xbuf, cv.defer_qkv ? eqp : eq,
+                          cv.norm_qkv ? L.attn_norm : nullptr);
+      if (rc) return rc;
+    }
 
     AttnArgs aa;
     aa.q = qbuf;
@@ -419,7 +429,15 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
                  static_cast<size_t>(4 * c.n_layers + 1) * (cv.gemv ? kGemvTraceCtas * kGemvTraceStamps : kGemmTraceCtas * 8);
       aa.trace_slot = l;
     }
-    if (cv.attn_o) {  // attention and the o projection with the residual add, one launch
+    if (cv.qkv_attn) {  // the q/k/v projection and the attention, one launch
+      aa.rope_cos = m.w.rope_cos;
+      aa.rope_sin = m.w.rope_sin;
+      aa.max_positions = c.max_positions;
+      rc = launch_attention_qkv(aa, cv.ap_qkv, cv.qkv_pairs, static_cast<const __nv_bfloat16*>(L.w_qkv),
+                                reinterpret_cast<const __nv_bfloat16*>(hidden),
+                                static_cast<const __nv_bfloat16*>(L.attn_norm), slot, c.rms_eps, c.hidden, s, pdl);
+      if (rc) return rc;
+    } else if (cv.attn_o) {  // attention and the o projection with the residual add, one launch
       rc = launch_attention_o(aa, cv.ap_o, cv.ao_P, cv.ao_rows, static_cast<const __nv_bfloat16*>(L.w_o),
                               reinterpret_cast<__nv_bfloat16*>(hidden), c.hidden, s, pdl);
       if (rc) return rc;
@@ -649,6 +667,11 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
   m->gemm_norm = c.dtype == SPECB200_BF16 && env_int("SPECB200_GEMM_NORM", 0) == 1;
   m->defer_resid = env_int("SPECB200_DEFER_RESID", 1) == 1;
   m->defer_qkv = env_int("SPECB200_DEFER_QKV", 1) == 1;
+  // q/k/v projection inside the attention clusters of the GEMV schedule: opt-in
+  // (SPECB200_DRAFT_QKV=1). One launch fewer per layer, but 0.608 vs 0.578 ms per 1-token
+  // draft step of the 135M model: its 80 KB CTAs do not fit beside the down GEMV's, so the
+  // clusters start late and lose the early weight and key loads.
+  m->qkv_attn = env_int("SPECB200_DRAFT_QKV", 0) == 1;
   // Decode-step GEMV schedule: bf16 weights, 16-byte aligned rows (SPECB200_GEMV=0 turns it off).
   auto al16 = [](const void* p) { return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   m->gemv_ok = c.dtype == SPECB200_BF16 && env_int("SPECB200_GEMV", 1) == 1 && al16(weights->lm_head) &&
@@ -679,7 +702,8 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
 }
 
 // Kernel launches of one forward call: 3 for the layer chain (chain kernel, final norm, LM head),
-// 1 for the layer stream, 2 + 5 L for the GEMV schedule (prep, 5 per layer, head), and for the
+// 1 for the layer stream, 2 + 5 L for the GEMV schedule (prep, 5 per layer, head; 4 per layer
+// when the o or the q/k/v projection runs inside the attention clusters), and for the
 // per-layer kernels 2 + 5 L (prep, 5 per layer, head) plus one launch per RMSNorm that is not
 // folded into its GEMM (at most 3 + 7 L).
 extern "C" int specb200_forward_launches(void* model, int B, int T) {
@@ -701,7 +725,8 @@ extern "C" int specb200_forward_launches(void* model, int B, int T) {
     int P = 0, rows = 0;  // counted for contexts up to 1024 keys
     const specb200_model_config& c = m.cfg;
     const bool ao = plan_attention_o(B, T, c.n_heads, c.n_kv_heads, c.head_dim, c.hidden, 1024, &ap, &P, &rows);
-    return (head_gemv || head_norm ? 2 : 3) + (ao ? 4 : 5) * m.cfg.n_layers;
+    const bool fq = !ao && m.qkv_attn && plan_attention_qkv(T, c.n_heads, c.n_kv_heads, c.head_dim, c.hidden, 1024, &ap, &P);
+    return (head_gemv || head_norm ? 2 : 3) + (ao || fq ? 4 : 5) * m.cfg.n_layers;
   }
   const int norms = (m.gemm_norm && gemm_norm_fits(plan_gemm(M, m.qkv_n, m.cfg.hidden, tc)) ? 0 : 1) +
                     (m.gemm_norm && gemm_norm_fits(plan_gemm(M, 2 * m.cfg.intermediate, m.cfg.hidden, tc)) ? 0 : 1);

@@ -409,6 +409,33 @@ def test_gemv_schedule_matches_per_layer_kernels(monkeypatch, dims):
         assert d <= 2 ** -7 * pa.float().abs().max().item(), d
 
 
+@pytest.mark.parametrize("dims", [(576, 2, 9, 3, 1536, 49152), (256, 2, 4, 4, 512, 49152)])
+def test_qkv_in_attention_clusters_matches_gemv_schedule(monkeypatch, dims):
+    """SPECB200_DRAFT_QKV=1: each KV head's attention cluster computes its own q/k/v rows (one
+    launch fewer per layer) against the separate q/k/v GEMV on identical inputs. The norm is
+    the same; only the dot products' summation order differs, so logits agree to bf16 noise
+    and the KV entries the calls wrote to one bf16 ulp of their scale."""
+    from specb200.engine import Engine
+
+    model = _bf16_model(*dims, seed=21, theta=100000.0).to(DEV)
+    gemv = Engine(model)
+    monkeypatch.setenv("SPECB200_DRAFT_QKV", "1")
+    fused = Engine(model)
+    head_launches = 1 if dims[-1] <= 4096 else 2
+    assert fused.schedule(1, 1) == "gemv" and gemv.launches(1, 1) == 1 + head_launches + 5 * 2
+    assert fused.launches(1, 1) == 1 + head_launches + 4 * 2
+    (la, ca), (lb, cb) = _gemv_steps(gemv, model), _gemv_steps(fused, model)
+    for a, b in zip(la, lb):
+        scale = a.abs().max().item()
+        assert (a - b).abs().max().item() <= 1e-2 * scale, ((a - b).abs().max().item(), scale)
+        top2 = a.topk(2, dim=-1).values
+        agree = a.argmax(-1) == b.argmax(-1)
+        assert bool((agree | ((top2[..., 0] - top2[..., 1]) < 1e-2 * scale)).all())
+    for pa, pb in ((ca.k, cb.k), (ca.v, cb.v)):
+        d = (pa.float() - pb.float()).abs().max().item()
+        assert d <= 2 ** -7 * pa.float().abs().max().item(), d
+
+
 @pytest.mark.parametrize("dims", [(576, 2, 9, 3, 1536, 49152), (128, 2, 4, 2, 256, 512)])
 def test_gemv_schedule_matches_oracle(dims):
     """The GEMV schedule against the bf16 oracle: after a prefill, 1-token steps of one and of
