@@ -183,6 +183,48 @@ def test_batched_plain_decode_matches_one_at_a_time(tiny, golden_generate):
     assert cache.allocator.num_used == 0 and not cache.tables
 
 
+def test_eos_stops_mid_window(tiny, golden_generate, path):
+    """With eos set to a token the reference emits partway through a request, the request
+    ends right after its first occurrence, inside a verify window (the reference's
+    tests/test_greedy_identity.py:76-82)."""
+    from spec.draft import ModelDraft
+    from spec.loop import generate
+
+    g = golden_generate
+    want = g["draft_k4"]["outputs"][0]
+    eos = want[5]
+    d = early_exit(tiny)
+    out, _ = generate(tiny, new_cache(tiny), ModelDraft(d, new_cache(d)), [g["prompts"][0]], g["max_new"], k=4,
+                      eos_id=eos)
+    assert out[0] == want[: want.index(eos) + 1]
+
+
+def test_uniform_draft_is_still_exact(tiny, golden_generate):
+    """A custom drafter that proposes uniform noise (the composable path) accepts almost
+    nothing, and the output is still the target's greedy continuation."""
+    from spec.draft import UniformDraft
+    from spec.loop import generate
+
+    g = golden_generate
+    out, st = generate(tiny, new_cache(tiny), UniformDraft(tiny.config.vocab_size), g["prompts"], g["max_new"], k=4,
+                       generator=torch.Generator().manual_seed(0))
+    assert out == g["plain"][: len(g["prompts"])]
+    assert st.accepted / st.drafted < 0.05
+
+
+def test_batched_plain_decode_drops_a_row_at_eos(tiny):
+    """Batched plain decoding retires a row at its eos and finishes the others, as one-at-a-time
+    decoding does (the reference's tests/test_batch_size.py:31-37)."""
+    from baselines import cached_autoregressive
+
+    prompts = [[5, 6, 7], list(range(30, 60))]
+    full = [cached_autoregressive.generate(tiny, new_cache(tiny), p, 12) for p in prompts]
+    eos = full[0][3]
+    want = [cached_autoregressive.generate(tiny, new_cache(tiny), p, 12, eos_id=eos) for p in prompts]
+    assert len(want[0]) <= 4
+    assert cached_autoregressive.generate_batch(tiny, new_cache(tiny), prompts, 12, eos_id=eos) == want
+
+
 class ScriptedDraft:
     """Proposes the target's own continuation for the first j positions, then a wrong token
     (the reference's tests/test_rollback.py:13-34)."""
