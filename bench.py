@@ -700,7 +700,10 @@ def main() -> None:
 
     vstep = time_verify_step(target, KVCache, device, PROMPT_LEN + NEW_TOKENS // 2)
     acc = time_accept(device)
-    latency = request_latency(target, draft, prompts, device, blocks)
+    try:
+        latency = request_latency(target, draft, prompts, device, blocks)
+    except Exception as e:  # noqa: BLE001  (the throughput line must still be printed)
+        latency = {"error": f"{type(e).__name__}: {e}"}
     pk = peaks()
     achieved = vstep["bytes"] / (vstep["us"] * 1e-6) / 1e9
     acc_gbs = acc["bytes"] / (acc["us"] * 1e-6) / 1e9
