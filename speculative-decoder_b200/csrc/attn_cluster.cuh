@@ -38,7 +38,8 @@ struct FuseO {
   int rows;  // o rows per CTA
 };
 
-// The q/k/v projection fused in front of the attention (decode steps of small models): the
+// The q/k/v projection fused in front of the attention (decode steps of small models; the
+// reference's input RMSNorm, q/k/v linears, RoPE and cache.write, lm/forward.py:55-60): the
 // cluster of KV head g computes that head's rows of Y = RMSNorm(x) W_qkv^T itself. The head's
 // (G + 2) * 32 rotary pairs (G query heads, the key head, the value head; pair c of a head is
 // rows c and c + 32) are split into runs of `pairs` between the cluster's CTAs; each CTA brings
