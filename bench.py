@@ -50,12 +50,10 @@ WEIGHT_BYTES = 3_422_752_768          # 1.7B linears + tied embedding, bf16, rea
 KV_BYTES_PER_TOKEN = 196_608          # 24 layers x 2 x 32 heads x 64 x 2 B
 ACCEPT_BYTES = 113_246_208            # config 3: 64 x (5 + 4) x 49152 x 4 B
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per algorithmic byte of one verify
-# forward, from ncu captures of the 6-layer case (1.0383 GB of algorithmic bytes): per-layer
-# kernels 1.0427 GB (profiles/traffic_verify_step_1p7b_6layers_perlayer.txt), layer-stream
-# kernel 1.0426 GB (profiles/stream_kernel_verify_1p7b_6layers.txt). Traffic grows with the
-# layers streamed, so the full-size figure scales by the same ratio.
-VERIFY_TRAFFIC_RATIO = {"layers": (1_046_855_168 + 181_760) / 1_038_340_096,
-                        "stream": (1_038_322_000 + 4_316_416) / 1_038_340_096}
+# forward, from an ncu capture of the 6-layer case (1.0383 GB of algorithmic bytes): 1.0427 GB
+# (profiles/traffic_verify_step_1p7b_6layers_perlayer.txt). Traffic grows with the layers
+# streamed, so the full-size figure scales by the same ratio.
+VERIFY_TRAFFIC_RATIO = {"layers": (1_046_855_168 + 181_760) / 1_038_340_096}
 
 
 def weight_bytes(spec: dict) -> int:
@@ -153,72 +151,6 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
-    """Per phase kind, medians over CTAs and layers (us) from the layer-stream kernel's
-    globaltimer stamps [grid, phases, 8]: barrier wait (and its minimum over CTAs: the last
-    arriver's, i.e. the barrier's own latency), operand build, MMA span, first accumulator,
-    work after the barrier (median and max over CTAs)."""
-    t = trace.double().cpu()
-
-    def med(x):
-        return float(x.median()) if x.numel() else None
-
-    out = {}
-    for j, name in enumerate(["qkv", "attn", "o", "gate_up", "down"]):
-        ph = t[:, [1 + 5 * l + j for l in range(n_layers)], :]
-        ok = ph[..., 3] > 0
-        d = lambda a, b: (ph[..., a] - ph[..., b])[ok & (ph[..., a] > 0) & (ph[..., b] > 0)] / 1e3  # noqa: E731
-        bar = d(1, 0)
-        per_layer_min = ((ph[..., 1] - ph[..., 0]).where(ok, torch.tensor(float("inf"))).amin(0)) / 1e3
-        out[name] = {"barrier_us": med(bar), "barrier_min_us": med(per_layer_min), "operand_us": med(d(2, 1)),
-                     "mma_span_us": med(d(5, 4)), "first_acc_us": med(d(6, 1)), "work_us": med(d(3, 1)),
-                     "work_max_us": float(d(3, 1).max()) if d(3, 1).numel() else None}
-    first = t[:, 0, 0][t[:, 0, 0] > 0].min()
-    out["total_us"] = float((t[:, :, 3].max() - first) / 1e3)
-    return out
-
-
-def chain_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
-    """The layer-chain kernel's profiling record ([C][n_layers * 5][16] in the flat trace
-    buffer; slot meanings in chain.cu): per phase kind, the median over layers of the critical
-    path (previous phase's last end to this phase's last end), and medians over CTAs and layers
-    of each stamp's offset from the CTA's phase start (us) and of the cycle counters (k cycles)."""
-    flat = trace.flatten().double().cpu()
-    per = n_layers * 5 * 16
-    C = 0
-    while (C + 1) * per <= flat.numel() and bool((flat[C * per:(C + 1) * per] > 0).any()):
-        C += 1
-    if C == 0:
-        return {}
-    t = flat[: C * per].view(C, n_layers * 5, 16)
-    ts = t / 1e3
-    ends = ts[:, :, 3].amax(0)
-    t0 = ts[:, 0, 0].amin()
-    out = {"cluster": C, "total_us": round(float(ends[-1] - t0), 1)}
-    for j, name in enumerate(["qkv", "attn", "o", "gate_up", "down"]):
-        span = [float(ends[5 * l + j] - (ends[5 * l + j - 1] if 5 * l + j > 0 else t0)) for l in range(n_layers)]
-        ph = ts[:, [5 * l + j for l in range(n_layers)], :]
-        start = ph[..., 0]
-        d = {"critical_us": round(statistics.median(span), 2)}
-        for k, key in [(12, "h_ready"), (1, "operand"), (2, "segments"), (3, "end"), (4, "mma_x"), (5, "mma_last"),
-                       (6, "copy_last")]:
-            v = ph[..., k]
-            ok = v > 0
-            if bool(ok.any()):
-                d[key] = round(float((v - start)[ok].median()), 2)
-        for k, key in [(8, "kcyc_wait"), (9, "kcyc_fma"), (10, "kcyc_release"), (11, "kcyc_mma_wait")]:
-            v = ph[..., k]
-            if bool((v > 0).any()):
-                d[key] = round(float(v.median()), 2)
-        if j == 1:
-            cyc, dur = t[:, [5 * l + 1 for l in range(n_layers)], 14], (ph[..., 3] - ph[..., 0]) * 1e3
-            okc = (cyc > 0) & (dur > 0)
-            if bool(okc.any()):
-                d["sm_mhz"] = round(float((cyc[okc] / dur[okc]).median() * 1e3), 1)
-        out[name] = d
-    return out
-
-
 def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30, trace: bool = False) -> dict:
     """The (k+1)-token target forward of one round at B=1 with `context_len` cached tokens,
     captured in a CUDA graph and replayed; CUDA events on the replay stream."""
@@ -266,17 +198,10 @@ def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30
     r = {"us": ms * 1e3, "bytes": weight_bytes(spec) + kv_bytes_per_token(spec) * kv_tokens, "context": kv_tokens,
          "layers": spec["num_hidden_layers"]}
     if trace:
-        n_ph = 2 + 5 * spec["num_hidden_layers"]
-        sched = eng.schedule(1, K + 1)
-        if sched == "layers":
-            tr = torch.zeros(5 * spec["num_hidden_layers"] + 1, 512, 8, dtype=torch.int64, device=device)
-        else:
-            tr = torch.zeros(torch.cuda.get_device_properties(device).multi_processor_count, n_ph, 8,
-                             dtype=torch.int64, device=device)
+        tr = torch.zeros(5 * spec["num_hidden_layers"] + 1, 512, 8, dtype=torch.int64, device=device)
         eng.forward_device(cache, ids, n_new, pastt, table, cap, False, logits, status, ws, trace=tr)
         torch.cuda.synchronize()
-        r["trace"] = (gemm_trace_summary(tr, spec["num_hidden_layers"]) if sched == "layers"
-                      else trace_summary(tr, spec["num_hidden_layers"]))
+        r["trace"] = gemm_trace_summary(tr, spec["num_hidden_layers"])
     return r
 
 
@@ -456,22 +381,12 @@ def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30, 
     r = {"us": st.elapsed_time(en) / reps * 1e3,
          "bytes": weight_bytes(spec) + kv_bytes_per_token(spec) * context_len, "context": context_len,
          "layers": spec["num_hidden_layers"]}
-    if trace:
-        n_ph = 2 + 5 * spec["num_hidden_layers"]
-        tr = torch.zeros(torch.cuda.get_device_properties(device).multi_processor_count, n_ph, 8, dtype=torch.int64,
-                         device=device)
-        sched = eng.schedule(1, 1)
-        if sched == "gemv":
-            L = spec["num_hidden_layers"]
-            tr = torch.zeros((4 * L + 1) * 296 * 8 + L * 512 * 8, dtype=torch.int64, device=device)
+    if trace and eng.schedule(1, tokens) == "gemv":
+        L = spec["num_hidden_layers"]
+        tr = torch.zeros((4 * L + 1) * 296 * 8 + L * 512 * 8, dtype=torch.int64, device=device)
         eng.forward_device(cache, ids, one, pastt, table, cap, True, logits, status, ws, trace=tr)
         torch.cuda.synchronize()
-        if sched == "chain":
-            r["trace"] = chain_trace_summary(tr, spec["num_hidden_layers"])
-        elif sched == "gemv":
-            r["trace"] = gemv_trace_summary(tr, spec["num_hidden_layers"])
-        else:
-            r["trace"] = trace_summary(tr, spec["num_hidden_layers"])
+        r["trace"] = gemv_trace_summary(tr, spec["num_hidden_layers"])
     return r
 
 
@@ -577,7 +492,7 @@ def main() -> None:
     ap.add_argument("--draft-tokens", type=int, default=1,
                     help="with --only draft: new tokens per draft forward (2 = a round's first step)")
     ap.add_argument("--trace", action="store_true",
-                    help="with --only verify/draft: per-phase timings of the layer-stream kernel")
+                    help="with --only verify/draft: per-launch timings from globaltimer stamps")
     ap.add_argument("--only", choices=["verify", "accept", "draft"],
                     help="time one piece alone (for profiling): the verify forward, the accept kernel or one "
                          "draft-model forward step")

@@ -160,13 +160,6 @@ typedef struct specb200_layer_weights {
   const void* mlp_norm;   /* [H]                                                    */
   const void* w_gate_up;  /* [2 I, H]: 64-row groups, gate rows 64g.. then up rows  */
   const void* w_down;     /* [H, I]                                                 */
-  /* Optional (bf16): the same four matrices as specb200_pack_tiles packs them. When all
-   * are given, decode/verify calls with at most 16 token rows run the persistent
-   * layer-stream kernel instead of one kernel per layer op. */
-  const void* p_qkv;
-  const void* p_o;
-  const void* p_gate_up;
-  const void* p_down;
 } specb200_layer_weights;
 
 typedef struct specb200_model_weights {
@@ -176,7 +169,6 @@ typedef struct specb200_model_weights {
   const float* rope_cos;    /* [max_positions, d/2] fp32, cos(pos * inv_freq)    */
   const float* rope_sin;    /* [max_positions, d/2] fp32                         */
   const specb200_layer_weights* layers; /* host array of n_layers entries          */
-  const void* p_lm_head;    /* optional: lm_head packed by specb200_pack_tiles    */
 } specb200_model_weights;
 
 /* Builds the host-side model handle: shapes, the weight pointers and one TMA descriptor
@@ -201,29 +193,21 @@ typedef struct specb200_batch {
   float* logits;                /* fp32 [B*T, V] or [B, V]                                */
   int max_kv_len;               /* >= past_len[b] + n_new[b] for every row                */
   int32_t* status;              /* device int32 status word (cleared by the call)         */
-  uint64_t* trace;              /* NULL, or globaltimer stamps (profiling only): the layer- */
-                                /* stream kernel writes [grid x phases x 8]; the GEMV       */
-                                /* schedule [4 n_layers + 1 launches][296 CTAs][8]: entry, */
+  uint64_t* trace;              /* NULL, or globaltimer stamps (profiling only): the        */
+                                /* GEMV schedule writes                                     */
+                                /* [4 n_layers + 1 launches][296 CTAs][8]: entry,           */
                                 /* wait return, inputs staged, weights landed, end; the    */
                                 /* per-layer schedule [4 n_layers + 1 GEMMs][512][8]; both */
                                 /* followed by the attention launches [n_layers][512][8]   */
                                 /* (zeroed first)                                          */
 } specb200_batch;
 
-/* Weight tiles for the layer-stream kernel: W [N, K] bf16 row-major is rewritten as
- * ceil(N/128) x ceil(K/64) contiguous 16 KB tiles of 128 rows x 64 columns (zero padded),
- * each already in the 128-byte swizzled K-major layout the tensor cores read, so one 1-D
- * bulk copy moves a tile and every SM streams a contiguous range of the buffer. */
-size_t specb200_packed_tile_bytes(int N, int K);
-int specb200_pack_tiles(const void* w, int N, int K, void* out, void* stream);
-
 size_t specb200_forward_workspace_bytes(void* model, int B, int T, int max_kv_len);
-/* Which schedule a call with B rows of T tokens runs: 2 = the layer stack on one thread-block
- * cluster (small models, at most 8 token rows; 3 launches with the final norm and LM head),
- * 1 = the persistent layer-stream kernel over all SMs (one launch), 3 = decode steps of at
- * most 4 token rows on the GEMV kernels with the norms folded in (2 + 5 n_layers launches),
- * 0 = one kernel per layer op (3 + 7 n_layers launches). */
-int specb200_forward_uses_stream(void* model, int B, int T);
+/* Which schedule a call with B rows of T tokens runs: 3 = decode steps of at most 4 token rows
+ * of a model whose layer weights fit on chip, on the GEMV kernels with the norms folded in
+ * (2 + 5 n_layers launches, 3 + 5 n_layers with a tensor-core LM head), 0 = one kernel per
+ * layer op (3 + 7 n_layers launches). */
+int specb200_forward_schedule(void* model, int B, int T);
 /* Kernel launches one forward call with B rows of T tokens makes (no reference counterpart;
  * used to count launches). */
 int specb200_forward_launches(void* model, int B, int T);

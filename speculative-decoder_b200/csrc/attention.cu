@@ -50,24 +50,7 @@ __global__ void __launch_bounds__(kAcThreads) attention_cluster_kernel(AttnKerne
   attention_cluster_cta(ka, blockIdx.z, blockIdx.y, ac_smem, true);
 }
 
-// Decode steps of small models: attention of every KV head of a sequence in one cluster
-// (P CTAs per head), then the o projection with the residual add (FuseO).
-__global__ void __launch_bounds__(kAcThreads) attention_o_kernel(AttnKernelArgs ka, FuseO fo) {
-  extern __shared__ __align__(16) uint8_t ac_smem[];
-  pdl_launch_dependents();
-  attention_cluster_cta(ka, blockIdx.y, 0, ac_smem, true, &fo);
-}
-
-// Decode steps of small models: each KV head's q/k/v projection computed by its own cluster in
-// front of the attention (FuseQKV).
-__global__ void __launch_bounds__(kAcThreads) attention_qkv_kernel(AttnKernelArgs ka, FuseQKV fq) {
-  extern __shared__ __align__(16) uint8_t ac_smem[];
-  pdl_launch_dependents();
-  attention_cluster_cta(ka, blockIdx.z, blockIdx.y, ac_smem, true, nullptr, &fq);
-}
-
 constexpr int kAcSmemLimit = 200 * 1024;
-constexpr int kAoMaxCluster = 16;  // non-portable cluster size
 
 cudaError_t launch_cluster(const AttnArgs& a, const AttnPlan& p, cudaStream_t s, bool pdl) {
   AttnKernelArgs ka;
@@ -113,16 +96,9 @@ bool attention_prepare() {
   static bool ok = false;
   std::call_once(once, [] {
     ok = cudaFuncSetAttribute(attention_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAcSmemLimit) ==
-             cudaSuccess &&
-         cudaFuncSetAttribute(attention_o_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAcSmemLimit) ==
-             cudaSuccess &&
-         cudaFuncSetAttribute(attention_o_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess &&
-         cudaFuncSetAttribute(attention_qkv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAcSmemLimit) ==
-             cudaSuccess;
+         cudaSuccess;
     // the largest carveout, as every kernel of a forward, so that consecutive kernels share SMs
     for (const void* f : {reinterpret_cast<const void*>(attention_cluster_kernel),
-                          reinterpret_cast<const void*>(attention_o_kernel),
-                          reinterpret_cast<const void*>(attention_qkv_kernel),
                           reinterpret_cast<const void*>(attention_mma_kernel),
                           reinterpret_cast<const void*>(attention_kernel<float, 16>),
                           reinterpret_cast<const void*>(attention_kernel<float, 32>),
@@ -137,11 +113,7 @@ bool attention_prepare() {
 }
 
 AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len, bool tensor_items) {
-  static const bool cluster_on = [] {
-    const char* v = std::getenv("SPECB200_ATTN_CLUSTER");
-    return !(v && *v == '0');
-  }();
-  if (tensor_items && T * (Hq / Hkv) <= kAmRows && cluster_on && attention_prepare()) {
+  if (tensor_items && T * (Hq / Hkv) <= kAmRows && attention_prepare()) {
     AttnPlan p;
     if (plan_attention_cluster(max_kv_len, &p) && ac_layout(p.chunk, T * (Hq / Hkv), p.splits_max, 1).total <= kAcSmemLimit)
       return p;
@@ -162,112 +134,6 @@ AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len, bool tens
   p.chunk = (((max_len + splits - 1) / splits) + kKeys - 1) / kKeys * kKeys;
   p.splits_max = (max_len + p.chunk - 1) / p.chunk;
   return p;
-}
-
-bool plan_attention_o(int B, int T, int Hq, int Hkv, int D, int H, int max_kv_len, AttnPlan* p, int* P, int* rows) {
-  if (D != 64 || Hq % Hkv || T * (Hq / Hkv) > kAcRowsMax || Hkv > kAoMaxCluster || !attention_prepare()) return false;
-  // Opt-in (SPECB200_ATTN_O=1): the 15-CTA clusters cannot be placed while the q/k/v GEMV
-  // holds the SMs, so they lose the early key and weight loads: 0.605 vs 0.573 ms per draft step.
-  static const bool on = [] {
-    const char* v = std::getenv("SPECB200_ATTN_O");
-    return v && *v == '1';
-  }();
-  if (!on) return false;
-  const int len = std::max(1, max_kv_len);
-  const int per = std::max(1, std::min(kAoMaxCluster / Hkv, (len + 63) / 64));
-  const int chunk = ((len + per - 1) / per + 7) / 8 * 8;
-  if (chunk > kAcMaxChunk) return false;
-  const int C = Hkv * per;
-  const int r = (H + C - 1) / C;
-  if (ac_layout(chunk, T * (Hq / Hkv), per, 1, T, Hq, r).total > kAcSmemLimit || (Hq * D * 2) % 16) return false;
-  p->qtiles = 1;
-  p->splits_max = C;
-  p->chunk = chunk;
-  p->mma = 3;
-  *P = per;
-  *rows = r;
-  return true;
-}
-
-int launch_attention_o(const AttnArgs& a, const AttnPlan& p, int P, int rows, const __nv_bfloat16* w_o,
-                       __nv_bfloat16* hidden, int H, cudaStream_t s, bool pdl) {
-  if (p.mma != 3 || a.D != 64 || (reinterpret_cast<uintptr_t>(w_o) & 15)) return SPECB200_ERR_UNSUPPORTED;
-  AttnKernelArgs ka;
-  ka.a = a;
-  ka.p = p;
-  ka.counters = nullptr;
-  ka.part = nullptr;
-  FuseO fo{w_o, hidden, H, P, rows};
-  const int R = a.T * (a.Hq / a.Hkv);
-  const AcLayout lay = ac_layout(p.chunk, R, P, a.bs, a.T, a.Hq, rows);
-  if (lay.total > kAcSmemLimit) return SPECB200_ERR_UNSUPPORTED;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.splits_max, a.B, 1);
-  cfg.blockDim = dim3(kAcThreads);
-  cfg.dynamicSmemBytes = lay.total;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = p.splits_max;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, attention_o_kernel, ka, fo) == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
-}
-
-bool plan_attention_qkv(int T, int Hq, int Hkv, int D, int H, int max_kv_len, AttnPlan* p, int* pairs) {
-  if (D != 64 || Hkv <= 0 || Hq % Hkv || T < 1 || T > kAcQkvMaxT || T * (Hq / Hkv) > kAcRowsMax || H % 8 ||
-      H > kAcThreads * 8 * kAcQkvChunks || !attention_prepare())
-    return false;
-  // Always the largest cluster: the head's weight rows spread over 8 CTAs (46 KB each for the
-  // 135M draft) and 8 warps per CTA share the products; CTAs past the keys only compute rows.
-  const int G = Hq / Hkv, C = kAcMaxCluster, len = std::max(1, max_kv_len);
-  const int chunk = ((len + C - 1) / C + 7) / 8 * 8;
-  if (chunk > kAcMaxChunk) return false;
-  const int pr = ((G + 2) * 32 + C - 1) / C;
-  if (ac_qkv_layout(ac_layout(chunk, T * G, C, 1).total, T, H, pr).total > kAcSmemLimit) return false;
-  p->qtiles = 1;
-  p->splits_max = C;
-  p->chunk = chunk;
-  p->mma = 4;
-  *pairs = pr;
-  return true;
-}
-
-int launch_attention_qkv(const AttnArgs& a, const AttnPlan& p, int pairs, const __nv_bfloat16* w_qkv,
-                         const __nv_bfloat16* x, const __nv_bfloat16* norm_w, const int32_t* slot, float eps, int H,
-                         cudaStream_t s, bool pdl) {
-  auto al16 = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15) == 0; };
-  if (p.mma != 4 || a.D != 64 || a.T > kAcQkvMaxT || H % 8 || !al16(w_qkv) || !al16(x) || !al16(norm_w) || !slot ||
-      !a.rope_cos || !a.rope_sin || a.max_positions <= 0 || pairs * p.splits_max < (a.Hq / a.Hkv + 2) * 32)
-    return SPECB200_ERR_UNSUPPORTED;
-  AttnKernelArgs ka;
-  ka.a = a;
-  ka.p = p;
-  ka.counters = nullptr;
-  ka.part = nullptr;
-  FuseQKV fq{w_qkv, x, norm_w, slot, eps, H, pairs};
-  const int R = a.T * (a.Hq / a.Hkv);
-  const AcQkvLayout ql = ac_qkv_layout(ac_layout(p.chunk, R, p.splits_max, a.bs).total, a.T, H, pairs);
-  if (ql.total > kAcSmemLimit) return SPECB200_ERR_UNSUPPORTED;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.splits_max, a.Hkv, a.B);
-  cfg.blockDim = dim3(kAcThreads);
-  cfg.dynamicSmemBytes = ql.total;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = p.splits_max;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, attention_qkv_kernel, ka, fq) == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
 }
 
 size_t attention_partials_bytes(const AttnPlan& p, int B, int Hkv, int D) {

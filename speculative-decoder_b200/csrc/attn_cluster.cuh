@@ -24,72 +24,20 @@ constexpr int kAcMaxCluster = 8;
 constexpr int kAcMaxChunk = 512;  // keys per CTA
 constexpr int kAcRowsMax = 16;
 constexpr int kQkvMaxSplits = 4;  // q/k/v partials summed by the attention (AttnArgs::qkv_parts)
-constexpr int kAcQkvChunks = 2;   // fused projection: 16-byte input chunks per thread (H <= 4096)
-constexpr int kAcQkvMaxT = 4;     // fused projection: token rows per sequence
 
-// The o projection fused behind the attention (decode steps of small models): one cluster per
-// sequence covers every KV head (P CTAs per head); after the heads' merges every CTA holds the
-// whole attention output and computes `rows` rows of o = W_o attn with the residual add.
-struct FuseO {
-  const __nv_bfloat16* w;  // [H, Hq d] row-major
-  __nv_bfloat16* hidden;   // residual stream [B T, H]
-  int H;
-  int P;     // CTAs per KV head
-  int rows;  // o rows per CTA
-};
-
-// The q/k/v projection fused in front of the attention (decode steps of small models; the
-// reference's input RMSNorm, q/k/v linears, RoPE and cache.write, lm/forward.py:55-60): the
-// cluster of KV head g computes that head's rows of Y = RMSNorm(x) W_qkv^T itself. The head's
-// (G + 2) * 32 rotary pairs (G query heads, the key head, the value head; pair c of a head is
-// rows c and c + 32) are split into runs of `pairs` between the cluster's CTAs; each CTA brings
-// its weight rows on chip by bulk copies issued before griddepcontrol.wait, normalises the
-// input rows, computes its pairs, rotates them and sends each value where the attention reads
-// it: q to every CTA, a new key or value to the CTA whose chunk holds its position (and to the
-// pool), through distributed shared memory.
-struct FuseQKV {
-  const __nv_bfloat16* w;       // [Hq d + 2 Hkv d, H] q/k/v weight rows
-  const __nv_bfloat16* x;       // residual stream [B T, H]
-  const __nv_bfloat16* norm_w;  // [H] RMSNorm weight in front of the projection
-  const int32_t* slot;          // [B T] pool slot of each token row, -1 for padding rows
-  float eps;
-  int H;
-  int pairs;  // rotary pairs per CTA
-};
-
-// Regions of the fused projection, after the attention's own layout (`base` bytes): weight
-// rows [2 pairs][H] bf16 (the pairs' first rows, then their second rows), the normalised
-// input [T][H] bf16, the rounded products [T][2 pairs] fp32, the norm's warp sums and the
-// weights' mbarrier.
-struct AcQkvLayout {
-  int w, x, res, red, bar, total;
-};
-__host__ __device__ inline AcQkvLayout ac_qkv_layout(int base, int T, int H, int pairs) {
-  AcQkvLayout q;
-  q.w = (base + 127) / 128 * 128;
-  q.x = q.w + 2 * pairs * H * 2;
-  q.res = q.x + (T * H * 2 + 15) / 16 * 16;
-  q.red = q.res + T * 2 * pairs * 4;
-  q.bar = (q.red + kAcWarps * 4 * 4 + 7) / 8 * 8;
-  q.total = q.bar + 8;
-  return q;
-}
-
-// Dynamic shared memory of the cluster kernel for chunk keys per CTA, R query rows, S merge
-// slots (CTAs per head) and, when fused, T tokens of Hq heads and `orows` o rows of K = Hq d.
+// Dynamic shared memory of the cluster kernel for chunk keys per CTA, R query rows and S merge
+// slots (CTAs per head).
 struct AcLayout {
-  int kv, scratch, slots, tab, attn, wo, bar, total;  // byte offsets (q rows at 0), total size
+  int kv, scratch, slots, tab, bar, total;  // byte offsets (q rows at 0), total size
 };
-__host__ __device__ inline AcLayout ac_layout(int chunk, int R, int S, int bs, int T = 0, int Hq = 0, int orows = 0) {
+__host__ __device__ inline AcLayout ac_layout(int chunk, int R, int S, int bs) {
   AcLayout L;
   const int region = chunk * 256 > kAcWarps * (R * 64 + 32) * 4 ? chunk * 256 : kAcWarps * (R * 64 + 32) * 4;
   L.kv = 2048;
   L.scratch = L.kv;  // the K / V region is reused by the warp merge once the products are done
   L.slots = L.kv + ((region + 127) / 128) * 128;
   L.tab = L.slots + S * (R * 64 + 32) * 4;
-  L.attn = L.tab + (((chunk + bs - 1) / bs + 2) * 4 + 127) / 128 * 128;
-  L.wo = L.attn + (T * Hq * 64 * 2 + 127) / 128 * 128;
-  L.bar = L.wo + orows * Hq * 64 * 2;
+  L.bar = L.tab + (((chunk + bs - 1) / bs + 2) * 4 + 127) / 128 * 128;
   L.total = L.bar + 16 + 128;
   return L;
 }
@@ -188,27 +136,19 @@ SPECB200_DEVINL void ac_merge_warps(const AmState& st, float* scratch, int R, fl
   __syncthreads();
 }
 
-// One CTA of the cluster for (sequence b, KV head g): keys [part * chunk, ...) of the row. Without
-// `fo` the cluster is one KV head (part = rank) and its first CTA writes the output; with `fo`
-// the cluster is every KV head of the sequence (g = rank / P, part = rank % P), each head's first
-// CTA sends the head's output to every CTA, and each CTA computes its o rows.
-// With `pdl` the cached keys (and the o or q/k/v weights) are loaded before griddepcontrol.wait.
-// With `fq` (never together with `fo`) the cluster computes its own q and new keys / values.
-static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, int g, uint8_t* smem, bool pdl,
-                                             const FuseO* fo = nullptr, const FuseQKV* fq = nullptr) {
+// One CTA of the cluster for (sequence b, KV head g): keys [rank * chunk, ...) of the row; the
+// cluster's first CTA writes the output. With `pdl` the cached keys are loaded before
+// griddepcontrol.wait.
+static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, int g, uint8_t* smem, bool pdl) {
   const AttnArgs& a = ka.a;
   constexpr int D = 64;
   const int chunk = ka.p.chunk;
   const int G = a.Hq / a.Hkv;
   const int R = a.T * G;
-  const int rank = static_cast<int>(ac_rank());
-  const int P = fo ? fo->P : ka.p.splits_max;  // CTAs per KV head
-  if (fo) g = rank / P;
-  const int part = fo ? rank % P : rank;
-  const int lead = rank - part;  // the head's first CTA
+  const int part = static_cast<int>(ac_rank());
+  const int P = ka.p.splits_max;  // CTAs per KV head
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int K = a.Hq * D;  // o projection inputs
-  const AcLayout lay = fo ? ac_layout(chunk, R, P, a.bs, a.T, a.Hq, fo->rows) : ac_layout(chunk, R, P, a.bs);
+  const AcLayout lay = ac_layout(chunk, R, P, a.bs);
   unsigned long long* tr = nullptr;  // optional record (AttnArgs::trace), thread 0
   if (a.trace && tid == 0) {
     const unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
@@ -228,62 +168,6 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
   const int kmax = min(total, past + (R - 1) / G + 1);
   const int kbeg = min(kmax, part * chunk);
   const int kend = min(kmax, kbeg + chunk);
-  // fused o projection: this CTA's weight rows [o0, o1) by one bulk copy, before the wait
-  const int o0 = fo ? min(fo->H, rank * fo->rows) : 0, o1 = fo ? min(fo->H, o0 + fo->rows) : 0;
-  uint64_t* obar = reinterpret_cast<uint64_t*>(smem + lay.bar);
-  __nv_bfloat16* wo_s = reinterpret_cast<__nv_bfloat16*>(smem + lay.wo);
-  __nv_bfloat16* attn_s = reinterpret_cast<__nv_bfloat16*>(smem + lay.attn);  // [T][Hq d]
-  if (fo && tid == 0) {
-    mbar_init(obar, 1);
-    fence_mbar_init();
-    if (o1 > o0) {
-      const uint32_t bytes = static_cast<uint32_t>(o1 - o0) * K * 2;
-      mbar_arrive_expect_tx(obar, bytes);
-      asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                       smem_u32(wo_s)),
-                   "l"(reinterpret_cast<uint64_t>(fo->w + static_cast<int64_t>(o0) * K)), "r"(bytes), "r"(smem_u32(obar))
-                   : "memory");
-    } else {
-      mbar_arrive(obar);
-    }
-  }
-  // fused q/k/v projection: this CTA's pairs [p0, p1) of the head's (G + 2) * 32, their weight
-  // rows by bulk copies (one per run of first rows and one per run of second rows within each
-  // head), and the norm weight into registers, all before the wait
-  const AcQkvLayout ql = fq ? ac_qkv_layout(lay.total, a.T, fq->H, fq->pairs) : AcQkvLayout{};
-  const int npairs_all = (G + 2) * 32;
-  const int p0 = fq ? min(npairs_all, part * fq->pairs) : 0;
-  const int np = fq ? min(npairs_all, p0 + fq->pairs) - p0 : 0;
-  uint64_t* wbar = reinterpret_cast<uint64_t*>(smem + ql.bar);
-  __nv_bfloat16* w_s = reinterpret_cast<__nv_bfloat16*>(smem + ql.w);
-  uint4 nw[kAcQkvChunks];
-  if (fq) {
-    const int Hf = fq->H;
-    if (tid == 0) {
-      mbar_init(wbar, 1);
-      fence_mbar_init();
-      mbar_arrive_expect_tx(wbar, static_cast<uint32_t>(2 * np) * Hf * 2);
-      for (int s0 = p0; s0 < p0 + np;) {  // one run per head
-        const int hh = s0 / 32, s1 = min(p0 + np, (hh + 1) * 32), c0 = s0 % 32;
-        const int base = hh < G ? (g * G + hh) * D : (hh == G ? a.Hq * D + g * D : (a.Hq + a.Hkv) * D + g * D);
-        const uint32_t bytes = static_cast<uint32_t>(s1 - s0) * Hf * 2;
-        const __nv_bfloat16* src = fq->w + static_cast<int64_t>(base + c0) * Hf;
-        for (int half = 0; half < 2; ++half)
-          asm volatile(
-              "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                  smem_u32(w_s + static_cast<int64_t>(half * np + s0 - p0) * Hf)),
-              "l"(reinterpret_cast<uint64_t>(src + static_cast<int64_t>(half * 32) * Hf)), "r"(bytes),
-              "r"(smem_u32(wbar))
-              : "memory");
-        s0 = s1;
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < kAcQkvChunks; ++i) {
-      const int ch = tid + i * kAcThreads;
-      nw[i] = ch * 8 < Hf ? __ldg(reinterpret_cast<const uint4*>(fq->norm_w) + ch) : make_uint4(0, 0, 0, 0);
-    }
-  }
   __nv_bfloat16* q_s = reinterpret_cast<__nv_bfloat16*>(smem);
   __nv_bfloat16* k_s = reinterpret_cast<__nv_bfloat16*>(smem + lay.kv);
   __nv_bfloat16* v_s = k_s + chunk * 64;
@@ -316,136 +200,7 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
   }
   if (pdl) pdl_wait();
   stamp(1);
-  if (fq) {
-    using T16 = __nv_bfloat16;
-    const int Hf = fq->H, nch = Hf >> 3, Tn = a.T;
-    __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(smem + ql.x);  // [T][H]
-    float* red = reinterpret_cast<float*>(smem + ql.red);               // [warp][4]
-    float* res = reinterpret_cast<float*>(smem + ql.res);               // [T][2 np]
-    // input rows, RMS-normalised as rmsnorm_kernel rounds: y = round(w * round(x * rsqrt(..)))
-    uint4 xv[kAcQkvChunks][4];
-    float ss[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int t = 0; t < 4; ++t)
-#pragma unroll
-      for (int i = 0; i < kAcQkvChunks; ++i) {
-        const int ch = tid + i * kAcThreads;
-        xv[i][t] = (t < Tn && ch < nch)
-                       ? __ldcg(reinterpret_cast<const uint4*>(fq->x + static_cast<int64_t>(b * Tn + t) * Hf) + ch)
-                       : make_uint4(0, 0, 0, 0);
-        float f[8];
-        ac_unpack8(xv[i][t], f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) ss[t] = fmaf(f[e], f[e], ss[t]);
-      }
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      ss[t] = warp_sum(ss[t]);
-      if (lane == 0) red[warp * 4 + t] = ss[t];
-    }
-    for (int i = tid; i < (16 - R) * 64; i += kAcThreads)  // query rows past R are zero
-      q_s[am_swz(R + i / 64, i % 64)] = __float2bfloat16_rn(0.f);
-    __syncthreads();
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      float tot = 0.f;
-#pragma unroll
-      for (int w = 0; w < kAcWarps; ++w) tot += red[w * 4 + t];
-      ss[t] = 1.0f / sqrtf(tot / static_cast<float>(Hf) + fq->eps);
-    }
-#pragma unroll
-    for (int i = 0; i < kAcQkvChunks; ++i) {
-      const int ch = tid + i * kAcThreads;
-      if (ch >= nch) break;
-      float wf[8];
-      ac_unpack8(nw[i], wf);
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        if (t >= Tn) break;
-        float f[8];
-        ac_unpack8(xv[i][t], f);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = wf[e] * round_to<T16>(f[e] * ss[t]);
-        reinterpret_cast<uint4*>(xs + t * Hf)[ch] = ac_pack8(f);
-      }
-    }
-    __syncthreads();
-    // this CTA's 2 np weight rows: one row per warp at a time, lanes over 16-byte chunks; the
-    // products are rounded to bf16 as the projection's output
-    mbar_wait_bounded(wbar, 0, a.status, nullptr);
-    const uint4* x4 = reinterpret_cast<const uint4*>(xs);
-    for (int j = warp; j < 2 * np; j += kAcWarps) {
-      const uint4* wr = reinterpret_cast<const uint4*>(w_s + static_cast<int64_t>(j) * Hf);
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int ch = lane; ch < nch; ch += 32) {
-        float wf[8];
-        ac_unpack8(wr[ch], wf);
-#pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          if (t >= Tn) break;
-          float f[8];
-          ac_unpack8(x4[t * nch + ch], f);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc[t] = fmaf(wf[e], f[e], acc[t]);
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < 4; ++t) acc[t] = warp_sum(acc[t]);
-      if (lane == 0) {
-#pragma unroll
-        for (int t = 0; t < 4; ++t)
-          if (t < Tn) res[t * 2 * np + j] = round_to<T16>(acc[t]);
-      }
-    }
-    __syncthreads();
-    // rotate q and k (EPI_QKV's rounding), then send: q to every CTA of the cluster, a new key
-    // or value to the CTA whose chunk holds its position, and to the pool
-    const int C = ka.p.splits_max;
-    ac_cluster_wait();  // every CTA of the cluster runs, so its shared memory can be written
-    for (int i = tid; i < Tn * np; i += kAcThreads) {
-      const int t = i / np, l = i - t * np;
-      const int pr = p0 + l, hh = pr >> 5, c = pr & 31;
-      float lo = res[t * 2 * np + l], hi = res[t * 2 * np + np + l];
-      if (hh <= G) {
-        const int pos = min(past + t, a.max_positions - 1);
-        const float cs = round_to<T16>(a.rope_cos[static_cast<int64_t>(pos) * 32 + c]);
-        const float sn = round_to<T16>(a.rope_sin[static_cast<int64_t>(pos) * 32 + c]);
-        const float lo2 = round_to<T16>(round_to<T16>(lo * cs) + round_to<T16>(-hi * sn));
-        const float hi2 = round_to<T16>(round_to<T16>(hi * cs) + round_to<T16>(lo * sn));
-        lo = lo2;
-        hi = hi2;
-      }
-      const unsigned short ulo = __bfloat16_as_ushort(__float2bfloat16_rn(lo));
-      const unsigned short uhi = __bfloat16_as_ushort(__float2bfloat16_rn(hi));
-      if (hh < G) {
-        const int r = t * G + hh;
-        const uint32_t olo = smem_u32(q_s + am_swz(r, c)), ohi = smem_u32(q_s + am_swz(r, c + 32));
-        for (int cr = 0; cr < C; ++cr) {
-          asm volatile("st.shared::cluster.u16 [%0], %1;" ::"r"(ac_mapa(olo, cr)), "h"(ulo) : "memory");
-          asm volatile("st.shared::cluster.u16 [%0], %1;" ::"r"(ac_mapa(ohi, cr)), "h"(uhi) : "memory");
-        }
-      } else if (t < nn) {
-        const int kk = past + t, tgt = kk / chunk;
-        const bool isv = hh > G;
-        if (tgt < C) {
-          __nv_bfloat16* dst = isv ? v_s : k_s;
-          const int rr = kk - tgt * chunk;
-          asm volatile("st.shared::cluster.u16 [%0], %1;" ::"r"(ac_mapa(smem_u32(dst + am_swz(rr, c)), tgt)), "h"(ulo)
-                       : "memory");
-          asm volatile("st.shared::cluster.u16 [%0], %1;" ::"r"(ac_mapa(smem_u32(dst + am_swz(rr, c + 32)), tgt)),
-                       "h"(uhi)
-                       : "memory");
-        }
-        const int sl = fq->slot[b * Tn + t];
-        if (sl >= 0) {
-          __nv_bfloat16* pool = const_cast<__nv_bfloat16*>(isv ? vp : kp) + (static_cast<int64_t>(sl) * a.Hkv + g) * D;
-          pool[c] = __ushort_as_bfloat16(ulo);
-          pool[c + 32] = __ushort_as_bfloat16(uhi);
-        }
-      }
-    }
-    ac_cluster_sync();  // every CTA's q rows and new keys / values have landed
-  } else if (a.qkv_parts) {
+  if (a.qkv_parts) {
     // q rows and the new keys / values from the q/k/v GEMM's partials: pair (c, c + 32) of a
     // head, summed over splits in order, rounded, rotated (q and k) as EPI_QKV does. Two pairs
     // per thread per pass with every partial load of the pass in flight together.
@@ -570,16 +325,15 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
   float* mo = slots + part * slot_floats;
   ac_merge_warps(st, scratch, R, mo, mo + R * 64, mo + R * 64 + 16);
   stamp(4);
-  if (!fq) ac_cluster_wait();  // (the fused projection waited on the start barrier already)
+  ac_cluster_wait();
   if (part != 0) {
-    const uint32_t dst = ac_mapa(smem_u32(slots + part * slot_floats), lead);
+    const uint32_t dst = ac_mapa(smem_u32(slots + part * slot_floats), 0);
     for (int i = tid; i < slot_floats; i += kAcThreads) ac_st_remote(dst + 4 * i, mo[i]);
   }
   ac_cluster_sync();
   stamp(5);
   if (part == 0) {
     __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
-    const int nc = fo ? static_cast<int>(gridDim.x) : 1;  // CTAs that receive the head's output
     for (int i = tid; i < R * D; i += kAcThreads) {
       const int r = i >> 6, c = i & 63;
       float M = -INFINITY;
@@ -593,52 +347,7 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
         L = fmaf(sp[R * 64 + 16 + r], w, L);
       }
       const int t = r / G, h = g * G + r % G;
-      const __nv_bfloat16 v = __float2bfloat16_rn(O / L);
-      if (!fo) {
-        out[(static_cast<int64_t>(b * a.T + t) * a.Hq + h) * D + c] = v;
-      } else {
-        const uint32_t off = smem_u32(attn_s + t * K + h * D + c);
-        for (int cr = 0; cr < nc; ++cr)
-          asm volatile("st.shared::cluster.u16 [%0], %1;" ::"r"(ac_mapa(off, cr)), "h"(__bfloat16_as_ushort(v)) : "memory");
-      }
-    }
-  }
-  if (!fo) {
-    stamp(6);
-    return;
-  }
-  ac_cluster_sync();  // every CTA holds the attention output of all heads
-  // o = W_o attn for rows [o0, o1) and the residual add (the GEMM's EPI_RESID rounding)
-  if (!mbar_wait_bounded(obar, 0, a.status, nullptr)) return;
-  const uint4* a4 = reinterpret_cast<const uint4*>(attn_s);
-  const int nch = K >> 3;
-  for (int n = o0 + warp; n < o1; n += kAcWarps) {
-    const uint4* wr = reinterpret_cast<const uint4*>(wo_s + static_cast<int64_t>(n - o0) * K);
-    float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int ch = lane; ch < nch; ch += 32) {
-      const uint4 wv = wr[ch];
-      const uint32_t wu[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        if (t >= a.T) break;
-        const uint4 xv = a4[t * nch + ch];
-        const uint32_t xu[4] = {xv.x, xv.y, xv.z, xv.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          acc[t] = fmaf(__uint_as_float(wu[q] << 16), __uint_as_float(xu[q] << 16), acc[t]);
-          acc[t] = fmaf(__uint_as_float(wu[q] & 0xffff0000u), __uint_as_float(xu[q] & 0xffff0000u), acc[t]);
-        }
-      }
-    }
-#pragma unroll
-    for (int t = 0; t < 4; ++t) acc[t] = warp_sum(acc[t]);
-    if (lane < a.T) {
-      float v = acc[0];
-#pragma unroll
-      for (int t = 1; t < 4; ++t)
-        if (lane == t) v = acc[t];
-      __nv_bfloat16* hp = fo->hidden + static_cast<int64_t>(b * a.T + lane) * fo->H + n;
-      *hp = __float2bfloat16_rn(__bfloat162float(*hp) + round_to<__nv_bfloat16>(v));
+      out[(static_cast<int64_t>(b * a.T + t) * a.Hq + h) * D + c] = __float2bfloat16_rn(O / L);
     }
   }
   stamp(6);

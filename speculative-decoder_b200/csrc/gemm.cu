@@ -116,110 +116,19 @@ constexpr uint32_t kWTileBytes = kTileN * kTileK * 2;  // 16 KB
 
 SPECB200_DEVINL uint32_t tmem_cols_for(int BN) { return BN <= 32 ? 32u : BN <= 64 ? 64u : BN <= 128 ? 128u : 256u; }
 
-// kNorm: the X operand is LlamaRMSNorm(rows of nrm.x) built by the epilogue warps in shared
-// memory (the 128-byte swizzled K-major layout the MMA reads) instead of loaded by TMA, which
-// folds the norm launch in front of q/k/v, gate/up and the LM head into the GEMM. Each CTA
-// reads its BN rows in full for the sums of squares (every element once, from L2) and keeps
-// the normalised values of its own K range; the rounding is rmsnorm_kernel's.
-constexpr int kNormMaxK = 2048;  // 8 16-byte chunks per lane per row
-
-// The normalised X rows of this CTA's K range into xhat (epilogue warps, 128 threads): warp w
-// takes live rows w, w + 4, ... two at a time; a lane holds chunks lane + 32 j of a row (all of
-// it for the sum of squares) and stores those inside [kb0, kb1) k-blocks, swizzled. Rows past
-// M are left unwritten: they only feed accumulator columns that the epilogue never reads.
-// Columns past K (inside the last k-block) are zero. Pairs of elements go through packed
-// conversions: x_hat = bf16(x * rs) two at a time, then w * x_hat as one bf16x2 multiply (the
-// product of two bf16 values is exact in fp32, so the rounding is that of rmsnorm_kernel).
-SPECB200_DEVINL void build_xhat(const GemmShape& s, const GemmNorm& nrm, uint8_t* xhat, int m_tile, int kb0, int kb1) {
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int BN = s.BN, K = s.K, nch = K >> 3;
-  const int c_lo = kb0 * 8, c_hi = kb1 * 8;  // 16-byte chunks of the K range
-  const int valid = min(BN, s.M - m_tile * BN);
-  for (int r0 = warp; r0 < valid; r0 += 8) {
-    const int rows[2] = {r0, r0 + 4};
-    uint4 v[2][8];
-    float ss[2] = {0.f, 0.f};
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = rows[h];
-      const bool live = r < valid;
-      int64_t src = 0;
-      if (live) {
-        const int m = m_tile * BN + r;
-        src = nrm.sel_n_new ? static_cast<int64_t>(m) * nrm.T_tokens + max(__ldcg(nrm.sel_n_new + m) - 1, 0) : m;
-      }
-      const uint4* row = reinterpret_cast<const uint4*>(nrm.x + src * K);
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int c = lane + 32 * jj;
-        v[h][jj] = (live && c < nch) ? __ldcg(row + c) : make_uint4(0, 0, 0, 0);
-      }
-    }
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      float a0 = 0.f, a1 = 0.f;
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const uint32_t u[4] = {v[h][jj].x, v[h][jj].y, v[h][jj].z, v[h][jj].w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const float lo = __uint_as_float(u[q] << 16), hi = __uint_as_float(u[q] & 0xffff0000u);
-          a0 = fmaf(lo, lo, a0);
-          a1 = fmaf(hi, hi, a1);
-        }
-      }
-      ss[h] = a0 + a1;
-    }
-    ss[0] = warp_sum(ss[0]);
-    ss[1] = warp_sum(ss[1]);
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = rows[h];
-      if (r >= valid) continue;
-      const float rs = 1.0f / sqrtf(ss[h] / static_cast<float>(K) + nrm.eps);
-#pragma unroll
-      for (int jj = 0; jj < 8; ++jj) {
-        const int c = lane + 32 * jj;
-        if (c < c_lo || c >= c_hi) continue;
-        uint4 o = make_uint4(0, 0, 0, 0);
-        if (c < nch) {
-          const uint4 nw = __ldg(reinterpret_cast<const uint4*>(nrm.w) + c);  // L1-resident after the first row
-          const uint32_t u[4] = {v[h][jj].x, v[h][jj].y, v[h][jj].z, v[h][jj].w};
-          const uint32_t w4[4] = {nw.x, nw.y, nw.z, nw.w};
-          uint32_t out[4];
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float lo = __uint_as_float(u[q] << 16), hi = __uint_as_float(u[q] & 0xffff0000u);
-            const __nv_bfloat162 xh = __floats2bfloat162_rn(lo * rs, hi * rs);
-            const __nv_bfloat162 y = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&w4[q]), xh);
-            out[q] = *reinterpret_cast<const uint32_t*>(&y);
-          }
-          o = make_uint4(out[0], out[1], out[2], out[3]);
-        }
-        const int kb = (c >> 3) - kb0, cc = c & 7;
-        *reinterpret_cast<uint4*>(xhat + static_cast<size_t>(kb) * BN * 128 + r * 128 + ((cc ^ (r & 7)) << 4)) = o;
-      }
-    }
-  }
-}
-
-template <bool kNorm>
 __global__ void __launch_bounds__(kTcThreads, 2)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap w_map, const __grid_constant__ CUtensorMap x_map, GemmShape s,
-                   Epilogue e, GemmScratch scratch, int32_t* status, int stages, GemmNorm nrm) {
+                   Epilogue e, GemmScratch scratch, int32_t* status, int stages) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int BN = s.BN;
-  const uint32_t x_bytes = kNorm ? 0u : static_cast<uint32_t>(BN) * kTileK * 2;
+  const uint32_t x_bytes = static_cast<uint32_t>(BN) * kTileK * 2;
   const uint32_t stage_bytes = kWTileBytes + x_bytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + stages * stage_bytes);
   uint64_t* empty = full + stages;
   uint64_t* tmem_full = empty + stages;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(tmem_full + 1);
   int* abort_flag = reinterpret_cast<int*>(tmem_holder + 1);
-  uint64_t* xready = tmem_full + 2;  // kNorm: the normalised operand is in place
-  // kNorm: [k-block of this CTA][BN rows][64] bf16, 1024-byte aligned
-  uint8_t* xhat = smem + ((stages * stage_bytes + (2 * stages + 3) * 8 + 1023) & ~1023u);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_tile = blockIdx.x, split = blockIdx.y, m_tile = blockIdx.z;
@@ -248,7 +157,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
       mbar_init(&empty[i], 1);
     }
     mbar_init(tmem_full, 1);
-    if (kNorm) mbar_init(xready, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -265,7 +173,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   if (warp == 4) {
     if (lane == 0) {
       tma_prefetch_desc(&w_map);
-      if (!kNorm) tma_prefetch_desc(&x_map);
+      tma_prefetch_desc(&x_map);
       const uint64_t pol_w = l2_policy_evict_first();
       const int pre = min(stages, nkb);
       // Weights do not depend on the previous kernel: start streaming them before the wait.
@@ -273,19 +181,16 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         mbar_arrive_expect_tx(&full[i], stage_bytes);
         tma_load_2d_hint(smem + i * stage_bytes, &w_map, &full[i], (kb0 + i) * kTileK, n_tile * kTileN, pol_w);
       }
-      if (!kNorm) {  // with kNorm the producer reads weights only and never waits
-        pdl_wait();
-        stamp(1);
-        for (int i = 0; i < pre; ++i)
-          tma_load_2d(smem + i * stage_bytes + kWTileBytes, &x_map, &full[i], (kb0 + i) * kTileK, m_tile * BN);
-      }
+      pdl_wait();
+      stamp(1);
+      for (int i = 0; i < pre; ++i)
+        tma_load_2d(smem + i * stage_bytes + kWTileBytes, &x_map, &full[i], (kb0 + i) * kTileK, m_tile * BN);
       for (int i = pre; i < nkb; ++i) {
         const int st = i % stages;
         if (!mbar_wait_bounded(&empty[st], ((i / stages) - 1) & 1, status, abort_flag)) break;
         mbar_arrive_expect_tx(&full[st], stage_bytes);
         tma_load_2d_hint(smem + st * stage_bytes, &w_map, &full[st], (kb0 + i) * kTileK, n_tile * kTileN, pol_w);
-        if (!kNorm)
-          tma_load_2d(smem + st * stage_bytes + kWTileBytes, &x_map, &full[st], (kb0 + i) * kTileK, m_tile * BN);
+        tma_load_2d(smem + st * stage_bytes + kWTileBytes, &x_map, &full[st], (kb0 + i) * kTileK, m_tile * BN);
       }
       // Tail: wait until the MMAs have released the last use of every stage, so that no
       // tcgen05.commit arrive lands on this CTA's shared memory after it has exited.
@@ -297,15 +202,13 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     // The whole warp runs the loop and one elected lane issues each MMA: issuing from a lone
     // lane while the others wait diverged costs about a third more per instruction.
     const uint32_t idesc = umma_idesc_bf16(kTileN, BN);
-    const bool have_x = !kNorm || mbar_wait_warp(xready, 0, status, abort_flag);
-    for (int i = 0; have_x && i < nkb; ++i) {
+    for (int i = 0; i < nkb; ++i) {
       const int st = i % stages;
       if (!mbar_wait_warp(&full[st], (i / stages) & 1, status, abort_flag)) break;
       if (i == 0 && lane == 0) stamp(2);
       tc_fence_after();
       const uint64_t da = umma_desc_sw128(smem_u32(smem + st * stage_bytes));
-      const uint64_t dx = umma_desc_sw128(
-          smem_u32(kNorm ? xhat + static_cast<size_t>(i) * BN * 128 : smem + st * stage_bytes + kWTileBytes));
+      const uint64_t dx = umma_desc_sw128(smem_u32(smem + st * stage_bytes + kWTileBytes));
 #pragma unroll
       for (int kk = 0; kk < kTileK / 16; ++kk)
         umma_bf16_elect(tmem_base, da + kk * 2, dx + kk * 2, idesc, (i > 0 || kk > 0) ? 1u : 0u);
@@ -314,19 +217,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     umma_commit_elect(tmem_full);
     __syncwarp();
   } else {
-    if (kNorm) {
-      // norm weights (parameters, not produced upstream) into L1 before the wait
-      for (int c = threadIdx.x; c < (s.K >> 3); c += 128)
-        asm volatile("prefetch.global.L1 [%0];" ::"l"(reinterpret_cast<const uint4*>(nrm.w) + c));
-      pdl_wait();
-      if (threadIdx.x == 0) stamp(1);
-      build_xhat(s, nrm, xhat, m_tile, kb0, kb1);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic writes -> tensor core reads
-      epi_bar_sync();
-      if (threadIdx.x == 0) mbar_arrive(xready);
-    } else {
-      pdl_wait();
-    }
+    pdl_wait();
     const bool ok = mbar_wait_bounded(tmem_full, 0, status, abort_flag);
     if (threadIdx.x == 0) stamp(3);
     tc_fence_after();
@@ -462,23 +353,17 @@ size_t gemm_partials_bytes(const GemmShape& s) {
 size_t gemm_workspace_bytes(const GemmShape& s) { return kGemmCounterBytes + gemm_partials_bytes(s); }
 
 namespace {
-// xhat: bytes of the normalised X operand (kNorm; the ring then holds weight tiles only).
-int tc_stages(int BN, size_t xhat, size_t* smem_bytes) {
-  const size_t stage = kWTileBytes + (xhat ? 0 : static_cast<size_t>(BN) * kTileK * 2);
+int tc_stages(int BN, size_t* smem_bytes) {
+  const size_t stage = kWTileBytes + static_cast<size_t>(BN) * kTileK * 2;
   const size_t tile = static_cast<size_t>(BN) * kEpiPitch * 4;
   // About 110 KB of ring lets a CTA of the next GEMM share the SM and prefetch its weights
   // (measured 1.343 vs 1.361 ms per verify with the 200 KB ring).
-  const size_t budget = 110 * 1024 - xhat;
+  const size_t budget = 110 * 1024;
   int stages = static_cast<int>(std::min<size_t>(8, budget / stage));
   while (static_cast<size_t>(stages) * stage < tile) ++stages;
   stages = std::max(stages, 2);
-  *smem_bytes = 1024 + stages * stage + 256 + (xhat ? 1024 + xhat : 0);
+  *smem_bytes = 1024 + stages * stage + 256;
   return stages;
-}
-
-size_t xhat_bytes(const GemmShape& s) {
-  const int max_nkb = (s.kblocks + s.splits - 1) / s.splits;
-  return static_cast<size_t>(max_nkb) * s.BN * 128;
 }
 
 }  // namespace
@@ -490,43 +375,29 @@ bool gemm_prepare() {
   static std::once_flag once;
   static bool ok = false;
   std::call_once(once, [] {
-    ok = cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                              cudaSharedmemCarveoutMaxShared) == cudaSuccess &&
-         cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributePreferredSharedMemoryCarveout,
+    ok = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
                               cudaSharedmemCarveoutMaxShared) == cudaSuccess;
   });
   return ok;
 }
 
-bool gemm_norm_fits(const GemmShape& s) {
-  return s.BN == 16 && s.K <= kNormMaxK && s.K % 8 == 0 && xhat_bytes(s) <= 64 * 1024;
-}
-
 int launch_gemm_tc(const GemmShape& s, const CUtensorMap& w_map, const CUtensorMap& x_map, const Epilogue& epi,
-                   GemmScratch scratch, int32_t* status, cudaStream_t stream, bool pdl, const GemmNorm* nrm) {
-  if (nrm && !gemm_norm_fits(s)) return SPECB200_ERR_UNSUPPORTED;
+                   GemmScratch scratch, int32_t* status, cudaStream_t stream, bool pdl) {
   size_t smem = 0;
-  const int stages = tc_stages(s.BN, nrm ? xhat_bytes(s) : 0, &smem);
+  const int stages = tc_stages(s.BN, &smem);
   static std::mutex mu;
-  static size_t smem_set[2] = {0, 0};
+  static size_t smem_set = 0;
   {
     std::lock_guard<std::mutex> lock(mu);
-    const int which = nrm ? 1 : 0;
-    if (smem > smem_set[which]) {
-      const cudaError_t ea =
-          nrm ? cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))
-              : cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     static_cast<int>(smem));
-      if (ea != cudaSuccess) return SPECB200_ERR_CUDA;
-      smem_set[which] = smem;
+    if (smem > smem_set) {
+      if (cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
+          cudaSuccess)
+        return SPECB200_ERR_CUDA;
+      smem_set = smem;
     }
   }
-  const GemmNorm none{};
-  cudaError_t err =
-      nrm ? launch_kernel(gemm_tc_kernel<true>, dim3(s.n_tiles, s.splits, s.m_tiles), dim3(kTcThreads), smem, stream, pdl,
-                          w_map, x_map, s, epi, scratch, status, stages, *nrm)
-          : launch_kernel(gemm_tc_kernel<false>, dim3(s.n_tiles, s.splits, s.m_tiles), dim3(kTcThreads), smem, stream,
-                          pdl, w_map, x_map, s, epi, scratch, status, stages, none);
+  const cudaError_t err = launch_kernel(gemm_tc_kernel, dim3(s.n_tiles, s.splits, s.m_tiles), dim3(kTcThreads), smem,
+                                        stream, pdl, w_map, x_map, s, epi, scratch, status, stages);
   return err == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
 }
 

@@ -65,22 +65,11 @@ struct GemmScratch {
 };
 constexpr int kGemmTraceCtas = 512;
 size_t gemm_partials_bytes(const GemmShape& s);
-// RMSNorm folded into the tcgen05 GEMM's X operand (LlamaRMSNorm of rows of x, as
-// rmsnorm_kernel): used when gemm_norm_fits(s).
-struct GemmNorm {
-  const __nv_bfloat16* x = nullptr;  // residual stream [rows, K]
-  const __nv_bfloat16* w = nullptr;  // norm weight [K]
-  const int32_t* sel_n_new = nullptr;  // output row b reads row b * T + n_new[b] - 1 (last token)
-  int T_tokens = 1;
-  float eps = 0.f;
-};
-bool gemm_norm_fits(const GemmShape& s);
 // Function attributes of the GEMM kernels (largest shared-memory carveout); call outside any
 // stream capture.
 bool gemm_prepare();
-// nrm == nullptr: X through x_map; else X = RMSNorm(nrm) built in shared memory (x_map unused).
 int launch_gemm_tc(const GemmShape& s, const CUtensorMap& w_map, const CUtensorMap& x_map, const Epilogue& epi,
-                   GemmScratch scratch, int32_t* status, cudaStream_t stream, bool pdl, const GemmNorm* nrm = nullptr);
+                   GemmScratch scratch, int32_t* status, cudaStream_t stream, bool pdl);
 template <typename T>
 int launch_gemm_simt(const GemmShape& s, const T* w, const T* x, const Epilogue& epi, GemmScratch scratch,
                      int32_t* status, cudaStream_t stream, bool pdl);

@@ -88,26 +88,11 @@ constexpr size_t kAttnCounterBytes = kAttnMaxCounters * sizeof(int);
 struct AttnPlan {
   int chunk, splits_max, qtiles;
   // 1: tensor-core decode items (bf16, d = 64, at most 16 query rows per KV head);
-  // 2: the cluster kernel for the same shapes (splits_max = cluster size, chunk = keys per CTA);
-  // 3: the cluster kernel with the o projection behind it; 4: with the q/k/v projection in front
+  // 2: the cluster kernel for the same shapes (splits_max = cluster size, chunk = keys per CTA)
   int mma = 0;
 };
 // Sets the cluster kernel's shared-memory limit; call outside any stream capture.
 bool attention_prepare();
-// Attention of every KV head of a sequence in one cluster followed by the o projection and the
-// residual add into hidden (decode steps of small bf16 models, d = 64). Plans P CTAs per KV
-// head and `rows` o rows per CTA; false when the shape does not fit.
-bool plan_attention_o(int B, int T, int Hq, int Hkv, int D, int H, int max_kv_len, AttnPlan* p, int* P, int* rows);
-int launch_attention_o(const AttnArgs& a, const AttnPlan& p, int P, int rows, const __nv_bfloat16* w_o,
-                       __nv_bfloat16* hidden, int H, cudaStream_t s, bool pdl);
-// Decode steps of small bf16 models (d = 64, T <= 4): the q/k/v projection (RMSNorm of the
-// residual stream x, the q/k/v weight rows, RoPE, the new keys and values into the pool at the
-// prep kernel's slots) computed by each KV head's attention cluster in front of its attention,
-// `pairs` rotary pairs per CTA; plan_attention_qkv returns false when the shape does not fit.
-bool plan_attention_qkv(int T, int Hq, int Hkv, int D, int H, int max_kv_len, AttnPlan* p, int* pairs);
-int launch_attention_qkv(const AttnArgs& a, const AttnPlan& p, int pairs, const __nv_bfloat16* w_qkv,
-                         const __nv_bfloat16* x, const __nv_bfloat16* norm_w, const int32_t* slot, float eps, int H,
-                         cudaStream_t s, bool pdl);
 // tensor_items: the call is bf16 with d = 64, so decode / verify shapes (T x G <= 16) may use
 // the tensor-core items (attn_item_mma.cuh).
 AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len, bool tensor_items);

@@ -32,13 +32,12 @@ class ModelConfig(ctypes.Structure):
 
 class LayerWeights(ctypes.Structure):
     _fields_ = [("attn_norm", c_void_p), ("w_qkv", c_void_p), ("w_o", c_void_p), ("mlp_norm", c_void_p),
-                ("w_gate_up", c_void_p), ("w_down", c_void_p), ("p_qkv", c_void_p), ("p_o", c_void_p),
-                ("p_gate_up", c_void_p), ("p_down", c_void_p)]
+                ("w_gate_up", c_void_p), ("w_down", c_void_p)]
 
 
 class ModelWeights(ctypes.Structure):
     _fields_ = [("embed", c_void_p), ("final_norm", c_void_p), ("lm_head", c_void_p), ("rope_cos", c_void_p),
-                ("rope_sin", c_void_p), ("layers", ctypes.POINTER(LayerWeights)), ("p_lm_head", c_void_p)]
+                ("rope_sin", c_void_p), ("layers", ctypes.POINTER(LayerWeights))]
 
 
 class Batch(ctypes.Structure):
@@ -65,13 +64,11 @@ PROTOTYPES: dict[str, tuple] = {
     "specb200_verify_ids": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p,
                                     c_void_p, c_void_p]),
     "specb200_scatter_tokens": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
-    "specb200_packed_tile_bytes": (c_size_t, [c_int, c_int]),
-    "specb200_pack_tiles": (c_int, [c_void_p, c_int, c_int, c_void_p, c_void_p]),
     "specb200_model_create": (c_int, [ctypes.POINTER(ModelConfig), ctypes.POINTER(ModelWeights),
                                       ctypes.POINTER(c_void_p)]),
     "specb200_model_destroy": (c_int, [c_void_p]),
     "specb200_forward_workspace_bytes": (c_size_t, [c_void_p, c_int, c_int, c_int]),
-    "specb200_forward_uses_stream": (c_int, [c_void_p, c_int, c_int]),
+    "specb200_forward_schedule": (c_int, [c_void_p, c_int, c_int]),
     "specb200_forward_launches": (c_int, [c_void_p, c_int, c_int]),
     "specb200_forward": (c_int, [c_void_p, ctypes.POINTER(Batch), c_void_p, c_size_t, c_void_p]),
     "specb200_rmsnorm": (c_int, [c_int, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p]),

@@ -92,23 +92,13 @@ class Engine:
             self.rope_cos = (freqs.cos() * scaling).to(device).contiguous()
             self.rope_sin = (freqs.sin() * scaling).to(device).contiguous()
 
-        # bf16 models also get their matrices in the tile-packed layout the layer-stream
-        # kernel streams (decode and verify calls with at most 16 token rows).
-        self.packed = dtype == torch.bfloat16
-        with torch.cuda.device(device):
-            for L in self.layers:
-                for name in ("w_qkv", "w_o", "w_gate_up", "w_down"):
-                    L["p_" + name[2:]] = self._pack(L[name]) if self.packed else None
-            self.p_lm_head = self._pack(self.lm_head) if self.packed else None
         self._c_layers = (_ffi.LayerWeights * self.n_layers)()
         for i, L in enumerate(self.layers):
             self._c_layers[i] = _ffi.LayerWeights(ptr(L["attn_norm"]), ptr(L["w_qkv"]), ptr(L["w_o"]), ptr(L["mlp_norm"]),
-                                                  ptr(L["w_gate_up"]), ptr(L["w_down"]), ptr(L["p_qkv"]), ptr(L["p_o"]),
-                                                  ptr(L["p_gate_up"]), ptr(L["p_down"]))
+                                                  ptr(L["w_gate_up"]), ptr(L["w_down"]))
         self._c_weights = _ffi.ModelWeights(ptr(self.embed), ptr(self.final_norm), ptr(self.lm_head),
                                             ptr(self.rope_cos), ptr(self.rope_sin),
-                                            ctypes.cast(self._c_layers, ctypes.POINTER(_ffi.LayerWeights)),
-                                            ptr(self.p_lm_head))
+                                            ctypes.cast(self._c_layers, ctypes.POINTER(_ffi.LayerWeights)))
         self._c_config = _ffi.ModelConfig(self.n_layers, self.hidden, self.n_heads, self.n_kv_heads, self.head_dim,
                                           self.intermediate, self.vocab, self.eps,
                                           _ffi.BF16 if dtype == torch.bfloat16 else _ffi.F32, self.max_positions)
@@ -117,13 +107,6 @@ class Engine:
             raise_for(lib().specb200_model_create(ctypes.byref(self._c_config), ctypes.byref(self._c_weights),
                                                   ctypes.byref(handle)), "specb200_model_create")
         self.handle = handle
-
-    @staticmethod
-    def _pack(w: torch.Tensor) -> torch.Tensor:
-        n, k = w.shape
-        out = torch.empty(lib().specb200_packed_tile_bytes(n, k), dtype=torch.uint8, device=w.device)
-        raise_for(lib().specb200_pack_tiles(ptr(w), n, k, ptr(out), stream_ptr(w.device)), "specb200_pack_tiles")
-        return out
 
     def __del__(self) -> None:
         h = getattr(self, "handle", None)
@@ -136,11 +119,10 @@ class Engine:
         return lib().specb200_forward_launches(self.handle, b, t)
 
     def schedule(self, b: int, t: int) -> str:
-        """The schedule a forward call of B rows x T tokens runs: "chain" (one thread-block
-        cluster), "stream" (persistent kernel over all SMs), "gemv" (decode steps of at most 4
-        token rows: a kernel per linear with the norms folded in) or "layers" (a kernel per op)."""
-        code = lib().specb200_forward_uses_stream(self.handle, b, t)
-        return {2: "chain", 1: "stream", 3: "gemv"}.get(code, "layers")
+        """The schedule a forward call of B rows x T tokens runs: "gemv" (decode steps of at most
+        4 token rows: a kernel per linear with the norms folded in) or "layers" (a kernel per op)."""
+        code = lib().specb200_forward_schedule(self.handle, b, t)
+        return {3: "gemv"}.get(code, "layers")
 
     def workspace_bytes(self, b: int, t: int, max_kv_len: int) -> int:
         return lib().specb200_forward_workspace_bytes(self.handle, b, t, max_kv_len)

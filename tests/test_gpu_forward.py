@@ -295,113 +295,12 @@ def test_verify_invariant_raises(tiny):
         verify(tiny, cache, [0], [[1, 2, 3]], torch.tensor([[4, 5]]), 0.0)
 
 
-def test_stream_kernel_matches_per_layer_kernels(monkeypatch):
-    """The persistent layer-stream kernel (decode/verify shapes) against the per-layer kernels
-    on identical inputs and weights at the 1.7B width (2 layers). The two sum in different
-    orders (stream-K vs split-K), so a bf16 activation can round one ulp apart and the logits
-    differ by bf16 noise: within 1e-2 of the logit scale, argmax equal except at near ties."""
-    from cache.kv import KVCache
-    from specb200.engine import Engine
-
-    model = _bf16_model(2048, 2, 32, 32, 8192, 49152, seed=3, theta=130000.0).to(DEV)
-    per_layer = Engine(model)
-    monkeypatch.setenv("SPECB200_STREAM", "1")
-    stream = Engine(model)
-    assert per_layer.schedule(1, 5) == "layers" and stream.schedule(1, 5) == "stream"
-    prompt = torch.randint(0, 49152, (1, 300), generator=torch.Generator().manual_seed(4))
-    outs = []
-    for eng in (per_layer, stream):
-        cache = KVCache.for_model(model.config, num_blocks=64, block_size=16, dtype=torch.bfloat16, device=DEV)
-        cache.add(0)
-        eng.forward(cache, [0], prompt, [300], last_only=True)
-        steps = [eng.forward(cache, [0], torch.tensor([[5, 6, 7, 8, 9]]), [5])]
-        steps.append(eng.forward(cache, [0], torch.tensor([[11]]), [1], last_only=True))
-        outs.append([x.float().cpu() for x in steps])
-    for a, b in zip(*outs):
-        scale = a.abs().max().item()
-        assert (a - b).abs().max().item() <= 1e-2 * scale
-        top2 = a.topk(2, dim=-1).values
-        agree = a.argmax(-1) == b.argmax(-1)
-        assert bool((agree | ((top2[..., 0] - top2[..., 1]) < 1e-2 * scale)).all())
-
-
-def _decode_steps(eng, model, prompt_len: int, seqs: int = 1):
-    """Prefill `seqs` sequences of different lengths, then a 5-token verify-shaped step, a
-    1-token draft-shaped step and a ragged 2-row step (4 tokens, 3 valid in row 1); returns the
-    logits of the three decode-shaped steps and the final KV pools."""
-    from cache.kv import KVCache
-
-    cache = KVCache.for_model(model.config, num_blocks=96, block_size=16, dtype=torch.bfloat16, device=DEV)
-    outs = []
-    for s in range(2):
-        cache.add(s)
-        n = prompt_len - 37 * s
-        p = torch.randint(0, model.config.vocab_size, (1, n), generator=torch.Generator().manual_seed(40 + s))
-        eng.forward(cache, [s], p, [n], last_only=True)
-    outs.append(eng.forward(cache, [0], torch.tensor([[5, 6, 7, 8, 9]]), [5]))
-    outs.append(eng.forward(cache, [0], torch.tensor([[11]]), [1], last_only=True))
-    outs.append(eng.forward(cache, [0, 1], torch.tensor([[12, 13, 14, 15], [16, 17, 18, 0]]), [4, 3]))
-    return [x.float().cpu() for x in outs], cache
-
-
-@pytest.mark.parametrize("fma", ["0", "1"])
-def test_chain_kernel_matches_per_layer_kernels(monkeypatch, fma):
-    """The cluster layer-chain kernel (small models, at most 8 token rows) against the
-    per-layer kernels on the 135M draft architecture (2 layers): verify-, draft- and ragged
-    2-row shapes. Both sum the split-K partials in different orders, so logits agree to bf16
-    noise (1e-2 of the logit scale, argmax equal except at near ties) and the KV entries the
-    calls wrote agree to one bf16 ulp of their scale. Both GEMM back ends are covered: tcgen05
-    MMAs and (for calls of at most two rows) CUDA-core FMAs."""
-    from specb200.engine import Engine
-
-    model = _bf16_model(576, 2, 9, 3, 1536, 49152, seed=5, theta=100000.0).to(DEV)
-    per_layer = Engine(model)
-    monkeypatch.setenv("SPECB200_CHAIN", "1")
-    monkeypatch.setenv("SPECB200_CHAIN_FMA", fma)
-    chain = Engine(model)
-    assert per_layer.schedule(1, 5) == "layers"
-    assert chain.schedule(1, 5) == "chain" and chain.schedule(1, 1) == "chain" and chain.schedule(2, 4) == "chain"
-    (la, ca), (lb, cb) = _decode_steps(per_layer, model, 300), _decode_steps(chain, model, 300)
-    for a, b in zip(la, lb):
-        scale = a.abs().max().item()
-        assert (a - b).abs().max().item() <= 1e-2 * scale, ((a - b).abs().max().item(), scale)
-        top2 = a.topk(2, dim=-1).values
-        agree = a.argmax(-1) == b.argmax(-1)
-        assert bool((agree | ((top2[..., 0] - top2[..., 1]) < 1e-2 * scale)).all())
-    for pa, pb in ((ca.k, cb.k), (ca.v, cb.v)):
-        d = (pa.float() - pb.float()).abs().max().item()
-        assert d <= 2 ** -7 * pa.float().abs().max().item(), d
-
-
-def test_chain_kernel_matches_oracle(monkeypatch):
-    """The cluster layer-chain kernel against the bf16 oracle after a prefill: 5-token and
-    1-token steps of the 135M draft architecture (2 layers), logits within rtol 2e-2."""
-    from lm.forward import forward
-    from specb200.engine import engine_for
-
-    monkeypatch.setenv("SPECB200_CHAIN", "1")
-    model = _bf16_model(576, 2, 9, 3, 1536, 49152, seed=12, theta=100000.0)
-    w = ofw.weights_from_model(model)
-    prec = ofw.Precision("bf16")
-    model = model.to(DEV)
-    assert engine_for(model).schedule(1, 5) == "chain"
-    cache = new_cache(model, block_size=16)
-    ocache = ofw.Cache(w, 4096, 16, prec)
-    cache.add(0)
-    ocache.add(0)
-    prompt = torch.randint(0, 49152, (1, 70), generator=torch.Generator().manual_seed(7)).numpy()
-    for ids_np, n_new in [(prompt, [70]), (np.array([[1, 2, 3, 4, 5]]), [5]), (np.array([[6]]), [1])]:
-        got = forward(model, cache, [0], torch.from_numpy(ids_np), n_new).float().cpu().numpy()
-        want = ofw.forward(w, ocache, [0], ids_np, n_new, prec)
-        g, o = got[0, : n_new[0]], want[0, : n_new[0]]
-        scale = np.abs(o).max()
-        assert np.abs(g - o).max() <= 2e-2 * scale + 1e-3, (np.abs(g - o).max(), scale)
-
-
-def _gemv_steps(eng, model, prompt_len: int = 300):
+def _gemv_steps(eng, model, prompt_len: int = 300, pad_to: int = 0):
     """Prefill two sequences, then decode-sized calls (at most 4 token rows) of every shape the
     GEMV schedule serves: 1 row x 1 token, 2 rows x 1 token (last rows), 2 rows x 2 tokens with
-    a ragged row, 1 row x 3 tokens. Returns their logits and the final KV pools."""
+    a ragged row, 1 row x 3 tokens. With pad_to, every call is right-padded to that many tokens
+    per row (padding writes no K/V), which moves it to the per-layer kernels. Returns the real
+    rows' logits and the final KV pools."""
     from cache.kv import KVCache
 
     cache = KVCache.for_model(model.config, num_blocks=96, block_size=16, dtype=torch.bfloat16, device=DEV)
@@ -410,63 +309,38 @@ def _gemv_steps(eng, model, prompt_len: int = 300):
         n = prompt_len - 37 * s
         p = torch.randint(0, model.config.vocab_size, (1, n), generator=torch.Generator().manual_seed(50 + s))
         eng.forward(cache, [s], p, [n], last_only=True)
-    outs = [eng.forward(cache, [0], torch.tensor([[11]]), [1], last_only=True),
-            eng.forward(cache, [0, 1], torch.tensor([[12], [13]]), [1, 1], last_only=True),
-            eng.forward(cache, [0, 1], torch.tensor([[14, 15], [16, 0]]), [2, 1]),
-            eng.forward(cache, [1], torch.tensor([[17, 18, 19]]), [3])]
-    return [x.float().cpu() for x in outs], cache
+
+    def call(seqs, rows, n_new, last_only=False):
+        width = max(pad_to, max(len(r) for r in rows))
+        ids = torch.tensor([r + [0] * (width - len(r)) for r in rows])
+        out = eng.forward(cache, seqs, ids, n_new, last_only=last_only).float().cpu()
+        return out if last_only else torch.cat([out[b, :n] for b, n in enumerate(n_new)])
+
+    outs = [call([0], [[11]], [1], True), call([0, 1], [[12], [13]], [1, 1], True),
+            call([0, 1], [[14, 15], [16]], [2, 1]), call([1], [[17, 18, 19]], [3])]
+    return outs, cache
 
 
 @pytest.mark.parametrize("dims", [(576, 2, 9, 3, 1536, 49152), (256, 2, 4, 4, 512, 49152),
                                   (128, 2, 4, 2, 256, 512)])
-def test_gemv_schedule_matches_per_layer_kernels(monkeypatch, dims):
-    """Decode-sized calls on the GEMV kernels (norms folded in, no split-K) against the
-    tensor-core per-layer kernels on identical inputs: the 135M draft width, a narrow model
-    with the same vocabulary and a head_dim-32 model with a small one (whose LM head is a GEMV
-    too), 2 layers each. The two sum in different orders, so logits agree to bf16 noise (1e-2
-    of the logit scale, argmax equal except at near ties) and the KV entries the calls wrote
-    to one bf16 ulp of their scale."""
+def test_gemv_schedule_matches_per_layer_kernels(dims):
+    """Decode-sized calls on the GEMV kernels (norms folded in, no split-K) against the same
+    tokens padded to 5 per row, which run on the tensor-core per-layer kernels: the 135M draft
+    width, a narrow model with the same vocabulary and a head_dim-32 model with a small one
+    (whose LM head is a GEMV too), 2 layers each. The two sum in different orders, so logits
+    agree to bf16 noise (1e-2 of the logit scale, argmax equal except at near ties) and the KV
+    entries the calls wrote to one bf16 ulp of their scale."""
     from specb200.engine import Engine
 
     model = _bf16_model(*dims, seed=8, theta=100000.0).to(DEV)
-    monkeypatch.setenv("SPECB200_GEMV", "0")
-    per_layer = Engine(model)
-    monkeypatch.delenv("SPECB200_GEMV")
-    gemv = Engine(model)
-    assert per_layer.schedule(1, 1) == "layers" and per_layer.schedule(2, 2) == "layers"
-    assert gemv.schedule(1, 1) == "gemv" and gemv.schedule(2, 2) == "gemv" and gemv.schedule(1, 3) == "gemv"
+    eng = Engine(model)
+    assert eng.schedule(1, 1) == "gemv" and eng.schedule(2, 2) == "gemv" and eng.schedule(1, 3) == "gemv"
+    assert eng.schedule(1, 5) == "layers" and eng.schedule(2, 5) == "layers"
     # prep, 5 per layer, then the LM head: a GEMV with the final norm folded in (small vocabulary)
     # or the final norm and the tensor-core GEMM
     head_launches = 1 if dims[-1] <= 4096 else 2
-    assert gemv.schedule(1, 5) == "layers" and gemv.launches(1, 1) == 1 + head_launches + 5 * 2
-    (la, ca), (lb, cb) = _gemv_steps(per_layer, model), _gemv_steps(gemv, model)
-    for a, b in zip(la, lb):
-        scale = a.abs().max().item()
-        assert (a - b).abs().max().item() <= 1e-2 * scale, ((a - b).abs().max().item(), scale)
-        top2 = a.topk(2, dim=-1).values
-        agree = a.argmax(-1) == b.argmax(-1)
-        assert bool((agree | ((top2[..., 0] - top2[..., 1]) < 1e-2 * scale)).all())
-    for pa, pb in ((ca.k, cb.k), (ca.v, cb.v)):
-        d = (pa.float() - pb.float()).abs().max().item()
-        assert d <= 2 ** -7 * pa.float().abs().max().item(), d
-
-
-@pytest.mark.parametrize("dims", [(576, 2, 9, 3, 1536, 49152), (256, 2, 4, 4, 512, 49152)])
-def test_qkv_in_attention_clusters_matches_gemv_schedule(monkeypatch, dims):
-    """SPECB200_DRAFT_QKV=1: each KV head's attention cluster computes its own q/k/v rows (one
-    launch fewer per layer) against the separate q/k/v GEMV on identical inputs. The norm is
-    the same; only the dot products' summation order differs, so logits agree to bf16 noise
-    and the KV entries the calls wrote to one bf16 ulp of their scale."""
-    from specb200.engine import Engine
-
-    model = _bf16_model(*dims, seed=21, theta=100000.0).to(DEV)
-    gemv = Engine(model)
-    monkeypatch.setenv("SPECB200_DRAFT_QKV", "1")
-    fused = Engine(model)
-    head_launches = 1 if dims[-1] <= 4096 else 2
-    assert fused.schedule(1, 1) == "gemv" and gemv.launches(1, 1) == 1 + head_launches + 5 * 2
-    assert fused.launches(1, 1) == 1 + head_launches + 4 * 2
-    (la, ca), (lb, cb) = _gemv_steps(gemv, model), _gemv_steps(fused, model)
+    assert eng.launches(1, 1) == 1 + head_launches + 5 * 2 and eng.launches(1, 5) == 3 + 7 * 2
+    (la, ca), (lb, cb) = _gemv_steps(eng, model, pad_to=5), _gemv_steps(eng, model)
     for a, b in zip(la, lb):
         scale = a.abs().max().item()
         assert (a - b).abs().max().item() <= 1e-2 * scale, ((a - b).abs().max().item(), scale)
@@ -505,86 +379,3 @@ def test_gemv_schedule_matches_oracle(dims):
             g, o = got[b, :n], want[b, :n]
             scale = np.abs(o).max()
             assert np.abs(g - o).max() <= 2e-2 * scale + 1e-3, (b, np.abs(g - o).max(), scale)
-
-
-def test_attention_o_kernel_matches_separate_launches():
-    """The opt-in fused attention + o projection (one cluster of P CTAs per KV head per
-    sequence, SPECB200_ATTN_O=1, read once per process) against the separate cluster attention
-    and o GEMV, in a child process: 1- and 2-token steps of the 135M draft width."""
-    import subprocess
-    import sys
-    import textwrap
-    code = textwrap.dedent('''
-        import os, sys, torch
-        sys.path[:0] = ["tests", "speculative-decoder_b200", "."]
-        from test_gpu_forward import _bf16_model, _gemv_steps
-        from specb200.engine import Engine
-        model = _bf16_model(576, 2, 9, 3, 1536, 49152, seed=31, theta=100000.0).to("cuda")
-        fused = Engine(model)
-        assert fused.launches(1, 1) == 3 + 4 * 2, fused.launches(1, 1)
-        (la, ca) = _gemv_steps(fused, model)
-        os.environ["SPECB200_GEMV"] = "0"
-        ref = Engine(model)
-        (lb, cb) = _gemv_steps(ref, model)
-        for a, b in zip(la, lb):
-            scale = a.abs().max().item()
-            assert (a - b).abs().max().item() <= 1e-2 * scale, ((a - b).abs().max().item(), scale)
-        for pa, pb in ((ca.k, cb.k), (ca.v, cb.v)):
-            d = (pa.float() - pb.float()).abs().max().item()
-            assert d <= 2 ** -7 * pa.float().abs().max().item(), d
-        print("ok")
-    ''')
-    env = dict(__import__("os").environ, SPECB200_ATTN_O="1")
-    res = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, env=env, timeout=600)
-    assert res.returncode == 0 and "ok" in res.stdout, res.stdout + res.stderr
-
-
-@pytest.mark.parametrize("dims", [(2048, 2, 32, 32, 8192, 49152), (576, 2, 9, 3, 1536, 49152)])
-def test_gemm_norm_matches_separate_norm(monkeypatch, dims):
-    """Verify-sized calls (5 and 2 x 4 ragged tokens, all rows and last rows only) on four
-    per-layer variants: separate RMSNorm launches after residual-add epilogues; the o and down
-    GEMMs storing split partials that the next RMSNorm launch adds to the residual stream; that
-    plus the q/k/v GEMM storing partials that the cluster attention sums, rotates and writes to
-    the pool (the default); and the RMSNorms folded into the GEMMs. Same roundings, sums in
-    other orders, so logits and the pools agree to bf16 noise; the folded schedule makes
-    2 + 5 L launches."""
-    from cache.kv import KVCache
-    from specb200.engine import Engine
-
-    model = _bf16_model(*dims, seed=21, theta=130000.0).to(DEV)
-    monkeypatch.setenv("SPECB200_GEMV", "0")
-    monkeypatch.setenv("SPECB200_GEMM_NORM", "0")
-    monkeypatch.setenv("SPECB200_DEFER_RESID", "0")
-    separate = Engine(model)
-    monkeypatch.setenv("SPECB200_DEFER_RESID", "1")
-    monkeypatch.setenv("SPECB200_DEFER_QKV", "0")
-    deferred = Engine(model)  # o / down partials summed into the residual by the next norm launch
-    monkeypatch.setenv("SPECB200_DEFER_QKV", "1")
-    deferred_qkv = Engine(model)  # ... and q/k/v partials summed, rotated and stored by the attention
-    monkeypatch.setenv("SPECB200_GEMM_NORM", "1")
-    fused = Engine(model)
-    assert separate.launches(1, 5) == 3 + 7 * 2 and fused.launches(1, 5) == 2 + 5 * 2
-    assert deferred.launches(1, 5) == 3 + 7 * 2 and deferred_qkv.launches(1, 5) == 3 + 7 * 2
-    outs, caches = [], []
-    for eng in (separate, deferred, deferred_qkv, fused):
-        cache = KVCache.for_model(model.config, num_blocks=96, block_size=16, dtype=torch.bfloat16, device=DEV)
-        for s in range(2):
-            cache.add(s)
-            p = torch.randint(0, dims[-1], (1, 200 - 37 * s), generator=torch.Generator().manual_seed(60 + s))
-            eng.forward(cache, [s], p, [200 - 37 * s], last_only=True)
-        steps = [eng.forward(cache, [0], torch.tensor([[5, 6, 7, 8, 9]]), [5]),
-                 eng.forward(cache, [0, 1], torch.tensor([[10, 11, 12, 13], [14, 15, 16, 0]]), [4, 3], last_only=True),
-                 eng.forward(cache, [1], torch.tensor([[17, 18, 19, 20, 21]]), [5], last_only=True)]
-        outs.append([x.float().cpu() for x in steps])
-        caches.append(cache)
-    for other in outs[1:]:
-        for a, b in zip(outs[0], other):
-            scale = a.abs().max().item()
-            assert (a - b).abs().max().item() <= 1e-2 * scale, ((a - b).abs().max().item(), scale)
-            top2 = a.topk(2, dim=-1).values
-            agree = a.argmax(-1) == b.argmax(-1)
-            assert bool((agree | ((top2[..., 0] - top2[..., 1]) < 1e-2 * scale)).all())
-    for other in caches[1:]:  # the keys and values every variant wrote to the pool
-        for pa, pb in ((caches[0].k, other.k), (caches[0].v, other.v)):
-            d = (pa.float() - pb.float()).abs().max().item()
-            assert d <= 2 ** -7 * pa.float().abs().max().item(), d
