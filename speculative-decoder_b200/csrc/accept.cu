@@ -648,7 +648,8 @@ namespace specb200 {
 namespace {
 // Both kernels on `s`: the counters are cleared first (a call with another B may have left
 // statistics where they sit); the residual kernel follows with programmatic dependent launch.
-int launch_accept(AcceptArgs& a, char* ws, const AcceptLayout& l, cudaStream_t s) {
+// Returns the first CUDA error met (memsets or launches), cudaSuccess otherwise.
+cudaError_t launch_accept(AcceptArgs& a, char* ws, const AcceptLayout& l, cudaStream_t s) {
   a.counters = reinterpret_cast<int*>(ws + l.counters);
   a.stats = reinterpret_cast<RowStat*>(ws + l.stats);
   a.nsel = reinterpret_cast<int*>(ws + l.nsel);
@@ -660,15 +661,17 @@ int launch_accept(AcceptArgs& a, char* ws, const AcceptLayout& l, cudaStream_t s
   a.rclen = ((a.V + a.nrc - 1) / a.nrc + 3) / 4 * 4;
   a.rcounters = a.counters + 2 * a.B;
   a.cstats = reinterpret_cast<RowStat*>(ws + l.cstats);
-  if (a.status) cudaMemsetAsync(a.status, 0, sizeof(int32_t), s);
-  cudaMemsetAsync(a.counters, 0, (2 * static_cast<size_t>(a.B) + (a.nrc > 1 ? static_cast<size_t>(a.B) * a.R : 0)) * sizeof(int),
-                  s);
   cudaError_t e = cudaSuccess;
+  if (a.status) e = cudaMemsetAsync(a.status, 0, sizeof(int32_t), s);
+  if (e != cudaSuccess) return e;
+  e = cudaMemsetAsync(a.counters, 0,
+                      (2 * static_cast<size_t>(a.B) + (a.nrc > 1 ? static_cast<size_t>(a.B) * a.R : 0)) * sizeof(int), s);
+  if (e != cudaSuccess) return e;
   accept_kernel<<<static_cast<unsigned>(a.R) * a.B * a.nrc, kAcceptThreads, 0, s>>>(a);
   e = cudaGetLastError();
   if (e == cudaSuccess && !a.greedy && !a.decide_only)
     e = launch_kernel(residual_kernel, dim3(static_cast<unsigned>(a.C) * a.B), dim3(kAcceptThreads), 0, s, true, a);
-  return e == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
+  return e;
 }
 }  // namespace
 }  // namespace specb200
@@ -715,8 +718,8 @@ extern "C" int specb200_accept(const float* p, const float* q, const int64_t* dr
   a.status = status;
   const AcceptLayout l = accept_layout(B, k, V);
   if (l.total > workspace_bytes) return specb200_set_error(SPECB200_ERR_WORKSPACE, "accept: workspace too small");
-  if (launch_accept(a, static_cast<char*>(workspace), l, static_cast<cudaStream_t>(stream)) != SPECB200_OK)
-    return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+  const cudaError_t e = launch_accept(a, static_cast<char*>(workspace), l, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
   return SPECB200_OK;
 }
 
@@ -822,7 +825,7 @@ extern "C" int specb200_accept_noalloc(const float* p, const float* q, const int
   const AcceptLayout l = accept_layout(B, k, V);
   if (l.total > kNoAllocScratchBytes) return specb200_set_error(SPECB200_ERR_ARG, "accept_noalloc: scratch too small");
   // the array keeps old tickets: launch_accept clears the counters first
-  if (launch_accept(a, static_cast<char*>(scratch), l, static_cast<cudaStream_t>(stream)) != SPECB200_OK)
-    return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(cudaGetLastError()));
+  const cudaError_t e = launch_accept(a, static_cast<char*>(scratch), l, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
   return SPECB200_OK;
 }

@@ -4,8 +4,11 @@ ranges, no collective inside a round, and one gather of tokens and statistics at
 The reference runs every request in one process (spec/loop.py:38-104); requests are fully
 independent there (each has its own context, cache sequence and draft state), so splitting
 the prompt list into contiguous ranges and concatenating the per-range outputs in rank order
-returns exactly what one process would. Statistics merge by addition, except the per-round
-lists (`emitted_per_round`, `drafted_per_round`), which concatenate in rank order.
+returns exactly what one process would. The statistics counters merge by addition, except
+`rounds`: one process steps its whole batch round by round until the longest request is done,
+so its round count is the largest of the ranks' counts. The per-(sequence, round) lists
+(`emitted_per_round`, `drafted_per_round`) hold the same entries as one process's, grouped by
+rank instead of interleaved round by round.
 
 The gather is the only collective: `torch.distributed` all_gather of a padded int64 payload
 (NCCL over NVLink on GPUs, gloo on CPU). It runs after the timed region, carries kilobytes,
@@ -64,7 +67,9 @@ def _unpack(flat: list[int]) -> tuple[list[list[int]], SpecStats]:
 
 
 def merge_stats(parts: Sequence[SpecStats]) -> SpecStats:
-    """Sum counters; concatenate per-round lists in order."""
+    """Sum the counters, take the largest round count (the batch loop of one process runs as
+    many rounds as its longest request needs), and concatenate the per-(sequence, round) lists
+    in rank order."""
     if not parts:
         raise ValueError("no statistics to merge")
     k = parts[0].k
@@ -72,7 +77,7 @@ def merge_stats(parts: Sequence[SpecStats]) -> SpecStats:
     for st in parts:
         if st.k != k:
             raise ValueError(f"draft length differs across ranks: {st.k} != {k}")
-        out.rounds += st.rounds
+        out.rounds = max(out.rounds, st.rounds)
         out.drafted += st.drafted
         out.accepted += st.accepted
         out.attempts = [a + b for a, b in zip(out.attempts, st.attempts)]

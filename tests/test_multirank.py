@@ -18,19 +18,25 @@ K = 4
 
 
 def fake_generate(prompts: list[list[int]]) -> tuple[list[list[int]], SpecStats]:
-    """Per-request outputs and statistics that depend only on the request itself."""
+    """Per-request outputs and statistics that depend only on the request itself, with the
+    batch semantics of spec.loop.generate: the batch runs as many rounds as its longest
+    request needs, and the per-(sequence, round) lists are filled round by round."""
     st = SpecStats(k=K)
-    outs = []
+    outs, lengths = [], []
     for p in prompts:
         n = 1 + (sum(p) % 7)
+        lengths.append(n)
         outs.append([(p[0] * 31 + i) % 1000 for i in range(n)])
-        st.rounds += n
         st.drafted += K * n
         st.accepted += sum(p) % (K * n + 1)
         st.attempts = [a + n for a in st.attempts]
         st.accepts = [a + (sum(p) >> i) % 2 for i, a in enumerate(st.accepts)]
-        st.emitted_per_round += [1] * n
-        st.drafted_per_round += [0] * n
+    st.rounds = max(lengths, default=0)
+    for r in range(st.rounds):
+        for b, n in enumerate(lengths):
+            if r < n:
+                st.emitted_per_round.append(1 + (b + r) % 3)
+                st.drafted_per_round.append((b + r) % 3)
     return outs, st
 
 
@@ -72,7 +78,8 @@ def test_two_rank_shard_and_gather_match_one_process(n_prompts):
         assert out == want_out, rank
         assert (rounds, drafted, accepted) == (want_st.rounds, want_st.drafted, want_st.accepted)
         assert attempts == want_st.attempts and accepts == want_st.accepts
-        assert emitted == want_st.emitted_per_round
+        # the same (sequence, round) entries, grouped by rank rather than interleaved by round
+        assert sorted(emitted) == sorted(want_st.emitted_per_round)
 
 
 def test_shard_range_covers_requests_once():
@@ -86,16 +93,16 @@ def test_shard_range_covers_requests_once():
         shard_range(4, 2, 2)
 
 
-def test_merge_stats_concatenates_rounds_in_order():
-    a, _ = fake_generate([[1, 2, 3]])
-    b, _ = fake_generate([[4, 5]])
+def test_merge_stats_takes_the_longest_round_count():
     _, sa = fake_generate([[1, 2, 3]])
     _, sb = fake_generate([[4, 5]])
+    assert sa.rounds != sb.rounds
     m = merge_stats([sa, sb])
     _, want = fake_generate([[1, 2, 3], [4, 5]])
-    assert (m.rounds, m.drafted, m.accepted, m.attempts, m.accepts) == (
-        want.rounds, want.drafted, want.accepted, want.attempts, want.accepts)
-    assert m.emitted_per_round == want.emitted_per_round
+    assert m.rounds == max(sa.rounds, sb.rounds) == want.rounds
+    assert (m.drafted, m.accepted, m.attempts, m.accepts) == (want.drafted, want.accepted, want.attempts, want.accepts)
+    assert m.emitted_per_round == sa.emitted_per_round + sb.emitted_per_round
+    assert sorted(m.emitted_per_round) == sorted(want.emitted_per_round)
     with pytest.raises(ValueError):
         merge_stats([SpecStats(k=2), SpecStats(k=3)])
 

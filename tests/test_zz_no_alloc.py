@@ -20,7 +20,9 @@ def _inputs(seed: int, B: int, k: int, V: int, temperature: float):
     g = torch.Generator().manual_seed(seed)
     pl = torch.randn(B, k + 1, V, generator=g) * 3.0
     ql = pl[:, :k] + torch.randn(B, k, V, generator=g)
-    if temperature == 0.0:
+    if k == 0:
+        draft = torch.zeros(B, 0, dtype=torch.int64)
+    elif temperature == 0.0:
         draft = ql.argmax(-1)
     else:
         draft = torch.multinomial(torch.softmax(ql / temperature, -1).reshape(-1, V), 1, generator=g).reshape(B, k)
@@ -55,15 +57,19 @@ def _no_alloc(lib, pl, ql, draft, ua, ur, flags, temperature):
 
 @pytest.mark.parametrize("temperature", [1.0, 0.0])
 def test_no_alloc_matches_workspace_entry_point_on_consecutive_calls(temperature):
-    """Two calls in a row with different inputs and batch sizes (the second starts on the
-    first one's leftover tickets and statistics): decisions and tokens identical to the
-    workspace entry point, as integers."""
+    """Calls in a row with different inputs and batch sizes (each starts on the previous one's
+    leftover tickets and statistics): decisions and tokens identical to the workspace entry
+    point, as integers."""
     from specb200 import _ffi
 
     lib = _ffi.lib()
     flags = _ffi.ACCEPT_LOGITS
-    for seed, B, V in ((11, 64, 49152), (12, 37, 5000)):
-        args = _inputs(seed, B, 4, V, temperature)
+    # Config-3 sizes take one CTA per row; the few-row shapes (the draft sampler's B = 1, k = 0
+    # and a small verify batch) split each row over column chunks whose partial statistics and
+    # row tickets also live in the shared array.
+    for seed, B, k, V in ((11, 64, 4, 49152), (12, 37, 4, 5000), (13, 1, 0, 49152), (14, 4, 4, 49152),
+                          (15, 1, 0, 49152)):
+        args = _inputs(seed, B, k, V, temperature)
         n_ref, nxt_ref, st_ref = _with_workspace(lib, *args, flags, temperature)
         n, nxt, st = _no_alloc(lib, *args, flags, temperature)
         torch.cuda.synchronize()
