@@ -35,8 +35,27 @@ import time
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
-# the package directory first: its `bench` package (the latency harness) must win over this file
-sys.path[:0] = [str(ROOT / "speculative-decoder_b200"), str(ROOT)]
+REF_INSTALL = ROOT / "baseline" / "_ref"
+
+
+def _reference_arm_requested(argv: list[str]) -> bool:
+    for i, a in enumerate(argv):
+        if a == "--impl" and i + 1 < len(argv):
+            return argv[i + 1] == "reference"
+        if a.startswith("--impl="):
+            return a.split("=", 1)[1] == "reference"
+    return False
+
+
+# The reference arm imports the unmodified reference (installed under baseline/_ref), whose
+# top-level packages (spec, cache, lm, bench, baselines) share names with the engine's; it
+# never imports the engine. Otherwise the engine's package directory comes first (its `bench`
+# package, the latency harness, must win over this file).
+REFERENCE_ARM = _reference_arm_requested(sys.argv[1:])
+if REFERENCE_ARM:
+    sys.path[:0] = ([str(REF_INSTALL)] if REF_INSTALL.is_dir() else []) + [str(ROOT)]
+else:
+    sys.path[:0] = [str(ROOT / "speculative-decoder_b200"), str(ROOT)]
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
@@ -454,11 +473,44 @@ def request_latency(target, draft, prompts, device, blocks: int, repeats: int = 
             "source": "bench.harness.measure + bench.latency.summarize (p50; device synced at each event)"}
 
 
-def cpu_baseline(target, draft, prompt: list[int], engine_rounds: int | None, max_rounds: int = 2) -> dict:
-    """The CPU oracle (numpy restatement of the reference path, oracle/) on this host: target
-    and draft prefill, first token and `max_rounds` rounds of config 2; tokens/s is then
-    extrapolated to the full 256-token request with the engine's round count (the same
-    greedy algorithm makes the same number of rounds)."""
+REF_SAMPLE_NEW = 4  # generated tokens per reference-arm step: the first token and three rounds
+
+
+def reference_request_rate(target, draft, prompt: list[int], emitted_per_round: float | None = None) -> dict:
+    """One bounded sample of config 2 through the reference's own stock code path (installed
+    unmodified under baseline/_ref): spec.loop.generate with spec.draft.ModelDraft and
+    cache.kv.KVCache on the host cores, REF_SAMPLE_NEW tokens (target and draft prefill of the
+    512-token prompt, first token, then rounds). The loop's own events split the time into the
+    prefill part and the rounds; tokens/s of the full 256-token request is the prefill part
+    plus the rounds a full request needs (at the sample's mean emitted tokens per round, or
+    `emitted_per_round` when given) at the sample's time per round."""
+    import math
+
+    from cache.kv import KVCache
+    from spec.draft import ModelDraft
+    from spec.loop import generate
+
+    blocks = (PROMPT_LEN + NEW_TOKENS + 2 * K + 8) // BLOCK + 2
+    tc = KVCache.for_model(target.config, num_blocks=blocks, block_size=BLOCK, dtype=torch.bfloat16, device="cpu")
+    dc = KVCache.for_model(draft.config, num_blocks=blocks, block_size=BLOCK, dtype=torch.bfloat16, device="cpu")
+    ev: dict[str, float] = {}
+    t0 = time.perf_counter()
+    _, st = generate(target, tc, ModelDraft(draft, dc), [prompt], REF_SAMPLE_NEW, k=K,
+                     on_event=lambda name: ev.setdefault(name, time.perf_counter() - t0))
+    t_end = time.perf_counter() - t0
+    per_round = (t_end - ev["draft_prefilled"]) / max(1, st.rounds)
+    emitted = emitted_per_round or max(1.0, (REF_SAMPLE_NEW - 1) / max(1, st.rounds))
+    rounds_full = math.ceil((NEW_TOKENS - 1) / emitted)
+    total = ev["draft_prefilled"] + rounds_full * per_round
+    return {"value": NEW_TOKENS / total, "prefill_s": ev["draft_prefilled"], "round_s": per_round,
+            "rounds_full": rounds_full, "sample_rounds": st.rounds}
+
+
+def port_request_rate(target, draft, prompt: list[int], engine_rounds: int | None, max_rounds: int = 2) -> dict:
+    """The CPU oracle (the numpy restatement of the reference path under oracle/) on this host:
+    target and draft prefill, first token and `max_rounds` rounds of config 2, extrapolated to
+    the full 256-token request with the given round count (the same greedy algorithm makes the
+    same number of rounds), or with the sample's own acceptance."""
     from oracle import forward as ofw
     from oracle import loop as oloop
 
@@ -469,15 +521,64 @@ def cpu_baseline(target, draft, prompt: list[int], engine_rounds: int | None, ma
     _, st = oloop.generate(tw, prec, drafter, [prompt], NEW_TOKENS, K, num_blocks=64, block_size=BLOCK,
                            max_rounds=max_rounds)
     per_round = st["seconds_rounds"] / max(1, st["rounds"])
-    if engine_rounds is None:  # no engine run to take the round count from: the sample's own acceptance
+    if engine_rounds is None:
         emitted = max(1.0, sum(st["emitted_per_round"]) / max(1, len(st["emitted_per_round"])))
         engine_rounds = int(np.ceil((NEW_TOKENS - 1) / emitted))
     total = st["seconds_prefill"] + per_round * engine_rounds
-    return {"value": NEW_TOKENS / total, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
+    return {"value": NEW_TOKENS / total, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
             "sample": (f"CPU oracle (numpy, bf16 rounding) on config 2 at B=1: prefill of the {PROMPT_LEN}-token "
                        f"prompt on target and draft + first token ({st['seconds_prefill']:.2f} s) and "
                        f"{st['rounds']} rounds ({per_round:.3f} s each), extrapolated to {engine_rounds} rounds "
                        f"for {NEW_TOKENS} tokens")}
+
+
+def reference_arm(args, metric: str, config: dict) -> dict:
+    """`--impl reference`: config 2 through the reference's own CPU code (baseline/_ref) on all
+    host cores, K bounded samples after W warm-up samples; the numpy port is timed once beside
+    it. Falls back to the port alone when the reference is not installed."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    target = make_model(TARGET, 0, "cpu")
+    draft = make_model(DRAFT, 1, "cpu")
+    prompt = prompts_for(0, 1)[0]
+    if REF_INSTALL.is_dir():
+        for _ in range(min(args.warmup, 1)):
+            reference_request_rate(target, draft, prompt)
+        samples = [reference_request_rate(target, draft, prompt) for _ in range(max(1, args.steps))]
+        v = statistics.median(s["value"] for s in samples)
+        mid = sorted(samples, key=lambda s: s["value"])[len(samples) // 2]
+        cb = {"value": v, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "reference",
+              "sample": (f"the reference's spec.loop.generate + ModelDraft (installed unmodified under baseline/_ref) "
+                         f"on config 2 at B=1 on the host cores, {len(samples)} samples of {REF_SAMPLE_NEW} tokens: "
+                         f"target and draft prefill + first token {mid['prefill_s']:.2f} s, {mid['round_s']:.3f} s "
+                         f"per round, extrapolated to {mid['rounds_full']} rounds for {NEW_TOKENS} tokens (median)")}
+        port = None
+        if not args.no_cpu_baseline:
+            try:
+                port = port_request_rate(target, draft, prompt, engine_rounds=mid["rounds_full"])
+                port["vs_reference"] = port["value"] / v
+            except Exception as e:  # noqa: BLE001
+                port = {"value": None, "sample": f"failed: {e}"}
+        cb["port"] = port
+    else:
+        cb = port_request_rate(target, draft, prompt, engine_rounds=None)
+        v = cb["value"]
+    return {"impl": "reference", "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": 0, "steps": args.steps,
+            "warmup": min(args.warmup, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic", "config": config, "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def cpu_baseline_subprocess(steps: int = 3) -> dict | None:
+    """The reference arm's measurement, run as a separate process (its packages cannot share
+    this process with the engine's): its cpu_baseline object."""
+    cmd = [sys.executable, str(Path(__file__).resolve()), "--impl", "reference", "--steps", str(steps), "--warmup", "1",
+           "--no-cpu-baseline"]
+    try:
+        res = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
+        lines = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
+        return json.loads(lines[-1])["cpu_baseline"] if lines else {"value": None, "sample": res.stderr[-500:]}
+    except Exception as e:  # noqa: BLE001
+        return {"value": None, "sample": f"failed: {e}"}
 
 
 def main() -> None:
@@ -510,22 +611,7 @@ def main() -> None:
     if args.impl == "reference":
         if rank != 0:
             return
-        torch.set_num_threads(os.cpu_count() or 1)
-        target = make_model(TARGET, 0, "cpu")
-        draft = make_model(DRAFT, 1, "cpu")
-        prompt = prompts_for(0, 1)[0]
-        # each step is a bounded sample (prefill + 2 rounds), extrapolated to the 256-token request
-        vals = []
-        for _ in range(max(1, args.steps)):
-            cb = cpu_baseline(target, draft, prompt, engine_rounds=None, max_rounds=2)
-            vals.append(cb["value"])
-        v = statistics.median(vals)
-        cb["value"] = v
-        print(json.dumps({"impl": "reference", "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": 0,
-                          "steps": args.steps, "warmup": 0, "higher_is_better": True, "scaling": "weak",
-                          "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config,
-                          "cpu_baseline": cb, "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0,
-                                                      "d2h_bytes_per_step": 0}}))
+        print(json.dumps(reference_arm(args, metric, config)))
         return
 
     device = torch.device("cuda", local)
@@ -632,10 +718,7 @@ def main() -> None:
     launches = args.steps * (te.launches(1, PROMPT_LEN) + de.launches(1, PROMPT_LEN) + 1) + rounds * launches_per_round
     cb = None
     if not args.no_cpu_baseline and world == 1:
-        try:
-            cb = cpu_baseline(target.cpu(), draft.cpu(), prompts[0], engine_rounds=rounds // max(1, args.steps))
-        except Exception as e:  # noqa: BLE001
-            cb = {"value": None, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port", "sample": f"failed: {e}"}
+        cb = cpu_baseline_subprocess()
     value = tokens_all / dev_s
     line = {
         "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,

@@ -132,6 +132,20 @@ int specb200_scatter_tokens(const int64_t* tokens, int B, int k, int j, int64_t*
                             void* stream);
 
 /* ======================================================================================
+ * Seeded logit noise for the noisy-copy drafter (BASELINE config 2's second variant: the
+ * target itself as the draft with N(0, sigma^2) added to its final logits). No counterpart
+ * in the reference, which has no such drafter.
+ * ====================================================================================== */
+
+/* logits[b, v] += sigma * z(seed, row_id[b], past[b] + n_new[b], v) for every row with
+ * n_new[b] > 0 (n_new NULL: every row, as if 1; past NULL: 0; row_id NULL: b). z is a
+ * standard normal by Box-Muller from Philox4x32-10 at counter (v, position, row id, 0) and key
+ * (seed low, seed high 32 bits); the position is that of the token the logits predict.
+ * logits: [B, ld] fp32 device rows, ld >= V. */
+int specb200_logit_noise(float* logits, int B, int V, int64_t ld, const int32_t* past, const int32_t* n_new,
+                         const int32_t* row_id, uint64_t seed, float sigma, void* stream);
+
+/* ======================================================================================
  * Llama verify / decode / prefill forward
  *   replaces lm/forward.py:21-68 (forward) and lm/forward.py:71-84 (logits), with
  *   cache/kv.py:79-112 (append's slot maps, write, gather) done inside the kernels:

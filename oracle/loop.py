@@ -14,6 +14,7 @@ import torch
 
 from oracle import accept as acc
 from oracle import forward as fw
+from oracle import noise
 from oracle.ngram import lookup_batch
 
 
@@ -68,11 +69,14 @@ class ModelDraft:
             self.cache.add(s)
         run(self.w, self.cache, seq_ids, prompts, self.prec)
 
+    def _logits(self, seq_ids, pending) -> np.ndarray:
+        return run(self.w, self.cache, seq_ids, pending, self.prec).astype(np.float32)
+
     def propose(self, seq_ids, contexts, k, temperature, generator):
         pending = [ctx[self.cache.length(s):] for s, ctx in zip(seq_ids, contexts)]
         tokens, qs = [], []
         for _ in range(k):
-            q = acc.probabilities(run(self.w, self.cache, seq_ids, pending, self.prec).astype(np.float32), temperature)
+            q = acc.probabilities(self._logits(seq_ids, pending), temperature)
             tok = sample(q, generator)
             tokens.append(tok)
             qs.append(q)
@@ -84,6 +88,23 @@ class ModelDraft:
 
     def release(self, seq_id) -> None:
         self.cache.free(seq_id)
+
+
+class NoisyDraft(ModelDraft):
+    """The noisy-copy drafter of BASELINE config 2's second variant (no counterpart in the
+    reference): ModelDraft whose model is the target, with sigma * z added to each step's
+    logits before probabilities(), z from oracle.noise at (seed, sequence id, position of the
+    predicted token)."""
+
+    def __init__(self, w: dict, prec: fw.Precision, num_blocks: int, block_size: int, sigma: float,
+                 seed: int = 0) -> None:
+        super().__init__(w, prec, num_blocks, block_size)
+        self.sigma, self.seed = float(sigma), int(seed)
+
+    def _logits(self, seq_ids, pending) -> np.ndarray:
+        logits = super()._logits(seq_ids, pending)
+        positions = [self.cache.length(s) for s in seq_ids]  # after the forward: past + n_new
+        return noise.add_noise(logits, self.seed, self.sigma, seq_ids, positions)
 
 
 def new_stats(k: int) -> dict:

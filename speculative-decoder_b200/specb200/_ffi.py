@@ -64,6 +64,8 @@ PROTOTYPES: dict[str, tuple] = {
     "specb200_verify_ids": (c_int, [c_void_p, c_int64, c_void_p, c_void_p, c_void_p, c_int, c_int, c_void_p, c_void_p,
                                     c_void_p, c_void_p]),
     "specb200_scatter_tokens": (c_int, [c_void_p, c_int, c_int, c_int, c_void_p, c_void_p, c_void_p]),
+    "specb200_logit_noise": (c_int, [c_void_p, c_int, c_int, c_int64, c_void_p, c_void_p, c_void_p, ctypes.c_uint64,
+                                     c_float, c_void_p]),
     "specb200_model_create": (c_int, [ctypes.POINTER(ModelConfig), ctypes.POINTER(ModelWeights),
                                       ctypes.POINTER(c_void_p)]),
     "specb200_model_destroy": (c_int, [c_void_p]),
@@ -120,8 +122,11 @@ def raise_for(code: int, where: str) -> None:
 
 
 def check_status(status: torch.Tensor, where: str) -> None:
-    """Reads a device status word (synchronises with its stream) and raises on error."""
-    code = int(status.item())
+    """Reads device status words (synchronises with their stream) and raises on the first
+    error found."""
+    words = status.reshape(-1)
+    bad = words[words != 0]
+    code = int(bad[0].item()) if bad.numel() else 0
     if code == ERR_ZERO_Q:
         raise ZeroDraftMass("a drafted token has zero draft probability; q is not what it was sampled from")
     if code == ERR_RANGE:

@@ -27,6 +27,7 @@ import torch
 
 from specb200 import _ffi
 from specb200._ffi import lib, ptr, raise_for
+from specb200.draftloop import DraftSteps
 from specb200.engine import Engine, engine_for
 
 
@@ -100,7 +101,6 @@ class FusedRound:
         # ---- device state
         self.ctx = torch.zeros(B, cap, dtype=i32, device=dev)
         self.ctx_len = torch.zeros(B, dtype=i32, device=dev)
-        self.draft = torch.zeros(B, k, dtype=i64, device=dev)
         self.ids = torch.zeros(B, k + 1, dtype=i32, device=dev)
         self.past = torch.zeros(B, dtype=i32, device=dev)
         self.n_new = torch.zeros(B, dtype=i32, device=dev)
@@ -111,10 +111,6 @@ class FusedRound:
         # n-gram, target forward, accept (a call clears its own word only)
         self.n_status = 2 * k + 3
         self.status = torch.zeros(self.n_status, dtype=i32, device=dev)
-        if draft is not None:
-            self.q_logits = torch.empty(k, B, self.V, dtype=f32, device=dev)  # step-major
-            self.d_ids = torch.zeros(B, 1, dtype=i32, device=dev)
-            self.d_tok = torch.zeros(B, dtype=i64, device=dev)
         # ---- outputs (pinned) and scratch
         self.out_h = torch.zeros(B * (2 + k), dtype=i64, pin_memory=True)
         self.status_h = torch.zeros(self.n_status, dtype=i32, pin_memory=True)
@@ -123,8 +119,17 @@ class FusedRound:
         if draft is not None:
             ws = max(ws, draft.workspace_bytes(B, 2, cap), draft.workspace_bytes(B, 1, cap))
         self.fwd_ws = torch.zeros(ws, dtype=torch.uint8, device=dev)
-        acc_ws = lib().specb200_accept_workspace_bytes(B, k)
+        acc_ws = max(lib().specb200_accept_workspace_bytes(B, k), lib().specb200_accept_workspace_bytes(B, 0))
         self.acc_ws = torch.zeros(acc_ws, dtype=torch.uint8, device=dev)
+        # the draft model's k steps (the draft path), or the n-gram kernel's output buffer
+        self.steps = None
+        if draft is not None:
+            self.steps = DraftSteps(draft, drafter.cache, B, k, cap, temperature, ids0=self.d_ids0, past=self.d_past,
+                                    n_new=self.d_n, table=self.d_table, u=self.d_u, fwd_ws=self.fwd_ws,
+                                    acc_ws=self.acc_ws, noise=drafter.noise())
+            self.draft = self.steps.draft
+        else:
+            self.draft = torch.zeros(B, k, dtype=i64, device=dev)
         self.graph: torch.cuda.CUDAGraph | None = None
         # numpy views of the pinned inputs: the host fills them with plain array writes
         self.np_active = self.active_h.numpy()
@@ -147,20 +152,8 @@ class FusedRound:
         self.g_int.copy_(self.h_int, non_blocking=True)
         self.g_flt.copy_(self.h_flt, non_blocking=True)
         st = self.status
-        if self.d is not None:
-            dc = self.drafter.cache
-            for j in range(k):
-                # step j: draft forward (the lag tokens at j = 0), then sample(probabilities(.))
-                # of spec/draft.py:51-52 with the fused kernel at k = 0
-                ids = self.d_ids0 if j == 0 else self.d_ids
-                self.d.forward_device(dc, ids, self.d_n[j], self.d_past[j], self.d_table, self.cap, True,
-                                      self.q_logits[j], st[2 * j:2 * j + 1], self.fwd_ws)
-                rc = L.specb200_accept(ptr(self.q_logits[j]), None, None, None, ptr(self.d_u[j]), B, 0, self.V,
-                                       _ffi.ACCEPT_LOGITS, self.T, ptr(self.n_acc), ptr(self.d_tok),
-                                       ptr(st[2 * j + 1:2 * j + 2]), ptr(self.acc_ws), self.acc_ws.numel(), s)
-                raise_for(rc, "specb200_accept (draft sampler)")
-                raise_for(L.specb200_scatter_tokens(ptr(self.d_tok), B, k, j, ptr(self.draft), ptr(self.d_ids), s),
-                          "specb200_scatter_tokens")
+        if self.steps is not None:
+            self.steps.launch(st[0:2 * k])
         else:
             raise_for(L.specb200_ngram(ptr(self.ctx), self.cap, ptr(self.ctx_len), B, k, self.drafter.max_n,
                                        ptr(self.draft), ptr(st[0:1]), s), "specb200_ngram")
@@ -169,7 +162,7 @@ class FusedRound:
         self.t.forward_device(self.cache, self.ids, self.n_new, self.past, self.table, self.cap, False, self.p_logits,
                               st[2 * k:2 * k + 1], self.fwd_ws)
         flags = _ffi.ACCEPT_LOGITS | (_ffi.ACCEPT_Q_STEP_MAJOR if self.d is not None else _ffi.ACCEPT_Q_ONEHOT)
-        q = self.q_logits if self.d is not None else None
+        q = self.steps.q_logits if self.steps is not None else None
         rc = L.specb200_accept(ptr(self.p_logits), ptr(q), ptr(self.draft), ptr(self.u_acc), ptr(self.u_res), B, k,
                                self.V, flags, self.T, ptr(self.n_acc), ptr(self.nxt), ptr(st[2 * k + 1:2 * k + 2]),
                                ptr(self.acc_ws),
@@ -268,16 +261,13 @@ def generate_fused(target, cache, drafter, prompts, max_new_tokens, k, temperatu
         if draft_eng is not None:
             dc = drafter.cache
             rnd.np_d_n[:] = 0
+            past, grow, pending = rnd.steps.plan(active, [contexts[s] for s in active])
             for j in range(k):
                 rnd.np_d_u[j, active] = d_u[j]
-                grow = [len(contexts[s]) - dc.length(s) if j == 0 else 1 for s in active]
-                before = dc.reserve(active, grow)
-                rnd.np_d_past[j, active] = before
-                rnd.np_d_n[j, active] = grow
-                if j == 0:
-                    for s, p in zip(active, before):
-                        pend = contexts[s][p:]
-                        rnd.np_d_ids0[s, : len(pend)] = pend
+                rnd.np_d_past[j, active] = past[j]
+                rnd.np_d_n[j, active] = grow[j]
+            for s, pend in zip(active, pending):
+                rnd.np_d_ids0[s, : len(pend)] = pend
             for s in active:
                 blocks = dc.tables[s].blocks
                 rnd.np_d_table[s, : len(blocks)] = blocks

@@ -134,3 +134,37 @@ def test_plain_decode_matches_reference(golden_generate):
     prec = ofw.Precision("f64")
     for p, want in zip(g["prompts"][:8] + g["repetitive"], g["plain"][:8] + g["plain"][-1:]):
         assert oloop.generate_plain(w, prec, p, g["max_new"], block_size=4) == want
+
+
+def test_philox_matches_known_answers():
+    """The noise oracle's Philox4x32-10 against the known-answer vectors published with the
+    generator (Salmon et al., SC 2011, Random123 kat_vectors: zero, all-ones and pi-digit
+    counters and keys)."""
+    from oracle.noise import philox4x32_10
+
+    cases = [((0, 0, 0, 0), (0, 0), (0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8)),
+             ((0xFFFFFFFF,) * 4, (0xFFFFFFFF, 0xFFFFFFFF), (0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD)),
+             ((0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344), (0xA4093822, 0x299F31D0),
+              (0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1))]
+    for ctr, key, want in cases:
+        got = philox4x32_10(*ctr, *key)
+        assert tuple(int(x) for x in got) == want
+
+
+def test_logit_noise_is_standard_normal_and_keyed():
+    """The noise is N(0, 1) per element (moments and a normality test over 2 x 49152 draws),
+    depends on every key field, and adds sigma * z to the logits row by row."""
+    from scipy.stats import normaltest
+
+    from oracle.noise import add_noise, normals
+
+    z = np.concatenate([normals(7, 0, 512, 49152), normals(7, 1, 513, 49152)])
+    assert abs(z.mean()) < 0.02 and abs(z.std() - 1.0) < 0.02
+    assert normaltest(z).pvalue > 1e-3
+    base = normals(7, 0, 512, 64)
+    for other in (normals(8, 0, 512, 64), normals(7, 1, 512, 64), normals(7, 0, 513, 64)):
+        assert not np.allclose(base, other)
+    logits = np.ones((2, 64), dtype=np.float32)
+    out = add_noise(logits, 7, 0.5, [0, 1], [512, 513])
+    np.testing.assert_allclose(out[0], 1 + 0.5 * base, rtol=1e-6)
+    np.testing.assert_allclose(out[1], 1 + 0.5 * normals(7, 1, 513, 64), rtol=1e-6)
