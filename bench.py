@@ -75,6 +75,47 @@ ACCEPT_BYTES = 113_246_208            # config 3: 64 x (5 + 4) x 49152 x 4 B
 VERIFY_TRAFFIC_RATIO = {"layers": (1_046_855_168 + 181_760) / 1_038_340_096}
 
 
+# BASELINE configs as bench workloads (requests per GPU; requests are independent, so N GPUs
+# run N times the requests with no collective in the timed region: weak scaling).
+WORKLOADS = {
+    2: dict(name="config2", B=1, prompt=PROMPT_LEN, new=NEW_TOKENS, k=K, T=0.0, block=BLOCK, drafter="model",
+            prompts="uniform",
+            metric="generated tokens/s, 1.7B target k=4 @B1 (config 2, 135M draft, greedy)",
+            workload="config2: 1.7B-arch target + 135M-arch draft, bf16 random init, B=1 per GPU, prompt 512, k=4, "
+                     "greedy, 256 new tokens, block 16"),
+    4: dict(name="config4", B=32, prompt=1024, new=128, k=8, T=0.8, block=16, drafter="model", prompts="uniform",
+            metric="generated tokens/s, 1.7B target k=8 T=0.8 @B32 per GPU (config 4, 135M draft)",
+            workload="config4: 1.7B-arch target + 135M-arch draft, bf16 random init, 32 requests per GPU (256 over "
+                     "8 GPUs), 1024-token uniform prompts, k=8, T=0.8 sampling, 128 new tokens, block 16"),
+    5: dict(name="config5", B=4, prompt=8192, new=256, k=6, T=0.0, block=32, drafter="ngram", prompts="segments",
+            metric="generated tokens/s, 1.7B target n-gram k=6 @8k context, 4 requests per GPU (config 5)",
+            workload="config5: 1.7B-arch target bf16 random init, n-gram drafter (max_n 3), 4 requests per GPU "
+                     "(32 over 8 GPUs), 8192-token prompts of 64-id segments each repeated with p=0.5, k=6, greedy, "
+                     "256 new tokens, block 32"),
+}
+NOISY_SIGMA = 0.09  # config 2b: N(0, sigma^2) on the target's logits, sigma measured for acceptance ~0.6
+
+
+def workload_prompts(w: dict, first: int, n: int) -> list[list[int]]:
+    """Requests first .. first + n - 1 of a workload, each from its own seed (1000 + index):
+    uniform-random ids, or (config 5) 64-id uniform segments each followed by a copy of itself
+    with probability 0.5, cut to the prompt length."""
+    out = []
+    for i in range(first, first + n):
+        g = torch.Generator().manual_seed(1000 + i)
+        if w["prompts"] == "uniform":
+            out.append(torch.randint(0, TARGET["vocab_size"], (w["prompt"],), generator=g).tolist())
+            continue
+        ids: list[int] = []
+        while len(ids) < w["prompt"]:
+            seg = torch.randint(0, TARGET["vocab_size"], (64,), generator=g).tolist()
+            ids += seg
+            if float(torch.rand(1, generator=g)) < 0.5:
+                ids += seg
+        out.append(ids[: w["prompt"]])
+    return out
+
+
 def weight_bytes(spec: dict) -> int:
     """bf16 bytes of every weight read once per forward: linears, RMSNorm weights and the tied
     embedding/head (3,422,752,768 B for the 1.7B architecture)."""
@@ -115,11 +156,6 @@ def make_model(spec: dict, seed: int, device):
     with torch.device(device):
         model = LlamaForCausalLM(cfg)
     return model.to(torch.bfloat16).eval()
-
-
-def prompts_for(rank: int, n: int) -> list[list[int]]:
-    g = torch.Generator().manual_seed(1000 + rank)
-    return [torch.randint(0, TARGET["vocab_size"], (PROMPT_LEN,), generator=g).tolist() for _ in range(n)]
 
 
 class Clocks:
@@ -170,28 +206,33 @@ class Clocks:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30, trace: bool = False) -> dict:
-    """The (k+1)-token target forward of one round at B=1 with `context_len` cached tokens,
-    captured in a CUDA graph and replayed; CUDA events on the replay stream."""
+def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30, trace: bool = False,
+                     B: int = 1, k: int = K, block: int = BLOCK) -> dict:
+    """The (k+1)-token target forward of one round for B rows with `context_len` cached tokens
+    each, captured in a CUDA graph and replayed; CUDA events on the replay stream."""
     from specb200.engine import engine_for
 
     eng = engine_for(target)
-    cache = cache_cls.for_model(target.config, num_blocks=(context_len + 64) // BLOCK + 4, block_size=BLOCK,
-                                dtype=torch.bfloat16, device=device)
-    cache.add(0)
-    cache.reserve([0], [context_len - 1])
+    per_row = -(-(context_len + 64) // block)
+    cache = cache_cls.for_model(target.config, num_blocks=B * per_row + 4, block_size=block, dtype=torch.bfloat16,
+                                device=device)
+    rows = list(range(B))
+    for r in rows:
+        cache.add(r)
+    cache.reserve(rows, [context_len - 1] * B)
     past = cache.length(0)
-    cache.reserve([0], [K + 1])
+    cache.reserve(rows, [k + 1] * B)
     cap = context_len + 64
-    table = torch.zeros(1, -(-cap // BLOCK), dtype=torch.int32, device=device)
-    blocks = cache.tables[0].blocks
-    table[0, : len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
-    ids = torch.randint(0, TARGET["vocab_size"], (1, K + 1), dtype=torch.int32, device=device)
-    n_new = torch.tensor([K + 1], dtype=torch.int32, device=device)
-    pastt = torch.tensor([past], dtype=torch.int32, device=device)
-    logits = torch.empty(1, K + 1, TARGET["vocab_size"], dtype=torch.float32, device=device)
+    table = torch.zeros(B, -(-cap // block), dtype=torch.int32, device=device)
+    for r in rows:
+        blocks = cache.tables[r].blocks
+        table[r, : len(blocks)] = torch.tensor(blocks, dtype=torch.int32)
+    ids = torch.randint(0, TARGET["vocab_size"], (B, k + 1), dtype=torch.int32, device=device)
+    n_new = torch.full((B,), k + 1, dtype=torch.int32, device=device)
+    pastt = torch.full((B,), past, dtype=torch.int32, device=device)
+    logits = torch.empty(B, k + 1, TARGET["vocab_size"], dtype=torch.float32, device=device)
     status = torch.zeros(1, dtype=torch.int32, device=device)
-    ws = torch.zeros(eng.workspace_bytes(1, K + 1, cap), dtype=torch.uint8, device=device)
+    ws = torch.zeros(eng.workspace_bytes(B, k + 1, cap), dtype=torch.uint8, device=device)
     run = lambda: eng.forward_device(cache, ids, n_new, pastt, table, cap, False, logits, status, ws)  # noqa: E731
     run()
     torch.cuda.synchronize()
@@ -212,10 +253,10 @@ def time_verify_step(target, cache_cls, device, context_len: int, reps: int = 30
     en.synchronize()
     ms = st.elapsed_time(en) / reps
     assert int(status.item()) == 0
-    kv_tokens = past + K + 1
+    kv_tokens = past + k + 1
     spec = dict(TARGET, num_hidden_layers=target.config.num_hidden_layers)
-    r = {"us": ms * 1e3, "bytes": weight_bytes(spec) + kv_bytes_per_token(spec) * kv_tokens, "context": kv_tokens,
-         "layers": spec["num_hidden_layers"]}
+    r = {"us": ms * 1e3, "bytes": weight_bytes(spec) + B * kv_bytes_per_token(spec) * kv_tokens, "context": kv_tokens,
+         "rows": B, "tokens_per_row": k + 1, "layers": spec["num_hidden_layers"]}
     if trace:
         tr = torch.zeros(5 * spec["num_hidden_layers"] + 1, 512, 8, dtype=torch.int64, device=device)
         eng.forward_device(cache, ids, n_new, pastt, table, cap, False, logits, status, ws, trace=tr)
@@ -473,36 +514,43 @@ def request_latency(target, draft, prompts, device, blocks: int, repeats: int = 
             "source": "bench.harness.measure + bench.latency.summarize (p50; device synced at each event)"}
 
 
-REF_SAMPLE_NEW = 4  # generated tokens per reference-arm step: the first token and three rounds
+REF_SAMPLE_NEW = 4  # generated tokens per reference-arm sample: the first token and three rounds
 
 
-def reference_request_rate(target, draft, prompt: list[int], emitted_per_round: float | None = None) -> dict:
-    """One bounded sample of config 2 through the reference's own stock code path (installed
-    unmodified under baseline/_ref): spec.loop.generate with spec.draft.ModelDraft and
-    cache.kv.KVCache on the host cores, REF_SAMPLE_NEW tokens (target and draft prefill of the
-    512-token prompt, first token, then rounds). The loop's own events split the time into the
-    prefill part and the rounds; tokens/s of the full 256-token request is the prefill part
-    plus the rounds a full request needs (at the sample's mean emitted tokens per round, or
+def reference_request_rate(target, draft, prompt: list[int], w: dict, emitted_per_round: float | None = None) -> dict:
+    """One bounded sample of a workload's request through the reference's own stock code path
+    (installed unmodified under baseline/_ref): spec.loop.generate with its ModelDraft or
+    NGramDraft and cache.kv.KVCache on the host cores, REF_SAMPLE_NEW tokens (prefills, first
+    token, then rounds). The loop's own events split the time into the prefill part and the
+    rounds; tokens/s of the full request is its token count over the prefill part plus the
+    rounds a full request needs (at the sample's mean emitted tokens per round, or
     `emitted_per_round` when given) at the sample's time per round."""
     import math
 
     from cache.kv import KVCache
     from spec.draft import ModelDraft
     from spec.loop import generate
+    from spec.ngram import NGramDraft
 
-    blocks = (PROMPT_LEN + NEW_TOKENS + 2 * K + 8) // BLOCK + 2
-    tc = KVCache.for_model(target.config, num_blocks=blocks, block_size=BLOCK, dtype=torch.bfloat16, device="cpu")
-    dc = KVCache.for_model(draft.config, num_blocks=blocks, block_size=BLOCK, dtype=torch.bfloat16, device="cpu")
+    blocks = (w["prompt"] + w["new"] + 2 * w["k"] + 8) // w["block"] + 2
+    tc = KVCache.for_model(target.config, num_blocks=blocks, block_size=w["block"], dtype=torch.bfloat16, device="cpu")
+    if w["drafter"] == "model":
+        dc = KVCache.for_model(draft.config, num_blocks=blocks, block_size=w["block"], dtype=torch.bfloat16,
+                               device="cpu")
+        drafter = ModelDraft(draft, dc)
+    else:
+        drafter = NGramDraft(TARGET["vocab_size"], max_n=3)
     ev: dict[str, float] = {}
     t0 = time.perf_counter()
-    _, st = generate(target, tc, ModelDraft(draft, dc), [prompt], REF_SAMPLE_NEW, k=K,
+    _, st = generate(target, tc, drafter, [prompt], REF_SAMPLE_NEW, k=w["k"], temperature=w["T"],
+                     generator=torch.Generator().manual_seed(0),
                      on_event=lambda name: ev.setdefault(name, time.perf_counter() - t0))
     t_end = time.perf_counter() - t0
     per_round = (t_end - ev["draft_prefilled"]) / max(1, st.rounds)
     emitted = emitted_per_round or max(1.0, (REF_SAMPLE_NEW - 1) / max(1, st.rounds))
-    rounds_full = math.ceil((NEW_TOKENS - 1) / emitted)
+    rounds_full = math.ceil((w["new"] - 1) / emitted)
     total = ev["draft_prefilled"] + rounds_full * per_round
-    return {"value": NEW_TOKENS / total, "prefill_s": ev["draft_prefilled"], "round_s": per_round,
+    return {"value": w["new"] / total, "prefill_s": ev["draft_prefilled"], "round_s": per_round,
             "rounds_full": rounds_full, "sample_rounds": st.rounds}
 
 
@@ -532,27 +580,28 @@ def port_request_rate(target, draft, prompt: list[int], engine_rounds: int | Non
                        f"for {NEW_TOKENS} tokens")}
 
 
-def reference_arm(args, metric: str, config: dict) -> dict:
-    """`--impl reference`: config 2 through the reference's own CPU code (baseline/_ref) on all
-    host cores, K bounded samples after W warm-up samples; the numpy port is timed once beside
-    it. Falls back to the port alone when the reference is not installed."""
+def reference_arm(args, w: dict, config: dict) -> dict:
+    """`--impl reference`: the workload's request through the reference's own CPU code
+    (baseline/_ref) on all host cores, K bounded samples after at most one warm-up sample; for
+    config 2 the numpy port is timed once beside it. Falls back to the port alone when the
+    reference is not installed (config 2 only)."""
     torch.set_num_threads(os.cpu_count() or 1)
     target = make_model(TARGET, 0, "cpu")
-    draft = make_model(DRAFT, 1, "cpu")
-    prompt = prompts_for(0, 1)[0]
+    draft = make_model(DRAFT, 1, "cpu") if w["drafter"] == "model" else None
+    prompt = workload_prompts(w, 0, 1)[0]
     if REF_INSTALL.is_dir():
         for _ in range(min(args.warmup, 1)):
-            reference_request_rate(target, draft, prompt)
-        samples = [reference_request_rate(target, draft, prompt) for _ in range(max(1, args.steps))]
+            reference_request_rate(target, draft, prompt, w)
+        samples = [reference_request_rate(target, draft, prompt, w) for _ in range(max(1, args.steps))]
         v = statistics.median(s["value"] for s in samples)
         mid = sorted(samples, key=lambda s: s["value"])[len(samples) // 2]
         cb = {"value": v, "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "reference",
-              "sample": (f"the reference's spec.loop.generate + ModelDraft (installed unmodified under baseline/_ref) "
-                         f"on config 2 at B=1 on the host cores, {len(samples)} samples of {REF_SAMPLE_NEW} tokens: "
-                         f"target and draft prefill + first token {mid['prefill_s']:.2f} s, {mid['round_s']:.3f} s "
-                         f"per round, extrapolated to {mid['rounds_full']} rounds for {NEW_TOKENS} tokens (median)")}
+              "sample": (f"the reference's spec.loop.generate (installed unmodified under baseline/_ref) on one "
+                         f"{w['name']} request on the host cores, {len(samples)} samples of {REF_SAMPLE_NEW} tokens: "
+                         f"prefill + first token {mid['prefill_s']:.2f} s, {mid['round_s']:.3f} s per round, "
+                         f"extrapolated to {mid['rounds_full']} rounds for {w['new']} tokens (median)")}
         port = None
-        if not args.no_cpu_baseline:
+        if w["name"] == "config2" and not args.no_cpu_baseline:
             try:
                 port = port_request_rate(target, draft, prompt, engine_rounds=mid["rounds_full"])
                 port["vs_reference"] = port["value"] / v
@@ -560,19 +609,21 @@ def reference_arm(args, metric: str, config: dict) -> dict:
                 port = {"value": None, "sample": f"failed: {e}"}
         cb["port"] = port
     else:
+        if w["name"] != "config2":
+            return {"impl": "reference", "unavailable": "the reference is not installed under baseline/_ref"}
         cb = port_request_rate(target, draft, prompt, engine_rounds=None)
         v = cb["value"]
-    return {"impl": "reference", "metric": metric, "value": v, "unit": "tokens/s", "n_gpus": 0, "steps": args.steps,
-            "warmup": min(args.warmup, 1), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-            "dtype": "bf16", "data": "synthetic", "config": config, "cpu_baseline": cb,
+    return {"impl": "reference", "metric": w["metric"], "value": v, "unit": "tokens/s", "n_gpus": 0,
+            "steps": args.steps, "warmup": min(args.warmup, 1), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": config, "cpu_baseline": cb,
             "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
-def cpu_baseline_subprocess(steps: int = 3) -> dict | None:
+def cpu_baseline_subprocess(config_id: int, steps: int = 3) -> dict | None:
     """The reference arm's measurement, run as a separate process (its packages cannot share
     this process with the engine's): its cpu_baseline object."""
-    cmd = [sys.executable, str(Path(__file__).resolve()), "--impl", "reference", "--steps", str(steps), "--warmup", "1",
-           "--no-cpu-baseline"]
+    cmd = [sys.executable, str(Path(__file__).resolve()), "--impl", "reference", "--config", str(config_id), "--steps",
+           str(steps), "--warmup", "1", "--no-cpu-baseline"]
     try:
         res = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
         lines = [ln for ln in res.stdout.splitlines() if ln.startswith("{")]
@@ -581,13 +632,40 @@ def cpu_baseline_subprocess(steps: int = 3) -> dict | None:
         return {"value": None, "sample": f"failed: {e}"}
 
 
+def time_requests(run, reps: int) -> dict:
+    """`run()` generates one batch and returns (tokens, SpecStats or None); device time with
+    CUDA events around `reps` calls after one warm-up call."""
+    run()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    tokens = rounds = accepted = drafted = 0
+    for _ in range(reps):
+        n, st = run()
+        tokens += n
+        if st is not None:
+            rounds, accepted, drafted = rounds + st.rounds, accepted + st.accepted, drafted + st.drafted
+    ev1.record()
+    ev1.synchronize()
+    s = ev0.elapsed_time(ev1) / 1e3
+    out = {"value": tokens / s, "unit": "tokens/s", "ms_per_request": s * 1e3 / reps, "requests": reps}
+    if drafted:
+        out.update({"acceptance": accepted / drafted, "rounds_per_request": rounds / reps})
+    return out
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    ap.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=2,
+                    help="BASELINE workload: 2 (default; 1.7B + 135M draft, B=1), 4 (32 requests per GPU, k=8, "
+                         "T=0.8) or 5 (8k-token prompts, n-gram drafter)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="config 2: skip the accept microbench, latency, plain-decode and noisy-draft lines")
     ap.add_argument("--layers", type=int, default=0,
                     help="with --only: build the models with this many layers (smaller profiling runs)")
     ap.add_argument("--draft-tokens", type=int, default=1,
@@ -602,16 +680,16 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    metric = "generated tokens/s, 1.7B target k=4 @B1 (config 2, 135M draft, greedy)"
-    config = {"workload": "config2: 1.7B-arch target + 135M-arch draft, bf16 random init, B=1 per GPU, prompt 512, "
-                          "k=4, greedy, 256 new tokens, block 16",
-              "global_batch": world, "seq_len": PROMPT_LEN + NEW_TOKENS, "parallelism": f"requests sharded x{world}",
+    w = WORKLOADS[args.config]
+    B = w["B"]
+    config = {"workload": w["workload"], "global_batch": B * world, "seq_len": w["prompt"] + w["new"],
+              "parallelism": f"requests sharded x{world}",
               "l2": "weights 3.4 GB >> 126 MB L2 (no flush needed); accept microbench flushes L2 between launches"}
 
     if args.impl == "reference":
         if rank != 0:
             return
-        print(json.dumps(reference_arm(args, metric, config)))
+        print(json.dumps(reference_arm(args, w, config)))
         return
 
     device = torch.device("cuda", local)
@@ -624,8 +702,8 @@ def main() -> None:
             r = time_accept(device, reps=max(1, args.steps))
         elif args.only == "verify":
             spec = dict(TARGET, num_hidden_layers=args.layers or TARGET["num_hidden_layers"])
-            r = time_verify_step(make_model(spec, 0, device), KVCache, device, PROMPT_LEN + NEW_TOKENS // 2,
-                                 reps=max(1, args.steps), trace=args.trace)
+            r = time_verify_step(make_model(spec, 0, device), KVCache, device, w["prompt"] + w["new"] // 2,
+                                 reps=max(1, args.steps), trace=args.trace, B=B, k=w["k"], block=w["block"])
         else:
             spec = dict(DRAFT, num_hidden_layers=args.layers or DRAFT["num_hidden_layers"])
             r = time_draft_step(make_model(spec, 1, device), KVCache, device, PROMPT_LEN + NEW_TOKENS // 2,
@@ -643,22 +721,29 @@ def main() -> None:
     from cache.kv import KVCache
     from spec.draft import ModelDraft
     from spec.loop import generate
+    from spec.ngram import NGramDraft
 
     from specb200.shard import gather_results, shard_range
 
     target = make_model(TARGET, 0, device)
-    draft = make_model(DRAFT, 1, device)
-    # one request per GPU: the box's requests are sharded as contiguous ranges, one per rank
-    all_prompts = [prompts_for(r, 1)[0] for r in range(world)]
-    lo, hi = shard_range(len(all_prompts), rank, world)
-    prompts = all_prompts[lo:hi]
-    blocks = (PROMPT_LEN + NEW_TOKENS + 2 * K + 8) // BLOCK + 2
+    draft = make_model(DRAFT, 1, device) if w["drafter"] == "model" else None
+    # the box's requests are sharded as contiguous ranges, B per rank
+    lo, hi = shard_range(B * world, rank, world)
+    prompts = workload_prompts(w, lo, hi - lo)
+    per_req = -(-(w["prompt"] + w["new"] + 2 * w["k"] + 8) // w["block"]) + 1
+    blocks = len(prompts) * per_req + 2
 
     def step():
-        cache = KVCache.for_model(target.config, num_blocks=blocks, block_size=BLOCK, dtype=torch.bfloat16, device=device)
-        dcache = KVCache.for_model(draft.config, num_blocks=blocks, block_size=BLOCK, dtype=torch.bfloat16,
-                                   device=device)
-        return generate(target, cache, ModelDraft(draft, dcache), prompts, NEW_TOKENS, k=K)
+        cache = KVCache.for_model(target.config, num_blocks=blocks, block_size=w["block"], dtype=torch.bfloat16,
+                                  device=device)
+        if w["drafter"] == "model":
+            dcache = KVCache.for_model(draft.config, num_blocks=blocks, block_size=w["block"], dtype=torch.bfloat16,
+                                       device=device)
+            drafter = ModelDraft(draft, dcache)
+        else:
+            drafter = NGramDraft(TARGET["vocab_size"], max_n=3)
+        gen = torch.Generator().manual_seed(1234)
+        return generate(target, cache, drafter, prompts, w["new"], k=w["k"], temperature=w["T"], generator=gen)
 
     for _ in range(args.warmup):
         out, stats = step()
@@ -670,25 +755,28 @@ def main() -> None:
         torch.cuda.synchronize()
         ev0.record()
         w0 = time.perf_counter()
-        tokens = 0
-        rounds = 0
+        tokens = rounds = accepted = drafted = 0
         for _ in range(args.steps):
             out, stats = step()
             tokens += sum(len(o) for o in out)
             rounds += stats.rounds
+            accepted += stats.accepted
+            drafted += stats.drafted
         ev1.record()
         torch.cuda.synchronize()
         wall = time.perf_counter() - w0
     dev_s = ev0.elapsed_time(ev1) / 1e3
+    per_rank = {"device_s": dev_s, "tokens": tokens}
     if world > 1:
         import torch.distributed as dist
 
         t = torch.tensor([dev_s, wall, float(tokens)], device=device, dtype=torch.float64)
-        mx = t.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        sm = t.clone()
-        dist.all_reduce(sm, op=dist.ReduceOp.SUM)
-        dev_s, wall, tokens_all = mx[0].item(), mx[1].item(), sm[2].item()
+        every = [torch.zeros_like(t) for _ in range(world)]
+        dist.all_gather(every, t)
+        dev_s = max(float(x[0]) for x in every)
+        wall = max(float(x[1]) for x in every)
+        tokens_all = sum(float(x[2]) for x in every)
+        per_rank = {"device_s": [round(float(x[0]), 4) for x in every], "tokens": [int(x[2]) for x in every]}
         # the last step's outputs and statistics of every request (kilobytes), over NCCL
         # after the timed region
         out, stats = gather_results(out, stats, device=device)
@@ -699,50 +787,81 @@ def main() -> None:
             torch.distributed.destroy_process_group()
         return
 
-    vstep = time_verify_step(target, KVCache, device, PROMPT_LEN + NEW_TOKENS // 2)
-    acc = time_accept(device)
-    try:
-        latency = request_latency(target, draft, prompts, device, blocks)
-    except Exception as e:  # noqa: BLE001  (the throughput line must still be printed)
-        latency = {"error": f"{type(e).__name__}: {e}"}
     pk = peaks()
+    vstep = time_verify_step(target, KVCache, device, w["prompt"] + w["new"] // 2, B=len(prompts), k=w["k"],
+                             block=w["block"])
     achieved = vstep["bytes"] / (vstep["us"] * 1e-6) / 1e9
-    acc_gbs = acc["bytes"] / (acc["us"] * 1e-6) / 1e9
-    alpha = stats.accepted / max(1, stats.drafted)
+    alpha = accepted / max(1, drafted)
     from specb200.engine import engine_for
 
-    te, de = engine_for(target), engine_for(draft)
-    # per round: k x (draft forward + sampler + token scatter), verify ids, verify forward,
-    # accept, commit; per step: target and draft prefill forwards and the first-token sampler
-    launches_per_round = K * (de.launches(1, 2) + 2) + 1 + te.launches(1, K + 1) + 2
-    launches = args.steps * (te.launches(1, PROMPT_LEN) + de.launches(1, PROMPT_LEN) + 1) + rounds * launches_per_round
-    cb = None
-    if not args.no_cpu_baseline and world == 1:
-        cb = cpu_baseline_subprocess()
+    te = engine_for(target)
+    nb = len(prompts)
+    if w["drafter"] == "model":
+        de = engine_for(draft)
+        # per round: k x (draft forward + sampler + token scatter), verify ids, verify forward,
+        # accept, commit; per step: target and draft prefill forwards and the first-token sampler
+        per_round = w["k"] * (de.launches(nb, 2) + 2) + 1 + te.launches(nb, w["k"] + 1) + 2
+        per_step = te.launches(nb, w["prompt"]) + de.launches(nb, w["prompt"]) + 1
+    else:
+        per_round = 1 + 1 + te.launches(nb, w["k"] + 1) + 2  # n-gram, verify ids, forward, accept, commit
+        per_step = te.launches(nb, w["prompt"]) + 1
+    launches = args.steps * per_step + rounds * per_round
     value = tokens_all / dev_s
     line = {
-        "metric": metric, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "metric": w["metric"], "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_s * 1e3 / args.steps, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, uniform-random prompts)",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random-init weights, seeded synthetic prompts)",
         "config": config,
-        "e2e": {"value": tokens_all / wall, "unit": "tokens/s", "h2d_bytes_per_step": PROMPT_LEN * 8 * world,
-                "d2h_bytes_per_step": NEW_TOKENS * 8 * world},
-        "roofline": {"bound": "hbm", "kernel": "verify step (one (k+1)-token target forward, CUDA graph)",
+        "e2e": {"value": tokens_all / wall, "unit": "tokens/s",
+                "h2d_bytes_per_step": w["prompt"] * 8 * B * world, "d2h_bytes_per_step": w["new"] * 8 * B * world},
+        "roofline": {"bound": "hbm", "kernel": f"verify step ({len(prompts)} x {w['k'] + 1}-token target forward, "
+                                               "CUDA graph)",
                      "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
-                     "traffic": (vstep["bytes"] * VERIFY_TRAFFIC_RATIO[te.schedule(1, K + 1)]
-                                 if te.schedule(1, K + 1) in VERIFY_TRAFFIC_RATIO else None),
-                     "traffic_source": f"ncu capture of the 6-layer verify ({te.schedule(1, K + 1)} schedule), "
-                                       "scaled by algorithmic bytes",
+                     "traffic": vstep["bytes"] * VERIFY_TRAFFIC_RATIO["layers"],
+                     "traffic_source": "ncu capture of the 6-layer B=1 verify, scaled by algorithmic bytes",
                      "peak_source": pk["source"], "verify_step_us": vstep["us"],
                      "algorithmic_bytes": vstep["bytes"], "context_tokens": vstep["context"]},
-        "accept": {"us": acc["us"], "achieved": acc_gbs, "frac": acc_gbs / pk["hbm_gbs"], "unit": "GB/s",
-                   "algorithmic_bytes": acc["bytes"], "config": "B=64, k=4, V=49152 fp32 logits, T=1"},
-        "latency": latency,
         "acceptance": alpha, "rounds_per_step": rounds / args.steps,
+        "per_rank": per_rank,
         "gpu_launches": launches,
         "clocks": clocks.summary(),
-        "cpu_baseline": cb,
     }
+    if w["name"] == "config2" and not args.no_extras:
+        from baselines import cached_autoregressive
+        from spec.draft import NoisyDraft
+
+        acc = time_accept(device)
+        acc_gbs = acc["bytes"] / (acc["us"] * 1e-6) / 1e9
+        line["accept"] = {"us": acc["us"], "achieved": acc_gbs, "frac": acc_gbs / pk["hbm_gbs"], "unit": "GB/s",
+                          "algorithmic_bytes": acc["bytes"], "config": "B=64, k=4, V=49152 fp32 logits, T=1"}
+        try:
+            line["latency"] = request_latency(target, draft, prompts, device, blocks)
+        except Exception as e:  # noqa: BLE001  (the throughput line must still be printed)
+            line["latency"] = {"error": f"{type(e).__name__}: {e}"}
+
+        def plain():
+            cache = KVCache.for_model(target.config, num_blocks=blocks, block_size=w["block"], dtype=torch.bfloat16,
+                                      device=device)
+            return len(cached_autoregressive.generate(target, cache, prompts[0], w["new"])), None
+
+        def noisy():
+            cache = KVCache.for_model(target.config, num_blocks=blocks, block_size=w["block"], dtype=torch.bfloat16,
+                                      device=device)
+            dcache = KVCache.for_model(target.config, num_blocks=blocks, block_size=w["block"], dtype=torch.bfloat16,
+                                       device=device)
+            o, st = generate(target, cache, NoisyDraft(target, dcache, sigma=NOISY_SIGMA, seed=0), prompts[:1],
+                             w["new"], k=w["k"])
+            return len(o[0]), st
+
+        line["plain"] = time_requests(plain, 3)
+        line["plain"]["source"] = "baselines.cached_autoregressive.generate on the engine (one graph replay per token)"
+        line["spec_vs_plain"] = value / world / line["plain"]["value"]
+        nz = time_requests(noisy, 3)
+        nz.update({"sigma": NOISY_SIGMA, "drafter": "spec.draft.NoisyDraft: the target itself + N(0, sigma^2) on "
+                                                   "its final logits (config 2's second variant)"})
+        line["variants"] = {"config2b_noisy_draft": nz}
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = cpu_baseline_subprocess(args.config, steps=3 if args.config == 2 else 1)
     print(json.dumps(line))
     if world > 1:
         torch.distributed.destroy_process_group()
