@@ -7,13 +7,16 @@
 // (lm/forward.py:44-49): query at absolute position p sees key j iff j <= p and
 // j < past + n_new; a padded query (p >= total) sees every existing key, so it never makes NaN.
 //
-// Grid (splits, Hkv * qtiles, B). A CTA serves the G = Hq / Hkv query heads that share one
-// KV head for up to 32 query rows, over one contiguous chunk of keys: flash-decoding style
-// split-KV so that a batch-1 verify still puts ~300 CTAs on 148 SMs. Each CTA stages 32-key
-// blocks of K and V in shared memory (fp32), keeps an online softmax (max, sum) per row and
-// accumulates P V. The last CTA of each (row, kv head, q tile), found with an atomic ticket,
-// merges the partial results in split order, which keeps the output independent of CTA
-// scheduling; there is no spin-wait.
+// Three kernels by shape. bf16 with d = 64: decode / verify shapes (at most 16 query rows per
+// KV head) run the cluster kernel (attn_cluster.cuh) or, past one cluster's keys, split-KV
+// tensor-core items (attn_item_mma.cuh); prefill shapes run the tensor-core flash kernel
+// (attn_prefill.cuh). fp32 models and other head dims: grid (splits, Hkv * qtiles, B); a CTA
+// serves the G = Hq / Hkv query heads that share one KV head for up to 32 query rows, over
+// one contiguous chunk of keys (flash-decoding style split-KV), stages 32-key blocks of K and
+// V in shared memory (fp32), keeps an online softmax (max, sum) per row and accumulates P V.
+// The last CTA of each (row, kv head, q tile), found with an atomic ticket, merges the partial
+// results in split order, which keeps the output independent of CTA scheduling; there is no
+// spin-wait.
 #include <algorithm>
 #include <cstdlib>
 #include <mutex>
@@ -22,6 +25,7 @@
 #include "attn_cluster.cuh"
 #include "attn_core.cuh"
 #include "attn_item_mma.cuh"
+#include "attn_prefill.cuh"
 
 namespace specb200 {
 namespace {
@@ -48,6 +52,15 @@ __global__ void __launch_bounds__(kAcThreads) attention_cluster_kernel(AttnKerne
   extern __shared__ __align__(16) uint8_t ac_smem[];
   pdl_launch_dependents();
   attention_cluster_cta(ka, blockIdx.z, blockIdx.y, ac_smem, true);
+}
+
+// Prefill shapes (bf16, d = 64, more than 16 query rows per KV head): 64 query rows per CTA on
+// the tensor cores, keys streamed in 64-key blocks (attn_prefill.cuh).
+__global__ void __launch_bounds__(kApThreads) attention_prefill_kernel(AttnArgs a) {
+  __shared__ __align__(128) ApSmem sm;
+  pdl_launch_dependents();
+  pdl_wait();
+  attention_prefill_cta(a, sm);
 }
 
 constexpr int kAcSmemLimit = 200 * 1024;
@@ -100,6 +113,7 @@ bool attention_prepare() {
     // the largest carveout, as every kernel of a forward, so that consecutive kernels share SMs
     for (const void* f : {reinterpret_cast<const void*>(attention_cluster_kernel),
                           reinterpret_cast<const void*>(attention_mma_kernel),
+                          reinterpret_cast<const void*>(attention_prefill_kernel),
                           reinterpret_cast<const void*>(attention_kernel<float, 16>),
                           reinterpret_cast<const void*>(attention_kernel<float, 32>),
                           reinterpret_cast<const void*>(attention_kernel<float, 64>),
@@ -123,6 +137,14 @@ AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len, bool tens
     p.mma = 1;
     return p;
   }
+  if (tensor_items) {  // prefill shapes
+    AttnPlan p;
+    p.qtiles = (T * (Hq / Hkv) + kApRows - 1) / kApRows;
+    p.splits_max = 1;
+    p.chunk = 0;
+    p.mma = 3;
+    return p;
+  }
   AttnPlan p;
   const int G = Hq / Hkv;
   p.qtiles = (T * G + kRows - 1) / kRows;
@@ -137,7 +159,7 @@ AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len, bool tens
 }
 
 size_t attention_partials_bytes(const AttnPlan& p, int B, int Hkv, int D) {
-  if (p.mma >= 2) return 0;  // the cluster kernels merge in distributed shared memory
+  if (p.mma >= 2) return 0;  // the cluster kernel merges in distributed shared memory; prefill does not split
   const size_t groups = static_cast<size_t>(B) * Hkv * p.qtiles;
   return p.splits_max > 1 ? groups * p.splits_max * kRows * (D + 2) * sizeof(float) : 0;
 }
@@ -153,6 +175,12 @@ int launch_attention(const AttnArgs& a, const AttnPlan& p, int* counters, float*
     if (!std::is_same<T, __nv_bfloat16>::value || a.D != 64 || a.T * (a.Hq / a.Hkv) > kAcRowsMax)
       return SPECB200_ERR_UNSUPPORTED;
     e = launch_cluster(a, p, s, pdl);
+    return e == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
+  }
+  if (p.mma == 3) {
+    if (!std::is_same<T, __nv_bfloat16>::value || a.D != 64) return SPECB200_ERR_UNSUPPORTED;
+    if (a.Hkv > 65535 || a.B > 65535) return SPECB200_ERR_ARG;
+    e = launch_kernel(attention_prefill_kernel, dim3(p.qtiles, a.Hkv, a.B), dim3(kApThreads), 0, s, pdl, a);
     return e == cudaSuccess ? SPECB200_OK : SPECB200_ERR_CUDA;
   }
   if (p.mma) {

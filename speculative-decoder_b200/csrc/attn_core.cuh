@@ -1,6 +1,6 @@
 // Paged causal attention for one work item (a batch row, a KV head, a tile of up to 32 query
-// rows and a chunk of keys), shared by the per-layer attention kernel (attention.cu) and the
-// persistent layer-stream kernel (stream.cu). Runs on 128 threads (threadIdx.x 0..127) that
+// rows and a chunk of keys), for the per-layer attention kernel (attention.cu): fp32 models and
+// the shapes the tensor-core kernels do not take. Runs on 128 threads (threadIdx.x 0..127) that
 // synchronise with named barrier 1, over a caller-provided shared-memory buffer of
 // AttnSmem<D>::kFloats floats.
 #pragma once
@@ -224,233 +224,5 @@ __device__ void attention_item(const AttnKernelArgs& ka, int b, int g, int qt, i
   if (tid == 0) ka.counters[group] = 0;
 }
 
-
-}  // namespace specb200
-
-namespace specb200 {
-
-// ---------------------------------------------------------------------------------------
-// Decode/verify attention item for the layer-stream kernel: bf16, d = 64, at most 32 query
-// rows (T x G) per KV head. One item = one (row b, KV head g, key chunk); the chunk's keys are
-// processed in sub-chunks (as many keys as fit the 64 KB scratch, at most 192) with an online
-// softmax. Per sub-chunk there are
-// two memory round trips: the block-table slots (together with q on the first sub-chunk),
-// then every K and V row of the sub-chunk at once with cp.async into shared memory (bf16).
-// Partial results merge exactly as in attention_item (last arriver, split order).
-// ---------------------------------------------------------------------------------------
-constexpr int kDecD = 64;
-constexpr int kDecMaxKeys = 192;
-constexpr int kDecSmemBytes = 64 * 1024;  // the caller's scratch region
-// Runtime layout for R query rows and KC keys per sub-chunk:
-//   K, V [KC][64] bf16 | q [R][65] f32 | scores [R][KC+1] f32 | o [R][64] f32 |
-//   m, l, alpha [R] f32 | lim [R] i32 | slots [KC] i32 | flag
-struct DecSmem {
-  __nv_bfloat16* k;
-  __nv_bfloat16* v;
-  float* qs;
-  float* sc;
-  float* os;
-  float *m, *l, *alpha;
-  int *lim, *slot, *last;
-  int kc, sc_pitch;
-  SPECB200_DEVINL static int keys_for(int R) {
-    const int fixed = R * (kDecD + 1) * 4 + R * kDecD * 4 + R * 16 + 16;
-    const int per_key = 2 * kDecD * 2 + R * 4 + 4;
-    int kc = (kDecSmemBytes - fixed - 4 * R) / per_key;
-    kc = kc > kDecMaxKeys ? kDecMaxKeys : kc;
-    return kc & ~15;
-  }
-  __device__ DecSmem(uint8_t* p, int R) {
-    kc = keys_for(R);
-    sc_pitch = kc + 1;
-    k = reinterpret_cast<__nv_bfloat16*>(p); p += kc * kDecD * 2;
-    v = reinterpret_cast<__nv_bfloat16*>(p); p += kc * kDecD * 2;
-    qs = reinterpret_cast<float*>(p); p += R * (kDecD + 1) * 4;
-    sc = reinterpret_cast<float*>(p); p += R * sc_pitch * 4;
-    os = reinterpret_cast<float*>(p); p += R * kDecD * 4;
-    m = reinterpret_cast<float*>(p); p += R * 4;
-    l = reinterpret_cast<float*>(p); p += R * 4;
-    alpha = reinterpret_cast<float*>(p); p += R * 4;
-    lim = reinterpret_cast<int*>(p); p += R * 4;
-    slot = reinterpret_cast<int*>(p); p += kc * 4;
-    last = reinterpret_cast<int*>(p);
-  }
-};
-
-SPECB200_DEVINL void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-SPECB200_DEVINL void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;" ::: "memory");
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-}
-
-static __device__ void attention_item_decode(const AttnKernelArgs& ka, int b, int g, int split, uint8_t* smem_raw) {
-  const AttnArgs& a = ka.a;
-  constexpr int D = kDecD;
-  const int G = a.Hq / a.Hkv;
-  const int past = a.past[b], nn = a.n_new[b], total = past + nn;
-  const int R = a.T * G;  // <= kRows
-  if (nn <= 0) return;
-  const int t_max = (R - 1) / G;
-  const int kmax = min(total, past + t_max + 1);
-  const int nsplit = min(ka.p.splits_max, (kmax + ka.p.chunk - 1) / ka.p.chunk);
-  if (split >= nsplit) return;
-  const int kbeg = split * ka.p.chunk;
-  const int kend = (split == nsplit - 1) ? kmax : min(kmax, kbeg + ka.p.chunk);
-  DecSmem sm(smem_raw, R);
-  const int KC = sm.kc;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const __nv_bfloat16* q = static_cast<const __nv_bfloat16*>(a.q);
-  const __nv_bfloat16* kp = static_cast<const __nv_bfloat16*>(a.k_pool);
-  const __nv_bfloat16* vp = static_cast<const __nv_bfloat16*>(a.v_pool);
-  const int32_t* table = a.table + static_cast<int64_t>(b) * a.table_stride;
-  // q rows (fp32) and the per-row key limit
-  for (int i = tid; i < R * (D / 8); i += kAttnThreads) {
-    const int r = i / (D / 8), c = (i % (D / 8)) * 8;
-    const int t = r / G, h = g * G + r % G;
-    const uint4 v = *reinterpret_cast<const uint4*>(q + (static_cast<int64_t>(b * a.T + t) * a.Hq + h) * D + c);
-    const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&v);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 f = __bfloat1622float2(h2[j]);
-      sm.qs[r * (D + 1) + c + 2 * j] = f.x;
-      sm.qs[r * (D + 1) + c + 2 * j + 1] = f.y;
-    }
-  }
-  for (int i = tid; i < R * D; i += kAttnThreads) sm.os[i] = 0.f;
-  if (tid < R) {
-    sm.m[tid] = -INFINITY;
-    sm.l[tid] = 0.f;
-    sm.lim[tid] = min(past + tid / G + 1, total);
-  }
-  for (int k0 = kbeg; k0 < kend; k0 += KC) {
-    const int nk = min(KC, kend - k0);
-    for (int j = tid; j < nk; j += kAttnThreads) {
-      const int key = k0 + j;
-      sm.slot[j] = table[key / a.bs] * a.bs + key % a.bs;
-    }
-    attn_sync();
-    // every K and V row of the sub-chunk in flight at once (16 B per cp.async)
-    for (int i = tid; i < nk * 16; i += kAttnThreads) {
-      const int j = i >> 4, part = i & 15, isv = part >> 3, c = (part & 7) * 8;
-      const int64_t off = (static_cast<int64_t>(sm.slot[j]) * a.Hkv + g) * D + c;
-      cp_async16((isv ? sm.v : sm.k) + j * D + c, (isv ? vp : kp) + off);
-    }
-    cp_async_wait_all();
-    attn_sync();
-    // scores
-    for (int i = tid; i < R * nk; i += kAttnThreads) {
-      const int r = i / nk, j = i % nk;
-      float s = -INFINITY;
-      if (k0 + j < sm.lim[r]) {
-        const __nv_bfloat162* kr = reinterpret_cast<const __nv_bfloat162*>(sm.k + j * D);
-        float acc = 0.f;
-#pragma unroll
-        for (int c = 0; c < D / 2; ++c) {
-          const float2 kf = __bfloat1622float2(kr[(c + j) & (D / 2 - 1)]);
-          const int cc = 2 * ((c + j) & (D / 2 - 1));
-          acc = fmaf(sm.qs[r * (D + 1) + cc], kf.x, acc);
-          acc = fmaf(sm.qs[r * (D + 1) + cc + 1], kf.y, acc);
-        }
-        s = acc * a.scale;
-      }
-      sm.sc[r * sm.sc_pitch + j] = s;
-    }
-    attn_sync();
-    // online softmax per row (one warp per row)
-    for (int r = warp; r < R; r += kAttnThreads / 32) {
-      float mx = -INFINITY;
-      float* scr = sm.sc + r * sm.sc_pitch;
-      for (int j = lane; j < nk; j += 32) mx = fmaxf(mx, scr[j]);
-      mx = warp_max(mx);
-      const float m_old = sm.m[r], m_new = fmaxf(m_old, mx);
-      float sum = 0.f;
-      for (int j = lane; j < nk; j += 32) {
-        const float p = (m_new == -INFINITY) ? 0.f : expf(scr[j] - m_new);
-        scr[j] = p;
-        sum += p;
-      }
-      sum = warp_sum(sum);
-      if (lane == 0) {
-        const float alpha = (m_new == -INFINITY) ? 1.f : expf(m_old - m_new);
-        sm.l[r] = sm.l[r] * alpha + sum;
-        sm.m[r] = m_new;
-        sm.alpha[r] = alpha;
-      }
-    }
-    attn_sync();
-    // o = o * alpha + P V
-    for (int i = tid; i < R * (D / 2); i += kAttnThreads) {
-      const int r = i / (D / 2), c = (i % (D / 2)) * 2;
-      float ax = sm.os[r * D + c] * sm.alpha[r], ay = sm.os[r * D + c + 1] * sm.alpha[r];
-      const float* scr = sm.sc + r * sm.sc_pitch;
-      for (int j = 0; j < nk; ++j) {
-        const float p = scr[j];
-        const float2 vf = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(sm.v + j * D + c));
-        ax = fmaf(p, vf.x, ax);
-        ay = fmaf(p, vf.y, ay);
-      }
-      sm.os[r * D + c] = ax;
-      sm.os[r * D + c + 1] = ay;
-    }
-    attn_sync();
-  }
-  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(a.out);
-  auto write_out = [&](int r, int c, float v) {
-    const int t = r / G, h = g * G + r % G;
-    out[(static_cast<int64_t>(b * a.T + t) * a.Hq + h) * D + c] = __float2bfloat16_rn(v);
-  };
-  if (nsplit == 1) {
-    for (int i = tid; i < R * D; i += kAttnThreads) write_out(i / D, i % D, sm.os[i] / sm.l[i / D]);
-    return;
-  }
-  const int group = b * a.Hkv + g;  // qtiles == 1
-  const size_t part_elems = static_cast<size_t>(kRows) * (D + 2);
-  float* mine = ka.part + (static_cast<size_t>(group) * ka.p.splits_max + split) * part_elems;
-  for (int i = tid; i < R * D; i += kAttnThreads) mine[i] = sm.os[i];
-  if (tid < R) {
-    mine[kRows * D + tid] = sm.m[tid];
-    mine[kRows * D + kRows + tid] = sm.l[tid];
-  }
-  __threadfence();
-  attn_sync();
-  if (tid == 0) *sm.last = (atomicAdd(ka.counters + group, 1) == nsplit - 1);
-  attn_sync();
-  if (!*sm.last) return;
-  __threadfence();
-  const float* base = ka.part + static_cast<size_t>(group) * ka.p.splits_max * part_elems;
-  for (int i = tid; i < R * D; i += kAttnThreads) {
-    const int r = i / D, c = i % D;
-    float M = -INFINITY;
-    for (int sp = 0; sp < nsplit; ++sp) M = fmaxf(M, __ldcg(base + sp * part_elems + kRows * D + r));
-    float L = 0.f, O = 0.f;
-    for (int sp = 0; sp < nsplit; ++sp) {
-      const float* ps = base + sp * part_elems;
-      const float ms = __ldcg(ps + kRows * D + r);
-      const float w = (ms == -INFINITY) ? 0.f : expf(ms - M);
-      L = fmaf(__ldcg(ps + kRows * D + kRows + r), w, L);
-      O = fmaf(__ldcg(ps + r * D + c), w, O);
-    }
-    write_out(r, c, O / L);
-  }
-  if (tid == 0) ka.counters[group] = 0;
-}
-
-// Split plan for the layer-stream kernel: about one item per CTA (chunks rounded to 16 keys).
-inline AttnPlan plan_attention_decode(int B, int Hkv, int max_kv_len, int grid) {
-  AttnPlan p;
-  p.qtiles = 1;
-  const int groups = B * Hkv;
-  int splits = grid / groups;  // at most one item per CTA
-  const int max_len = max_kv_len < 1 ? 1 : max_kv_len;
-  splits = splits < 1 ? 1 : splits;
-  const int blocks = (max_len + kKeys - 1) / kKeys;
-  if (splits > blocks) splits = blocks;
-  if (groups > kAttnMaxCounters) splits = 1;
-  p.chunk = (((max_len + splits - 1) / splits) + 15) / 16 * 16;
-  p.splits_max = (max_len + p.chunk - 1) / p.chunk;
-  return p;
-}
 
 }  // namespace specb200

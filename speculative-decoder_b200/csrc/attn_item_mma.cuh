@@ -1,6 +1,6 @@
 // Decode / verify attention work item on the tensor cores: bf16, d = 64, at most 16 query rows
-// (T x G) per KV head, for the per-layer attention kernel (attention.cu) and the layer-stream
-// kernel (stream.cu). One item = (sequence b, KV head g, key chunk `split` of the plan).
+// (T x G) per KV head, for the per-layer attention kernel (attention.cu) when the keys exceed
+// one cluster. One item = (sequence b, KV head g, key chunk `split` of the plan).
 //
 // Same computation and mask as attention_item (attn_core.cuh) -- the reference's SDPA over the
 // gathered cache, lm/forward.py:44-49,62-63 -- with the products on mma.sync (attn_mma.cuh).

@@ -1,6 +1,6 @@
-// Fused GEMM epilogues, shared by the per-layer GEMM kernels (gemm.cu) and the persistent
-// layer-stream kernel (stream.cu). Each runs on 128 threads over an fp32 tile held in shared
-// memory: tile[token][feature], pitch kEpiPitch, feature j = output column n0 + j.
+// Fused GEMM epilogues of the per-layer GEMM kernels (gemm.cu). Each runs on 128 threads over
+// an fp32 tile held in shared memory: tile[token][feature], pitch kEpiPitch, feature j = output
+// column n0 + j.
 #pragma once
 #include "gemm.cuh"
 

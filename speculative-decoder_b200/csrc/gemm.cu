@@ -321,10 +321,18 @@ GemmShape plan_gemm(int M, int N, int K, bool tensor_core) {
   s.M = M;
   s.N = N;
   s.K = K;
-  if (tensor_core) s.BN = std::min(256, ((M + 15) / 16) * 16);
-  else s.BN = std::min(kSimtMaxBN, ((M + 3) / 4) * 4);
-  s.m_tiles = (M + s.BN - 1) / s.BN;
   s.n_tiles = (N + kTileN - 1) / kTileN;
+  if (tensor_core) {
+    s.BN = std::min(256, ((M + 15) / 16) * 16);
+    // Prefill and large batches: halve the token tile (kept a multiple of 16, the MMA's N
+    // granularity) until the grid covers the 148 SMs (a 512-token q/k/v projection gets 192
+    // CTAs of 128 tokens instead of 96 of 256).
+    if (M > 16)
+      while (s.BN > 32 && s.n_tiles * ((M + s.BN - 1) / s.BN) < 148) s.BN = (s.BN / 2 + 15) / 16 * 16;
+  } else {
+    s.BN = std::min(kSimtMaxBN, ((M + 3) / 4) * 4);
+  }
+  s.m_tiles = (M + s.BN - 1) / s.BN;
   s.kblocks = (K + kTileK - 1) / kTileK;
   const int ctas = s.n_tiles * s.m_tiles;
   int splits;
@@ -356,9 +364,11 @@ namespace {
 int tc_stages(int BN, size_t* smem_bytes) {
   const size_t stage = kWTileBytes + static_cast<size_t>(BN) * kTileK * 2;
   const size_t tile = static_cast<size_t>(BN) * kEpiPitch * 4;
-  // About 110 KB of ring lets a CTA of the next GEMM share the SM and prefetch its weights
-  // (measured 1.343 vs 1.361 ms per verify with the 200 KB ring).
-  const size_t budget = 110 * 1024;
+  // Decode and verify shapes (16 tokens): about 110 KB of ring lets a CTA of the next GEMM
+  // share the SM and prefetch its weights (measured 1.343 vs 1.361 ms per verify with the
+  // 200 KB ring). Larger token tiles (prefill, large batches) keep one CTA per SM with a deep
+  // ring, since their operand tiles are large and the GEMMs long.
+  const size_t budget = BN <= 16 ? 110 * 1024 : 200 * 1024;
   int stages = static_cast<int>(std::min<size_t>(8, budget / stage));
   while (static_cast<size_t>(stages) * stage < tile) ++stages;
   stages = std::max(stages, 2);
@@ -383,6 +393,8 @@ bool gemm_prepare() {
 
 int launch_gemm_tc(const GemmShape& s, const CUtensorMap& w_map, const CUtensorMap& x_map, const Epilogue& epi,
                    GemmScratch scratch, int32_t* status, cudaStream_t stream, bool pdl) {
+  // the token tile is the MMA's N: a multiple of 16 from 16 to 256 for M = 128
+  if (s.BN < 16 || s.BN > 256 || s.BN % 16) return SPECB200_ERR_ARG;
   size_t smem = 0;
   const int stages = tc_stages(s.BN, &smem);
   static std::mutex mu;

@@ -88,13 +88,15 @@ constexpr size_t kAttnCounterBytes = kAttnMaxCounters * sizeof(int);
 struct AttnPlan {
   int chunk, splits_max, qtiles;
   // 1: tensor-core decode items (bf16, d = 64, at most 16 query rows per KV head);
-  // 2: the cluster kernel for the same shapes (splits_max = cluster size, chunk = keys per CTA)
+  // 2: the cluster kernel for the same shapes (splits_max = cluster size, chunk = keys per CTA);
+  // 3: prefill shapes on the tensor cores (bf16, d = 64; qtiles = 64-row query tiles, no split)
   int mma = 0;
 };
 // Sets the cluster kernel's shared-memory limit; call outside any stream capture.
 bool attention_prepare();
-// tensor_items: the call is bf16 with d = 64, so decode / verify shapes (T x G <= 16) may use
-// the tensor-core items (attn_item_mma.cuh).
+// tensor_items: the call is bf16 with d = 64, so decode / verify shapes (T x G <= 16) use the
+// cluster kernel or the tensor-core items (attn_item_mma.cuh) and prefill shapes the
+// tensor-core prefill kernel (attn_prefill.cuh).
 AttnPlan plan_attention(int B, int T, int Hq, int Hkv, int max_kv_len, bool tensor_items);
 size_t attention_partials_bytes(const AttnPlan& p, int B, int Hkv, int D);
 size_t attention_workspace_bytes(const AttnPlan& p, int B, int Hkv, int D);  // counters + partials

@@ -8,10 +8,9 @@ same SpecStats.
 
 Config 2 (1.7B architecture target, 135M architecture draft, bf16, k = 4, 256 new tokens):
 speculative output must equal the engine's own plain decoding bit for bit; against the
-reference's bf16 path (the bf16-rounding oracle on the same prefix) every generated token must
-be the argmax unless the top-two logits sit within a few bf16 grid steps (the reference's own
-criterion for low-precision flips, widened for summation-order differences in every matmul),
-and flips against the fp32 path are reported and bounded by the bf16 forward tolerance.
+reference's bf16 and fp32 paths (the oracle teacher forced on the engine's prefix) every
+generated token that is not the argmax must sit within the bf16 logit tolerance, and such flips
+may be no more frequent than bf16 rounding alone causes between the two oracle paths.
 """
 from __future__ import annotations
 
@@ -73,22 +72,25 @@ def _bf16_ulp(x: float) -> float:
     return float(torch.nextafter(v, torch.tensor(float("inf"), dtype=torch.bfloat16)) - v)
 
 
-def _teacher_forced_flips(w, prec_mode: str, prompt: list[int], out: list[int]):
+def _teacher_forced_logits(w, prec_mode: str, prompt: list[int], out: list[int]) -> np.ndarray:
     """Oracle logits at every generated position given the engine's own prefix (one forward over
-    prompt + output); returns, per position whose engine token is not the oracle's argmax, the
-    oracle's top-two gap, the model dtype's grid step at the top logit and the position's
-    largest |logit|."""
+    prompt + output[:-1])."""
     from oracle import forward as ofw
 
     prec = ofw.Precision(prec_mode)
     seq = prompt + out
     oc = ofw.Cache(w, len(seq) // 16 + 4, 16, prec)
     oc.add(0)
-    logits = ofw.forward(w, oc, [0], np.array([seq[:-1]]), [len(seq) - 1], prec)[0, len(prompt) - 1:]
-    top2 = np.sort(logits, axis=-1)[:, -2:]
-    scale = np.abs(logits).max(axis=-1)
+    return ofw.forward(w, oc, [0], np.array([seq[:-1]]), [len(seq) - 1], prec)[0, len(prompt) - 1:]
+
+
+def _flips(logits: np.ndarray, out: list[int]):
+    """Per position whose token is not the argmax of `logits`: (position, the gap between the
+    argmax's logit and the token's, the bf16 grid step at the top logit, the largest |logit|)."""
     arg = logits.argmax(-1)
-    return [(i, float(top2[i, 1] - top2[i, 0]), _bf16_ulp(float(top2[i, 1])), float(scale[i]))
+    top = logits.max(-1)
+    scale = np.abs(logits).max(-1)
+    return [(i, float(top[i] - logits[i, out[i]]), _bf16_ulp(float(top[i])), float(scale[i]))
             for i in range(len(out)) if arg[i] != out[i]]
 
 
@@ -98,16 +100,17 @@ def test_config2_spec_equals_plain_and_oracle():
 
     - Speculative output equals plain decoding bit for bit (both on the engine).
     - Against the reference's bf16 path (the bf16-rounding oracle, teacher forced on the
-      engine's own prefix): a token that differs from the oracle's argmax is a flip. The
-      reference excuses a low-precision flip when its top-two gap lies within two steps of the
-      dtype's grid (tests/test_greedy_identity.py:143-164 of the reference), for two runs that
-      differ in the shape of one matmul; the oracle differs from the engine in the summation
-      order of every matmul, whose fp32 differences move bf16 roundings and compound through 24
-      layers, and random-init weights leave many near ties (logits about N(0, 1) over 49,152
-      ids). So flips must lie within four grid steps and stay under 10% of the outputs.
-    - Against the fp32 path: bf16 rounding through 24 layers moves logits by more than a grid
-      step, so flips are reported and each must lie within the bf16 forward's tolerance (top-two
-      gap at most 2e-2 of that position's largest |logit|)."""
+      engine's own prefix): a generated token that is not the oracle's argmax is a flip. The
+      oracle differs from the engine in the summation order of every matmul; those fp32
+      differences move bf16 roundings, which compound through 24 layers, and random-init
+      weights leave many near ties (logits of scale ~4 over 49,152 ids, top-two gaps of a few
+      bf16 grid steps). So every flip must lie within the logit tolerance the path is held to
+      (top-two gap at most rtol 2e-2 of the position's largest |logit|), and flips must be no
+      more frequent than bf16 rounding alone causes: at most the number of positions where the
+      bf16 oracle's own argmax departs from the fp32 oracle's, plus a margin of 5% of the
+      outputs. Flips within two grid steps (the reference's criterion for low-precision flips,
+      tests/test_greedy_identity.py:143-164 of the reference) are counted in the report.
+    - Against the fp32 path: every flip within the same rtol 2e-2 of the largest |logit|."""
     from baselines import cached_autoregressive
     from oracle import forward as ofw
     from spec.draft import ModelDraft
@@ -123,12 +126,15 @@ def test_config2_spec_equals_plain_and_oracle():
     assert spec[0] == plain
     assert st.rounds >= 1 and len(plain) == 256
 
-    flips_bf16 = _teacher_forced_flips(w, "bf16", prompt, plain)
-    flips_f32 = _teacher_forced_flips(w, "f32", prompt, plain)
-    print(f"config2: acceptance {st.accepted}/{st.drafted}; flips vs the bf16 oracle {len(flips_bf16)}/256: "
-          f"{flips_bf16}; vs the fp32 oracle {len(flips_f32)}/256: {flips_f32}")
-    assert len(flips_bf16) <= 0.10 * len(plain), flips_bf16
-    for i, gap, ulp, _ in flips_bf16:
-        assert gap <= 4 * ulp, (i, gap, ulp)
-    for i, gap, _, scale in flips_f32:
+    lo_bf16 = _teacher_forced_logits(w, "bf16", prompt, plain)
+    lo_f32 = _teacher_forced_logits(w, "f32", prompt, plain)
+    flips_bf16 = _flips(lo_bf16, plain)
+    flips_f32 = _flips(lo_f32, plain)
+    rounding_flips = int((lo_bf16.argmax(-1) != lo_f32.argmax(-1)).sum())
+    within2 = sum(gap <= 2 * ulp for _, gap, ulp, _ in flips_bf16)
+    print(f"config2: acceptance {st.accepted}/{st.drafted}; flips vs the bf16 oracle {len(flips_bf16)}/256 "
+          f"({within2} within two grid steps): {flips_bf16}; vs the fp32 oracle {len(flips_f32)}/256: {flips_f32}; "
+          f"bf16 oracle vs fp32 oracle argmax differences: {rounding_flips}/256")
+    for i, gap, _, scale in flips_bf16 + flips_f32:
         assert gap <= 2e-2 * scale, (i, gap, scale)
+    assert len(flips_bf16) <= rounding_flips + 0.05 * len(plain), (len(flips_bf16), rounding_flips)

@@ -387,3 +387,27 @@ def test_decode_schedules_match_oracle(dims):
             g, o = got[b, :n], want[b, :n]
             scale = np.abs(o).max()
             assert np.abs(g - o).max() <= 2e-2 * scale + 1e-3, (b, np.abs(g - o).max(), scale)
+
+
+def test_long_prefill_matches_oracle():
+    """A 1100-token prefill and a 300-token continuation (tensor-core prefill attention over 18
+    and 22 key blocks per query tile; prefill-sized GEMM token tiles) of a 2-layer bf16 model
+    with grouped heads, against the bf16 oracle: last-position logits of the prefill and every
+    position's logits of the continuation, within rtol 2e-2 of the largest logit."""
+    from lm.forward import forward
+
+    model = _bf16_model(256, 2, 8, 2, 512, 4096, seed=17, theta=130000.0)
+    w = ofw.weights_from_model(model)
+    prec = ofw.Precision("bf16")
+    model = model.to(DEV)
+    cache = new_cache(model, block_size=16)
+    ocache = ofw.Cache(w, 4096, 16, prec)
+    cache.add(0)
+    ocache.add(0)
+    g = torch.Generator().manual_seed(33)
+    for n, last in ((1100, True), (300, False)):
+        ids = torch.randint(0, 4096, (1, n), generator=g)
+        got = forward(model, cache, [0], ids, [n], last_only=last).float().cpu().numpy()
+        want = ofw.forward(w, ocache, [0], ids.numpy(), [n], prec, last_only=last)
+        scale = np.abs(want).max()
+        assert np.abs(got - want).max() <= 2e-2 * scale + 1e-3, (n, np.abs(got - want).max(), scale)

@@ -76,7 +76,14 @@ def test_resident_draft_matches_oracle(draft):
             for pool, opool in ((cache.k, ocache.k), (cache.v, ocache.v)):
                 e = pool[:, torch.tensor(slots)].float().cpu().numpy()
                 o = opool[:, oslots]
-                assert np.abs(e - o).max() <= 2 ** -6 * max(1.0, np.abs(o).max()), (s, np.abs(e - o).max())
+                # layer 0's entries depend on the step's own tokens only: within one bf16
+                # grid step of the oracle. Deeper layers also carry bf16 roundings of every
+                # earlier layer, made in another summation order (they drift by a few grid
+                # steps over 30 layers); a wrong position, rotation or slot is off by O(1).
+                for layer in range(o.shape[0]):
+                    d = np.abs(e[layer] - o[layer]).max()
+                    bound = (2 ** -7 if layer == 0 else 4e-2) * max(1.0, np.abs(o[layer]).max())
+                    assert d <= bound, (s, layer, d)
 
 
 def test_resident_repeated_calls_are_identical(draft):
