@@ -177,6 +177,7 @@ int run_resident(const Model& m, const specb200_batch& bt, char* ws, const Carve
   a.region = reinterpret_cast<uint8_t*>(ws + cv.res_region);
   a.status = bt.status;
   a.wait_limit = g_wait_limit.load();
+  a.trace = reinterpret_cast<unsigned long long*>(bt.trace);
   a.p = cv.rp;
   return launch_resident(a, s);
 }

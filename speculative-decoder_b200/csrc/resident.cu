@@ -61,6 +61,15 @@ SPECB200_DEVINL int ld_volatile_i32(const unsigned* p) {
 
 SPECB200_DEVINL void cons_sync() { asm volatile("bar.sync 2, 256;" ::: "memory"); }
 
+// Phase stamp j of this CTA (thread 0 of the compute warps) when the launch records a trace.
+SPECB200_DEVINL void stamp(const ResArgs& a, int j) {
+  if (a.trace && threadIdx.x == 0) {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    a.trace[static_cast<size_t>(j) * gridDim.x + blockIdx.x] = t;
+  }
+}
+
 SPECB200_DEVINL void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
@@ -188,6 +197,32 @@ SPECB200_DEVINL bool pk_wait(const ResArgs& a, const ResShared& s, const uint4* 
       atomicExch(ctl + 2, 1u);
       *s.abort = 1;
       return false;
+    }
+  }
+}
+
+// Packets i = tid, tid + 256, ... < n of the compute warps: the loads of up to four go out
+// together (one round trip when they have all arrived), and only the ones whose epoch has not
+// arrived yet are then waited for. use(i, v, ok) consumes packet i (ok false after a wait gave
+// up or the launch was aborted).
+template <class At, class Use>
+SPECB200_DEVINL void pk_gather(const ResArgs& a, const ResShared& s, int n, uint32_t ep, unsigned* ctl, At&& at,
+                               Use&& use) {
+  constexpr int kBatch = 4;
+  for (int base = threadIdx.x; base < n; base += kBatch * kResConsumers) {
+    uint4 v[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = base + j * kResConsumers;
+      if (i < n) v[j] = pk_load(at(i));
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int i = base + j * kResConsumers;
+      if (i >= n) break;
+      bool ok = v[j].y == ep && v[j].w == ep;
+      if (!ok) ok = pk_wait(a, s, at(i), ep, v[j], ctl);
+      use(i, v[j], ok);
     }
   }
 }
@@ -433,32 +468,39 @@ SPECB200_DEVINL void att_item(const ResArgs& a, const ResShared& s, const Region
   const int G = a.Hq / a.Hkv, R = a.T * G, P = (a.Hq + 2 * a.Hkv) * 32;
   const int past = a.past[it.b], nn = a.n_new[it.b], total = past + nn;
   const uint4* qkv = rg.qkv + static_cast<size_t>(par) * rg.qkv_n;
-  // q rows (row r = token t, head g G + r % G) and this call's keys / values inside the chunk
-  for (int i = tid; i < 16 * 32; i += kResConsumers) {
+  // q rows (row r = token t, head g G + r % G; rows past R are zero) and this call's keys /
+  // values inside the chunk, their packets requested together
+  for (int i = R * 32 + tid; i < 16 * 32; i += kResConsumers) {
     const int r = i >> 5, c = i & 31;
-    uint32_t w = 0;
-    if (r < R) {
-      const int t = r / G, h = it.g * G + r % G;
-      const int word = (it.b * a.T + t) * P + h * 32 + c;
-      uint4 v;
-      if (!pk_wait(a, s, qkv + (word >> 1), ep_in, v, rg.ctl)) w = 0;
-      else w = (word & 1) ? v.z : v.x;
-    }
-    q_s[am_swz(r, c)] = __ushort_as_bfloat16(static_cast<unsigned short>(w & 0xffffu));
-    q_s[am_swz(r, c + 32)] = __ushort_as_bfloat16(static_cast<unsigned short>(w >> 16));
+    q_s[am_swz(r, c)] = __float2bfloat16_rn(0.f);
+    q_s[am_swz(r, c + 32)] = __float2bfloat16_rn(0.f);
   }
+  auto q_word = [&](int i) {
+    const int r = i >> 5, c = i & 31, t = r / G, h = it.g * G + r % G;
+    return (it.b * a.T + t) * P + h * 32 + c;
+  };
+  pk_gather(
+      a, s, R * 32, ep_in, rg.ctl, [&](int i) { return qkv + (q_word(i) >> 1); },
+      [&](int i, const uint4& v, bool ok) {
+        const uint32_t w = ok ? ((q_word(i) & 1) ? v.z : v.x) : 0u;
+        const int r = i >> 5, c = i & 31;
+        q_s[am_swz(r, c)] = __ushort_as_bfloat16(static_cast<unsigned short>(w & 0xffffu));
+        q_s[am_swz(r, c + 32)] = __ushort_as_bfloat16(static_cast<unsigned short>(w >> 16));
+      });
   const int nlo = max(it.kbeg, past), nhi = it.kend;  // new keys inside the chunk
-  for (int i = tid; i < max(0, nhi - nlo) * 64; i += kResConsumers) {
+  auto kv_word = [&](int i) {
     const int key = nlo + (i >> 6), isv = (i >> 5) & 1, c = i & 31;
-    const int t = key - past;
-    const int word = (it.b * a.T + t) * P + (a.Hq + (isv ? a.Hkv : 0) + it.g) * 32 + c;
-    uint4 v;
-    uint32_t w = 0;
-    if (pk_wait(a, s, qkv + (word >> 1), ep_in, v, rg.ctl)) w = (word & 1) ? v.z : v.x;
-    bf16* dst = isv ? v_s : k_s;
-    dst[am_swz(key - it.kbeg, c)] = __ushort_as_bfloat16(static_cast<unsigned short>(w & 0xffffu));
-    dst[am_swz(key - it.kbeg, c + 32)] = __ushort_as_bfloat16(static_cast<unsigned short>(w >> 16));
-  }
+    return (it.b * a.T + (key - past)) * P + (a.Hq + (isv ? a.Hkv : 0) + it.g) * 32 + c;
+  };
+  pk_gather(
+      a, s, max(0, nhi - nlo) * 64, ep_in, rg.ctl, [&](int i) { return qkv + (kv_word(i) >> 1); },
+      [&](int i, const uint4& v, bool ok) {
+        const uint32_t w = ok ? ((kv_word(i) & 1) ? v.z : v.x) : 0u;
+        const int key = nlo + (i >> 6), isv = (i >> 5) & 1, c = i & 31;
+        bf16* dst = isv ? v_s : k_s;
+        dst[am_swz(key - it.kbeg, c)] = __ushort_as_bfloat16(static_cast<unsigned short>(w & 0xffffu));
+        dst[am_swz(key - it.kbeg, c + 32)] = __ushort_as_bfloat16(static_cast<unsigned short>(w >> 16));
+      });
   cp_async_wait<0>();
   cons_sync();
   AmState st;
@@ -492,18 +534,18 @@ SPECB200_DEVINL void att_gather(const ResArgs& a, const ResShared& s, const Regi
   const bool valid = tab[kResMaxRows + 1] == 0;  // the item table fits the packet buffer
   float* stage = reinterpret_cast<float*>(s.att);  // [items][R][66]
   const uint4* src = rg.att + static_cast<size_t>(par) * rg.att_n;
-  for (int i = tid; i < n_items * R * kResAttRow; i += kResConsumers) {
-    const int item = i / (R * kResAttRow), rem = i - item * R * kResAttRow;
-    const int r = rem / kResAttRow, q = rem - r * kResAttRow;
-    uint4 v;
-    float f0 = 0.f, f1 = 0.f;
-    if (pk_wait(a, s, src + static_cast<size_t>(item) * kResMaxQRows * kResAttRow + r * kResAttRow + q, ep, v, rg.ctl)) {
-      f0 = __uint_as_float(v.x);
-      f1 = __uint_as_float(v.z);
-    }
-    stage[(item * R + r) * 66 + 2 * q] = f0;
-    stage[(item * R + r) * 66 + 2 * q + 1] = f1;
-  }
+  pk_gather(
+      a, s, n_items * R * kResAttRow, ep, rg.ctl,
+      [&](int i) {
+        const int item = i / (R * kResAttRow), rem = i - item * R * kResAttRow;
+        return src + static_cast<size_t>(item) * kResMaxQRows * kResAttRow + rem;
+      },
+      [&](int i, const uint4& v, bool ok) {
+        const int item = i / (R * kResAttRow), rem = i - item * R * kResAttRow;
+        const int r = rem / kResAttRow, q = rem - r * kResAttRow;
+        stage[(item * R + r) * 66 + 2 * q] = ok ? __uint_as_float(v.x) : 0.f;
+        stage[(item * R + r) * 66 + 2 * q + 1] = ok ? __uint_as_float(v.z) : 0.f;
+      });
   cons_sync();
   const int QD = a.Hq * 64;
   for (int i = tid; valid && i < a.M * QD; i += kResConsumers) {
@@ -532,26 +574,23 @@ SPECB200_DEVINL void read_rows(const ResArgs& a, const ResShared& s, const uint4
                                bool to_h, unsigned* ctl) {
   const int tid = threadIdx.x;
   const int per = words / 2;  // uint4 per row
-  for (int i = tid; i < a.M * per; i += kResConsumers) {
-    const int m = i / per, q = i - m * per;
-    uint4 v;
-    uint32_t w0 = 0, w1 = 0;
-    if (pk_wait(a, s, src + i, ep, v, ctl)) {
-      w0 = v.x;
-      w1 = v.z;
-    }
-    if (to_h) {
-      float* hr = s.h + m * a.H + 4 * q;
-      hr[0] = bf_lo(w0);
-      hr[1] = bf_hi(w0);
-      hr[2] = bf_lo(w1);
-      hr[3] = bf_hi(w1);
-    } else {
-      uint32_t* xr = reinterpret_cast<uint32_t*>(s.x) + m * words + 2 * q;
-      xr[0] = w0;
-      xr[1] = w1;
-    }
-  }
+  pk_gather(
+      a, s, a.M * per, ep, ctl, [&](int i) { return src + i; },
+      [&](int i, const uint4& v, bool ok) {
+        const int m = i / per, q = i - m * per;
+        const uint32_t w0 = ok ? v.x : 0u, w1 = ok ? v.z : 0u;
+        if (to_h) {
+          float* hr = s.h + m * a.H + 4 * q;
+          hr[0] = bf_lo(w0);
+          hr[1] = bf_hi(w0);
+          hr[2] = bf_lo(w1);
+          hr[3] = bf_hi(w1);
+        } else {
+          uint32_t* xr = reinterpret_cast<uint32_t*>(s.x) + m * words + 2 * q;
+          xr[0] = w0;
+          xr[1] = w1;
+        }
+      });
   cons_sync();
 }
 
@@ -568,7 +607,8 @@ SPECB200_DEVINL void write_rows(const ResArgs& a, const ResShared& s, uint4* dst
 }
 
 // ---------------------------------------------------------------- the kernel
-__global__ void __launch_bounds__(kResThreads, 1) resident_kernel(const __grid_constant__ ResArgs a) {
+// 288 threads, one CTA per SM: up to 216 registers a thread (62,208 of the SM's 65,536).
+__global__ void __maxnreg__(216) resident_kernel(const __grid_constant__ ResArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cta = blockIdx.x, S = a.p.slots;
@@ -678,6 +718,7 @@ __global__ void __launch_bounds__(kResThreads, 1) resident_kernel(const __grid_c
     };
     const int P = (a.Hq + 2 * a.Hkv) * 32;
     const int n_items = items_total(a, tab);
+    stamp(a, 9 * a.L + 2);
     for (int l = 0; l < a.L; ++l) {
       const int par = l & 1;
       const ResLayer& Lw = a.layers[l];
@@ -699,6 +740,7 @@ __global__ void __launch_bounds__(kResThreads, 1) resident_kernel(const __grid_c
       } else {
         read_rows(a, s, rg.hout + static_cast<size_t>(par ^ 1) * rg.h_n, a.H / 2, ep(l - 1, 4), true, rg.ctl);
       }
+      stamp(a, 9 * l);
       // ---- q / k / v with RoPE; k and v also into the pool
       res_norm(a, s, Lw.attn_norm, a.M, nullptr);
       int p0, p1;
@@ -731,6 +773,7 @@ __global__ void __launch_bounds__(kResThreads, 1) resident_kernel(const __grid_c
         }
       });
       if (!*s.abort) write_rows(a, s, rg.qkv + static_cast<size_t>(par) * rg.qkv_n, P, p0, p1, ep(l, 0));
+      stamp(a, 9 * l + 1);
       // ---- attention items
       for (int it = cta; it < n_items; it += a.p.grid) {
         const Item item = item_at(a, tab, it);
@@ -741,8 +784,10 @@ __global__ void __launch_bounds__(kResThreads, 1) resident_kernel(const __grid_c
         att_item(a, s, rg, item, par, ep(l, 0), ep(l, 1), it);
       }
       if (!has_item) cp_async_wait<0>();
+      stamp(a, 9 * l + 2);
       // ---- o with the residual add
       att_gather(a, s, rg, tab, par, ep(l, 1));
+      stamp(a, 9 * l + 3);
       int r0, r1;
       share(a.H, a.p.grid, cta, 4, r0, r1);
       consume(l, PH_O, [&](const Piece& pc) {
@@ -753,9 +798,11 @@ __global__ void __launch_bounds__(kResThreads, 1) resident_kernel(const __grid_c
         }
       });
       if (!*s.abort) write_rows(a, s, rg.hmid + static_cast<size_t>(par) * rg.h_n, a.H / 2, r0 / 2, r1 / 2, ep(l, 2));
+      stamp(a, 9 * l + 4);
       // ---- gate / up with SiLU * mul
       read_rows(a, s, rg.hmid + static_cast<size_t>(par) * rg.h_n, a.H / 2, ep(l, 2), true, rg.ctl);
       res_norm(a, s, Lw.mlp_norm, a.M, nullptr);
+      stamp(a, 9 * l + 5);
       int f0, f1;
       share(a.I, a.p.grid, cta, 4, f0, f1);
       consume(l, PH_GU, [&](const Piece& pc) {
@@ -768,8 +815,10 @@ __global__ void __launch_bounds__(kResThreads, 1) resident_kernel(const __grid_c
         }
       });
       if (!*s.abort) write_rows(a, s, rg.act + static_cast<size_t>(par) * rg.act_n, a.I / 2, f0 / 2, f1 / 2, ep(l, 3));
+      stamp(a, 9 * l + 6);
       // ---- down with the residual add
       read_rows(a, s, rg.act + static_cast<size_t>(par) * rg.act_n, a.I / 2, ep(l, 3), false, rg.ctl);
+      stamp(a, 9 * l + 7);
       consume(l, PH_DOWN, [&](const Piece& pc) {
         bf16* ob = reinterpret_cast<bf16*>(s.out);
         for (int i = tid; i < a.M * pc.n; i += kResConsumers) {
@@ -778,10 +827,12 @@ __global__ void __launch_bounds__(kResThreads, 1) resident_kernel(const __grid_c
         }
       });
       if (!*s.abort) write_rows(a, s, rg.hout + static_cast<size_t>(par) * rg.h_n, a.H / 2, r0 / 2, r1 / 2, ep(l, 4));
+      stamp(a, 9 * l + 8);
     }
     // ---- final norm (each sequence's last token row when last_only) and the LM head
     const int lp = (a.L - 1) & 1;
     read_rows(a, s, rg.hout + static_cast<size_t>(lp) * rg.h_n, a.H / 2, ep(a.L - 1, 4), true, rg.ctl);
+    stamp(a, 9 * a.L);
     const int rows_out = a.last_only ? a.B : a.M;
     int* sel = s.misc + 16;
     if (tid < rows_out) sel[tid] = a.last_only ? tid * a.T + max(a.n_new[tid] - 1, 0) : tid;
@@ -793,6 +844,7 @@ __global__ void __launch_bounds__(kResThreads, 1) resident_kernel(const __grid_c
         a.logits[static_cast<int64_t>(o) * a.V + pc.first + u] = s.res[o * 64 + u];
       }
     });
+    stamp(a, 9 * a.L + 1);
   }
   __syncthreads();
   // ---- the last CTA to finish advances the launch generation and clears the abort flag

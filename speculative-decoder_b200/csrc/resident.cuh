@@ -57,6 +57,11 @@ struct ResArgs {
   uint8_t* region;        // kResRegionBytes of the workspace (zeroed once by the caller)
   int32_t* status;
   long long wait_limit;   // clock cycles a packet wait may spin before it gives up
+  // Optional phase record (globaltimer ns): stamp j of CTA c at trace[j * grid + c]; per layer
+  // l the stamps 9 l .. 9 l + 8 (input read, q/k/v published, attention items done, attention
+  // gathered, o published, MLP input normalised, gate/up published, activation read, down
+  // published), then 9 L (final rows read), 9 L + 1 (head done), 9 L + 2 (kernel entry).
+  unsigned long long* trace;
   ResPlan p;
 };
 
