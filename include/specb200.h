@@ -78,7 +78,7 @@ int specb200_accept(const float* p, const float* q, const int64_t* draft, const 
  * arguments and results, minus the workspace. For callers that cannot allocate device memory
  * or hold a scratch buffer for this library (a runtime that reserves all HBM up front and
  * forbids later cudaMalloc, or an operator interface that passes only inputs and outputs).
- * Its scratch is a fixed device array inside the library (about 250 KB per GPU, held until
+ * Its scratch is a fixed device array inside the library (about 600 KB per GPU, held until
  * exit), so B is limited to specb200_accept_noalloc_max_rows() (512) and k to 15; larger
  * calls return SPECB200_ERR_ARG. The first call on each device looks up the array's device
  * address with that device current: make it before any stream capture. Every call shares the

@@ -10,18 +10,26 @@
 //   spec/accept.py:29-35        sample_inverse_cdf(): first index whose cdf exceeds u * total,
 //                               clamped to V - 1
 //
-// Two launches, chained with programmatic dependent launch:
-//   accept_kernel, grid R x B of 256 threads (one wave of 4 CTAs per SM at config 3): one CTA
-//     per input row (R = k+1 target rows, plus k draft rows when q is a real tensor) streams
-//     its row once from HBM (128-bit loads) and leaves per-row statistics (max and sum of exp
-//     for the softmax, the value at the drafted token, the argmax) in the workspace. The last
-//     CTA of batch row b (atomic ticket, no spin-wait) makes the accept decisions: n, and for
-//     greedy rows the next token.
-//   residual_kernel (sampling only), grid C x B: chunk c of the residual row max(0, p_n - q_n)
-//     of sequence b, re-read from L2, summed in double; the last chunk CTA of b scans the chunk
-//     sums in order and then the elements of the chunk holding the crossing. Splitting the
-//     residual pass over C CTAs per sequence keeps its exp/sum work off one SM.
-// Decisions therefore cost one HBM pass over p and q.
+// One persistent launch (a few CTAs per SM) that takes work units from a queue in the order
+// the CTAs ask for them (an atomic counter, so a unit is only ever waited on by units taken
+// after it, whichever CTAs are resident):
+//   statistics units (sequence-major): a column chunk of one input row (R = k+1 target rows,
+//     plus k draft rows when q is a real tensor) streamed once from HBM with 128-bit loads,
+//     leaving the chunk's softmax statistics (max and sum of exp), its argmax and, in the
+//     chunk holding the drafted token, the value there. The last chunk of a row (ticket)
+//     combines them; the last row of a sequence (ticket) makes the accept decisions: n, and
+//     for greedy rows the next token. Sampling rows then raise the sequence's ready flag.
+//   residual units (sampling only, after every statistics unit): chunk c of the residual row
+//     max(0, p_n - q_n) of sequence b -- it waits (bounded) for the sequence's ready flag,
+//     re-reads its chunk of the two rows from L2 and sums the residual and p in double. The
+//     last chunk of b (ticket) scans the chunk sums in order and then the elements of the
+//     chunk holding the crossing.
+// Sequences finish in queue order, so the residual passes of early sequences overlap the
+// statistics of later ones. Tickets, flags and the queue return to zero by the end of every
+// call (the last CTA clears the queue and the flags), so the workspace needs no clearing
+// between calls. Decisions therefore cost one HBM pass over p and q.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -30,6 +38,7 @@ namespace {
 
 constexpr int kAcceptThreads = 256;
 constexpr int kAcceptWarps = kAcceptThreads / 32;
+constexpr int kAcceptCtasPerSm = 4;
 
 struct RowStat {
   float m;     // max of z = x / T (logit rows)
@@ -50,51 +59,68 @@ struct AcceptArgs {
   int64_t* n_accepted;
   int64_t* next_token;
   int32_t* status;
-  int* counters;   // [2B]: statistics tickets, then residual tickets
-  RowStat* stats;  // [B, R]
-  int* nsel;       // [B] accepted length n (the residual row)
-  double* chunk_sums;  // [B, C]
-  int C, chunk;        // residual chunks per sequence and their length (a multiple of 4 * kAcceptThreads)
-  // Statistics of a row in nrc column chunks of rclen elements (few rows: small batches and the
-  // draft sampler), combined in chunk order by the row's last CTA (ticket in rcounters).
-  int nrc, rclen;
-  RowStat* cstats;  // [B, R, nrc]
-  int* rcounters;   // [B, R]
+  int* ctl;            // [0] unit queue, [1] CTAs finished
+  int* row_tickets;    // [B, R]: chunks of the row done
+  int* seq_tickets;    // [B]: rows of the sequence done
+  int* res_tickets;    // [B]: residual chunks of the sequence done
+  int* ready;          // [B]: decisions made (sampling rows)
+  RowStat* stats;      // [B, R]
+  RowStat* cstats;     // [B, R, nrc]: chunk statistics of chunked rows
+  int* nsel;           // [B] accepted length n (the residual row)
+  double* chunk_sums;  // [B, C, 2]: residual and p sums of each residual chunk
+  int nrc, rclen;      // statistics chunks per row and their length (a multiple of 4)
+  int C, chunk;        // residual chunks per sequence and their length (a multiple of 1024)
+  int units_stat, units_total;
 };
+
+// Statistics chunks: about 8192 elements (32 KB: one batch of eight 128-bit loads per thread),
+// shorter when rows are few so that the queue still holds about two units per SM, longer when
+// the partials would not fit their region.
+constexpr int kStatChunkMax = 8192;
+constexpr int kStatChunkMin = 2048;
+constexpr int kMaxStatParts = 8192;
+inline void stat_chunks(int rows, int V, bool logits, int* nrc, int* len) {
+  if (!logits) {  // probability rows: one load at the drafted token
+    *nrc = 1;
+    *len = V;
+    return;
+  }
+  long long want = (static_cast<long long>(V) * rows + 295) / 296;
+  want = (want + 1023) / 1024 * 1024;
+  int l = static_cast<int>(want < kStatChunkMin ? kStatChunkMin : (want > kStatChunkMax ? kStatChunkMax : want));
+  int n = (V + l - 1) / l;
+  if (static_cast<long long>(n) * rows > kMaxStatParts) n = kMaxStatParts / rows > 1 ? kMaxStatParts / rows : 1;
+  l = ((V + n - 1) / n + 3) / 4 * 4;
+  *nrc = (V + l - 1) / l;
+  *len = l;
+}
+// Residual chunks: at most 16 per sequence, at least 4096 elements (16 per thread).
+constexpr int kResChunks = 16;
+inline void residual_chunks(int V, int* C, int* len) {
+  int c = (V + 4095) / 4096;
+  c = c < kResChunks ? c : kResChunks;
+  *len = ((V + c - 1) / c + 1023) / 1024 * 1024;
+  *C = (V + *len - 1) / *len;
+}
 
 // Workspace carve, shared by the caller-workspace and the allocation-free entry points.
 struct AcceptLayout {
-  size_t counters, stats, nsel, sums, cstats, total;
+  size_t ctl, row_tickets, seq_tickets, res_tickets, ready, stats, cstats, nsel, sums, total;
 };
-// Statistics CTAs aimed for when rows are few (one wave at 4 per SM); rows are split into at
-// most kMaxRowChunks column chunks of at least kMinRowChunk elements.
-constexpr int kStatCtas = 4 * 148;
-constexpr int kMinRowChunk = 2048;
-constexpr int kMaxRowChunks = 64;
-inline int row_chunks(int rows, int V, bool logits) {
-  if (!logits || 2 * rows >= kStatCtas) return 1;
-  int n = kStatCtas / rows;
-  const int by_len = V / kMinRowChunk;
-  n = n < by_len ? n : by_len;
-  n = n < kMaxRowChunks ? n : kMaxRowChunks;
-  return n < 1 ? 1 : n;
-}
-constexpr int residual_chunks(int V) {
-  const int per = 4 * kAcceptThreads;
-  const int blocks = (V + per - 1) / per;
-  return blocks < 16 ? blocks : 16;
-}
-constexpr AcceptLayout accept_layout(int B, int k, int V) {
+constexpr AcceptLayout accept_layout(int B, int k) {
   auto al = [](size_t x) { return (x + 255) / 256 * 256; };
   const size_t R = 2 * static_cast<size_t>(k) + 1;
   AcceptLayout l{};
-  // sequence tickets [2B], then the row tickets [B R] of chunked rows (B R < kStatCtas / 2)
-  l.counters = 256;
-  l.stats = l.counters + al((2 * static_cast<size_t>(B) + kStatCtas / 2) * sizeof(int));
-  l.nsel = l.stats + al(static_cast<size_t>(B) * R * sizeof(RowStat));
+  l.ctl = 0;
+  l.row_tickets = 256;
+  l.seq_tickets = l.row_tickets + al(static_cast<size_t>(B) * R * sizeof(int));
+  l.res_tickets = l.seq_tickets + al(static_cast<size_t>(B) * sizeof(int));
+  l.ready = l.res_tickets + al(static_cast<size_t>(B) * sizeof(int));
+  l.stats = l.ready + al(static_cast<size_t>(B) * sizeof(int));
+  l.cstats = l.stats + al(static_cast<size_t>(B) * R * sizeof(RowStat));
+  l.nsel = l.cstats + al(static_cast<size_t>(kMaxStatParts) * sizeof(RowStat));
   l.sums = l.nsel + al(static_cast<size_t>(B) * sizeof(int));
-  l.cstats = l.sums + al(static_cast<size_t>(B) * residual_chunks(V) * sizeof(double));
-  l.total = l.cstats + al(static_cast<size_t>(kStatCtas) * sizeof(RowStat));  // B R nrc <= kStatCtas
+  l.total = l.sums + al(static_cast<size_t>(B) * kResChunks * 2 * sizeof(double));
   return l;
 }
 
@@ -114,10 +140,10 @@ SPECB200_DEVINL void combine_ms(float& m, float& s, float m2, float s2) {
   m = mx;
 }
 
-// Statistics of row r of sequence b over columns [x0, x1) (x0 % 4 == 0; the whole row when
-// the row is not chunked); thread 0 writes them to *out. With `finish`, also the value at the
-// drafted token (only the CTA that sees the whole row, or the row's combining CTA, needs it).
-__device__ void row_statistics(const AcceptArgs& a, int b, int r, int x0, int x1, bool finish, RowStat* out) {
+// Statistics of row r of sequence b over columns [x0, x1) (x0 % 4 == 0); thread 0 writes them
+// to *out: max and sum of exp of z = x / T, the first argmax (greedy rows), and z at the
+// drafted token when it lies in [x0, x1). Every thread of the CTA calls it.
+__device__ void chunk_statistics(const AcceptArgs& a, int b, int r, int x0, int x1, RowStat* out) {
   __shared__ float sh_m[kAcceptWarps], sh_s[kAcceptWarps];
   __shared__ int sh_i[kAcceptWarps];
   const float* row = row_ptr(a, b, r);
@@ -129,7 +155,7 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, int x0, int x1
   if (!a.logits) {  // probability rows: only the value at the drafted token is needed
     if (tid == 0) {
       RowStat st{0.f, 1.f, 0.f, 0};
-      if (d >= 0 && d < a.V) st.zx = row[d];
+      if (d >= x0 && d < x1) st.zx = row[d];
       *out = st;
     }
     return;
@@ -162,7 +188,7 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, int x0, int x1
     __syncthreads();
     if (tid == 0) {
       for (int w = 1; w < kAcceptWarps; ++w) argmax_merge(best, bi, sh_m[w], sh_i[w]);
-      RowStat st{best, 1.f, 0.f, (bi == 0x7fffffff && finish) ? 0 : bi};  // chunk partials keep "none"
+      RowStat st{best, 1.f, 0.f, bi};  // 0x7fffffff: nothing seen (the combine turns it into 0)
       *out = st;
     }
     return;
@@ -222,16 +248,9 @@ __device__ void row_statistics(const AcceptArgs& a, int b, int r, int x0, int x1
   if (tid == 0) {
     for (int w = 1; w < kAcceptWarps; ++w) combine_ms(m, s, sh_m[w], sh_s[w]);
     RowStat st{m, s, 0.f, 0};
-    if (finish && d >= 0 && d < a.V) st.zx = row[d] / T;
+    if (d >= x0 && d < x1) st.zx = row[d] / T;
     *out = st;
   }
-}
-
-// Probability of token x in target row pr (or draft row qr) for the finishing CTA.
-SPECB200_DEVINL float prob_at(const AcceptArgs& a, const float* row, const RowStat& st, float inv_s, int x) {
-  float v = row[x];
-  if (!a.logits) return v;
-  return expf(v / a.temperature - st.m) * inv_s;
 }
 
 // Residual sampling at row n: r = max(0, p_n - q_n); sample by inverse CDF with u.
@@ -311,31 +330,70 @@ __device__ ResidualRow residual_row(const AcceptArgs& a, int b, int n) {
   return r;
 }
 
-// Double sum of the residual (or of p when use_p) over [x0, x1), x0 % 4 == 0; block-wide.
-// Groups of 4 elements go to threads round-robin, four groups per thread per batch so that
-// their loads are in flight together.
-__device__ double residual_block_sum(const AcceptArgs& a, const ResidualRow& r, int use_p, int x0, int x1) {
-  __shared__ double sh_part[kAcceptWarps];
+// Double sums over [x0, x1) (x0 % 4 == 0), block-wide, of the residual max(0, p - q) and of p
+// (the fallback when the residual sums to zero), in one pass with the arithmetic of
+// seg_values. Groups of 4 elements go to threads round-robin, the loads of four groups per
+// thread in flight together; warp totals are added in warp order.
+__device__ void residual_block_sums(const AcceptArgs& a, const ResidualRow& r, int x0, int x1, double& res,
+                                    double& pr) {
+  __shared__ double sh_part[2][kAcceptWarps];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  double acc = 0.0;
+  const bool vec = (a.V % 4 == 0);
+  double acc = 0.0, accp = 0.0;
   for (int xb = x0; xb < x1; xb += 16 * kAcceptThreads) {
-    float v[4][4];
+    float4 pv[4], qv[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const int x = xb + 4 * (tid + i * kAcceptThreads);
-      v[i][0] = v[i][1] = v[i][2] = v[i][3] = 0.f;
-      if (x < x1) seg_values(a, r.prow, r.ps, r.p_inv, r.qrow, r.qs, r.q_inv, r.q_row, r.q_hot, r.dn, use_p, x, v[i]);
+      pv[i] = qv[i] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      if (x < x1 && vec && x + 3 < a.V) {
+        pv[i] = *reinterpret_cast<const float4*>(r.prow + x);
+        if (r.q_row) qv[i] = *reinterpret_cast<const float4*>(r.qrow + x);
+      } else if (x < x1) {
+        float* pp = &pv[i].x;
+        float* qq = &qv[i].x;
+        for (int j = 0; j < 4 && x + j < x1; ++j) {
+          pp[j] = r.prow[x + j];
+          if (r.q_row) qq[j] = r.qrow[x + j];
+        }
+      }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc += static_cast<double>(v[i][0]) + v[i][1] + v[i][2] + v[i][3];
+    for (int i = 0; i < 4; ++i) {
+      const int x = xb + 4 * (tid + i * kAcceptThreads);
+      const float* pp = &pv[i].x;
+      const float* qq = &qv[i].x;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (x + j >= x1) continue;
+        float px = pp[j];
+        if (a.logits) px = __expf((a.temperature == 1.f ? px : px / a.temperature) - r.ps.m) * r.p_inv;
+        float qx = 0.f;
+        if (r.q_row) {
+          qx = qq[j];
+          if (a.logits) qx = __expf((a.temperature == 1.f ? qx : qx / a.temperature) - r.qs.m) * r.q_inv;
+        } else if (r.q_hot) {
+          qx = (x + j == r.dn) ? 1.f : 0.f;
+        }
+        acc += static_cast<double>(fmaxf(px - qx, 0.f));  // torch.clamp(p - q, min=0)
+        accp += static_cast<double>(px);
+      }
+    }
   }
   acc = warp_sum_d(acc);
-  if (lane == 0) sh_part[warp] = acc;
+  accp = warp_sum_d(accp);
+  if (lane == 0) {
+    sh_part[0][warp] = acc;
+    sh_part[1][warp] = accp;
+  }
   __syncthreads();
-  double tot = 0.0;
-  for (int w = 0; w < kAcceptWarps; ++w) tot += sh_part[w];  // fixed order
+  res = 0.0;
+  pr = 0.0;
+  for (int w = 0; w < kAcceptWarps; ++w) {  // fixed order
+    res += sh_part[0][w];
+    pr += sh_part[1][w];
+  }
   __syncthreads();
-  return tot;
 }
 
 // First index x in [x0, x1) (x0 % 4 == 0) where base + cumsum passes target, or -1; base is the
@@ -413,62 +471,33 @@ __device__ int residual_block_find(const AcceptArgs& a, const ResidualRow& r, in
   return hit == 0x7fffffff ? -1 : hit;
 }
 
-// Grid C * B (1-D, b-major): chunk sums of the residual row; the last chunk CTA of b draws
-// the sample.
-__global__ void __launch_bounds__(kAcceptThreads) residual_kernel(AcceptArgs a) {
-  pdl_wait();
-  const int c = blockIdx.x % a.C, b = blockIdx.x / a.C, tid = threadIdx.x;
-  __shared__ int sh_last;
-  const int n = __ldcg(a.nsel + b);
-  const ResidualRow r = residual_row(a, b, n);
-  const int x0 = c * a.chunk, x1 = min(a.V, x0 + a.chunk);
-  const double part = residual_block_sum(a, r, 0, x0, x1);
-  double* sums = a.chunk_sums + static_cast<int64_t>(b) * a.C;
-  if (tid == 0) sums[c] = part;
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) sh_last = (atomicAdd(a.counters + a.B + b, 1) == a.C - 1);
-  __syncthreads();
-  if (!sh_last) return;
-  __threadfence();
-  if (tid == 0) a.counters[a.B + b] = 0;  // ready for the next launch
-  double total = 0.0;
-  for (int i = 0; i < a.C; ++i) total += __ldcg(sums + i);  // chunk order
-  int use_p = 0;
-  if (!(total > 0.0)) {  // residual sums to 0: residual_distribution falls back to p
-    use_p = 1;
-    total = 0.0;
-    for (int i = 0; i < a.C; ++i) total += residual_block_sum(a, r, 1, i * a.chunk, min(a.V, (i + 1) * a.chunk));
-  }
-  const double target = static_cast<double>(a.u_residual[b]) * total;
-  // the chunk whose running sum passes the target, then its elements (later chunks too, if
-  // rounding put the crossing past the chunk's end); past the end: V - 1 (searchsorted, clamped)
-  double base = 0.0;
-  int first = a.C;
-  for (int i = 0; i < a.C; ++i) {
-    const double si = use_p ? residual_block_sum(a, r, 1, i * a.chunk, min(a.V, (i + 1) * a.chunk)) : __ldcg(sums + i);
-    if (base + si > target) {
-      first = i;
-      break;
+SPECB200_DEVINL int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+SPECB200_DEVINL void st_release(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Bounded wait for a flag another CTA raises (set while it runs a unit taken from the queue
+// earlier): false, with SPECB200_ERR_TIMEOUT in the status word, once the limit ran out.
+SPECB200_DEVINL bool wait_flag(const int* flag, int32_t* status) {
+  if (ld_acquire(flag)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    __nanosleep(32);
+    if (ld_acquire(flag)) return true;
+    if (clock64() - t0 > SPECB200_SPIN_LIMIT_CYCLES) {
+      set_status(status, SPECB200_ERR_TIMEOUT);
+      return false;
     }
-    base += si;
   }
-  int64_t tok = a.V - 1;
-  for (int i = first; i < a.C; ++i) {
-    const int lo = i * a.chunk, hi = min(a.V, lo + a.chunk);
-    const int x = residual_block_find(a, r, use_p, lo, hi, base, target);
-    if (x >= 0) {
-      tok = x;
-      break;
-    }
-    base += use_p ? residual_block_sum(a, r, 1, lo, hi) : __ldcg(sums + i);
-  }
-  if (tid == 0) a.next_token[b] = tok;
 }
 
 // Decisions for sequence b once all its row statistics are in the workspace (the caller is
-// the last CTA of b): n accepted drafts, then the greedy next token. All threads of the CTA
-// call it.
+// the CTA that finished its last row): n accepted drafts, then the greedy next token, or the
+// ready flag that lets the residual units of b start. All threads of the CTA call it.
 __device__ void decide(const AcceptArgs& a, int b) {
   __shared__ RowStat sst[32];
   __shared__ int64_t sdraft[16];
@@ -490,7 +519,7 @@ __device__ void decide(const AcceptArgs& a, int b) {
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    a.counters[b] = 0;  // ready for the next launch
+    a.seq_tickets[b] = 0;  // ready for the next call
     int n = 0;
     bool run = true;
     for (int i = 0; i < a.k; ++i) {
@@ -517,44 +546,41 @@ __device__ void decide(const AcceptArgs& a, int b) {
     a.n_accepted[b] = n;
     a.nsel[b] = n;
     if (a.greedy && !a.decide_only) a.next_token[b] = sst[n].amax;
+    if (!a.greedy && !a.decide_only) {
+      __threadfence();
+      st_release(a.ready + b, 1);
+    }
   }
   __syncthreads();
 }
 
-__global__ void __launch_bounds__(kAcceptThreads, 4) accept_kernel(AcceptArgs a) {
-  pdl_wait();
-  pdl_launch_dependents();  // the residual kernel may start its prologue; it waits for this grid
-  // b-major, then row, then column chunk: a sequence's CTAs run together
-  const int c = blockIdx.x % a.nrc, rb = blockIdx.x / a.nrc;
+// Statistics unit u: chunk c of row r of sequence b. The row's last chunk combines the
+// chunks (warp 0: chunk order within each lane, then a fixed xor tree); the sequence's last
+// row decides.
+__device__ void stat_unit(const AcceptArgs& a, int u) {
+  __shared__ int sh_last;
+  const int c = u % a.nrc, rb = u / a.nrc;
   const int r = rb % a.R, b = rb / a.R;
   RowStat* st = a.stats + static_cast<int64_t>(b) * a.R;
-  __shared__ int sh_last;
   if (a.nrc == 1) {
-    row_statistics(a, b, r, 0, a.V, true, st + r);
+    chunk_statistics(a, b, r, 0, a.V, st + r);
   } else {
-    // this chunk's partial, then the row's last CTA combines the chunks in column order
     RowStat* part = a.cstats + static_cast<int64_t>(rb) * a.nrc;
-    row_statistics(a, b, r, c * a.rclen, min(a.V, (c + 1) * a.rclen), false, part + c);
+    chunk_statistics(a, b, r, c * a.rclen, min(a.V, (c + 1) * a.rclen), part + c);
     __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) sh_last = (atomicAdd(a.rcounters + rb, 1) == a.nrc - 1);
+    if (threadIdx.x == 0) sh_last = (atomicAdd(a.row_tickets + rb, 1) == a.nrc - 1);
     __syncthreads();
     if (!sh_last) return;
     __threadfence();
-    RowStat t{-INFINITY, 0.f, 0.f, 0x7fffffff};
     if (threadIdx.x < 32) {
-      // warp 0 combines the chunk partials: lane l folds chunks l, l + 32 (their loads in
-      // flight together), then a fixed xor tree across lanes (deterministic order)
       const int lane = threadIdx.x;
-#pragma unroll
-      for (int q = 0; q < kMaxRowChunks / 32; ++q) {
-        const int j = lane + 32 * q;
-        if (j < a.nrc) {
-          const float m2 = __ldcg(&part[j].m), s2 = __ldcg(&part[j].s);
-          const int i2 = __ldcg(&part[j].amax);
-          if (a.greedy) argmax_merge(t.m, t.amax, m2, i2);
-          else combine_ms(t.m, t.s, m2, s2);
-        }
+      RowStat t{-INFINITY, 0.f, 0.f, 0x7fffffff};
+      for (int j = lane; j < a.nrc; j += 32) {
+        const float m2 = __ldcg(&part[j].m), s2 = __ldcg(&part[j].s);
+        const int i2 = __ldcg(&part[j].amax);
+        if (a.greedy) argmax_merge(t.m, t.amax, m2, i2);
+        else combine_ms(t.m, t.s, m2, s2);
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) {
@@ -563,27 +589,126 @@ __global__ void __launch_bounds__(kAcceptThreads, 4) accept_kernel(AcceptArgs a)
         if (a.greedy) argmax_merge(t.m, t.amax, m2, i2);
         else combine_ms(t.m, t.s, m2, s2);
       }
-    }
-    if (threadIdx.x == 0) {
-      if (a.greedy) {
-        t.s = 1.f;
-        t.amax = t.amax == 0x7fffffff ? 0 : t.amax;
-      } else {
-        const int i = r <= a.k ? r : r - a.k - 1;
-        const int64_t d = i < a.k ? a.draft[static_cast<int64_t>(b) * a.k + i] : -1;
-        if (d >= 0 && d < a.V) t.zx = row_ptr(a, b, r)[d] / a.temperature;
+      if (lane == 0) {
+        if (a.greedy) {
+          t.s = 1.f;
+          t.amax = t.amax == 0x7fffffff ? 0 : t.amax;
+        } else {
+          const int i = r <= a.k ? r : r - a.k - 1;
+          const int64_t d = i < a.k ? a.draft[static_cast<int64_t>(b) * a.k + i] : -1;
+          if (d >= 0 && d < a.V) t.zx = __ldcg(&part[d / a.rclen].zx);
+        }
+        st[r] = t;
+        a.row_tickets[rb] = 0;
       }
-      st[r] = t;
-      a.rcounters[rb] = 0;
     }
   }
   __threadfence();
   __syncthreads();
-  if (threadIdx.x == 0) sh_last = (atomicAdd(a.counters + b, 1) == a.R - 1);
+  if (threadIdx.x == 0) sh_last = (atomicAdd(a.seq_tickets + b, 1) == a.R - 1);
   __syncthreads();
   if (!sh_last) return;
   __threadfence();
   decide(a, b);
+}
+
+// Residual unit v: chunk c of the residual row of sequence b (after b's decisions). The last
+// chunk of b draws the sample: the residual total (chunk order; p when it is zero) times u,
+// the first chunk whose running sum passes it, then that chunk's elements (later chunks too,
+// if rounding put the crossing past the chunk's end); past the end: V - 1 (searchsorted,
+// clamped).
+__device__ void residual_unit(const AcceptArgs& a, int v) {
+  __shared__ int sh_ok, sh_last;
+  const int b = v / a.C, c = v % a.C, tid = threadIdx.x;
+  if (tid == 0) sh_ok = wait_flag(a.ready + b, a.status) ? 1 : 0;
+  __syncthreads();
+  const bool ok = sh_ok;
+  double* sums = a.chunk_sums + static_cast<int64_t>(b) * a.C * 2;
+  ResidualRow r{};
+  if (ok) {
+    r = residual_row(a, b, __ldcg(a.nsel + b));
+    double sr, sp;
+    residual_block_sums(a, r, c * a.chunk, min(a.V, (c + 1) * a.chunk), sr, sp);
+    if (tid == 0) {
+      sums[2 * c] = sr;
+      sums[2 * c + 1] = sp;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) sh_last = (atomicAdd(a.res_tickets + b, 1) == a.C - 1);
+  __syncthreads();
+  if (!sh_last) return;
+  __threadfence();
+  if (tid == 0) a.res_tickets[b] = 0;  // ready for the next call
+  if (!ok) {
+    if (tid == 0) a.next_token[b] = a.V - 1;
+    return;
+  }
+  double total = 0.0;
+  for (int i = 0; i < a.C; ++i) total += __ldcg(sums + 2 * i);  // chunk order
+  int use_p = 0;
+  if (!(total > 0.0)) {  // residual sums to 0: residual_distribution falls back to p
+    use_p = 1;
+    total = 0.0;
+    for (int i = 0; i < a.C; ++i) total += __ldcg(sums + 2 * i + 1);
+  }
+  const double target = static_cast<double>(a.u_residual[b]) * total;
+  double base = 0.0;
+  int first = a.C;
+  for (int i = 0; i < a.C; ++i) {
+    const double si = __ldcg(sums + 2 * i + use_p);
+    if (base + si > target) {
+      first = i;
+      break;
+    }
+    base += si;
+  }
+  int64_t tok = a.V - 1;
+  for (int i = first; i < a.C; ++i) {
+    const int lo = i * a.chunk, hi = min(a.V, lo + a.chunk);
+    const int x = residual_block_find(a, r, use_p, lo, hi, base, target);
+    if (x >= 0) {
+      tok = x;
+      break;
+    }
+    base += __ldcg(sums + 2 * i + use_p);
+  }
+  if (tid == 0) a.next_token[b] = tok;
+}
+
+// Persistent CTAs: take units from the queue until it is empty; the next unit's number is
+// fetched while the current one runs. The last CTA to finish clears the queue and the flags.
+__global__ void __launch_bounds__(kAcceptThreads, kAcceptCtasPerSm) accept_kernel(AcceptArgs a) {
+  __shared__ int sh_unit, sh_end;
+  pdl_wait();
+  pdl_launch_dependents();
+  const int tid = threadIdx.x;
+  if (tid == 0) sh_unit = atomicAdd(a.ctl, 1);
+  __syncthreads();
+  int u = sh_unit;
+  while (u < a.units_total) {
+    int nxt = 0;
+    if (tid == 0) nxt = atomicAdd(a.ctl, 1);
+    if (u < a.units_stat) stat_unit(a, u);
+    else residual_unit(a, u - a.units_stat);
+    __syncthreads();
+    if (tid == 0) sh_unit = nxt;
+    __syncthreads();
+    u = sh_unit;
+  }
+  if (tid == 0) {
+    __threadfence();
+    sh_end = (atomicAdd(a.ctl + 1, 1) == static_cast<int>(gridDim.x) - 1);
+  }
+  __syncthreads();
+  if (sh_end) {
+    for (int b = tid; b < a.B; b += kAcceptThreads) a.ready[b] = 0;
+    if (tid == 0) {
+      a.ctl[0] = 0;
+      a.ctl[1] = 0;
+    }
+  }
 }
 
 // probabilities() of lm/sampling.py:13-18, materialised: one-hot of the first maximum at
@@ -646,39 +771,51 @@ using namespace specb200;
 
 namespace specb200 {
 namespace {
-// Both kernels on `s`: the counters are cleared first (a call with another B may have left
-// statistics where they sit); the residual kernel follows with programmatic dependent launch.
-// Returns the first CUDA error met (memsets or launches), cudaSuccess otherwise.
+int g_sm_count[64] = {};
+
+// Streaming multiprocessors of the current device (looked up once per device).
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  int n = __atomic_load_n(&g_sm_count[dev], __ATOMIC_RELAXED);
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    __atomic_store_n(&g_sm_count[dev], n, __ATOMIC_RELAXED);
+  }
+  return n;
+}
+
+// One launch on `s` (after clearing the caller's status word). The workspace's tickets,
+// flags and queue are zero on entry and on exit. Returns the first CUDA error met.
 cudaError_t launch_accept(AcceptArgs& a, char* ws, const AcceptLayout& l, cudaStream_t s) {
-  a.counters = reinterpret_cast<int*>(ws + l.counters);
+  a.ctl = reinterpret_cast<int*>(ws + l.ctl);
+  a.row_tickets = reinterpret_cast<int*>(ws + l.row_tickets);
+  a.seq_tickets = reinterpret_cast<int*>(ws + l.seq_tickets);
+  a.res_tickets = reinterpret_cast<int*>(ws + l.res_tickets);
+  a.ready = reinterpret_cast<int*>(ws + l.ready);
   a.stats = reinterpret_cast<RowStat*>(ws + l.stats);
+  a.cstats = reinterpret_cast<RowStat*>(ws + l.cstats);
   a.nsel = reinterpret_cast<int*>(ws + l.nsel);
   a.chunk_sums = reinterpret_cast<double*>(ws + l.sums);
-  a.C = residual_chunks(a.V);
-  const int per = 4 * kAcceptThreads;
-  a.chunk = ((a.V + a.C - 1) / a.C + per - 1) / per * per;
-  a.nrc = row_chunks(a.B * a.R, a.V, a.logits != 0);
-  a.rclen = ((a.V + a.nrc - 1) / a.nrc + 3) / 4 * 4;
-  a.rcounters = a.counters + 2 * a.B;
-  a.cstats = reinterpret_cast<RowStat*>(ws + l.cstats);
+  stat_chunks(a.B * a.R, a.V, a.logits != 0, &a.nrc, &a.rclen);
+  residual_chunks(a.V, &a.C, &a.chunk);
+  const bool sampling = !a.greedy && !a.decide_only;
+  a.units_stat = a.B * a.R * a.nrc;
+  a.units_total = a.units_stat + (sampling ? a.B * a.C : 0);
+  const int ctas = std::min(a.units_total, kAcceptCtasPerSm * sm_count());
   cudaError_t e = cudaSuccess;
   if (a.status) e = cudaMemsetAsync(a.status, 0, sizeof(int32_t), s);
   if (e != cudaSuccess) return e;
-  e = cudaMemsetAsync(a.counters, 0,
-                      (2 * static_cast<size_t>(a.B) + (a.nrc > 1 ? static_cast<size_t>(a.B) * a.R : 0)) * sizeof(int), s);
-  if (e != cudaSuccess) return e;
-  accept_kernel<<<static_cast<unsigned>(a.R) * a.B * a.nrc, kAcceptThreads, 0, s>>>(a);
-  e = cudaGetLastError();
-  if (e == cudaSuccess && !a.greedy && !a.decide_only)
-    e = launch_kernel(residual_kernel, dim3(static_cast<unsigned>(a.C) * a.B), dim3(kAcceptThreads), 0, s, true, a);
-  return e;
+  accept_kernel<<<ctas, kAcceptThreads, 0, s>>>(a);
+  return cudaGetLastError();
 }
 }  // namespace
 }  // namespace specb200
 
-// Workspace for the largest V the kernels accept (the residual chunk sums depend on V).
+// Workspace of a call with B sequences and k drafts (any V the kernel accepts).
 extern "C" size_t specb200_accept_workspace_bytes(int B, int k) {
-  return accept_layout(B, k, kMaxSegs * kSeg).total;
+  if (B <= 0 || k < 0) return 0;
+  return accept_layout(B, k).total;
 }
 
 extern "C" int specb200_set_error(int code, const char* msg);
@@ -716,7 +853,7 @@ extern "C" int specb200_accept(const float* p, const float* q, const int64_t* dr
   a.n_accepted = n_accepted;
   a.next_token = next_token;
   a.status = status;
-  const AcceptLayout l = accept_layout(B, k, V);
+  const AcceptLayout l = accept_layout(B, k);
   if (l.total > workspace_bytes) return specb200_set_error(SPECB200_ERR_WORKSPACE, "accept: workspace too small");
   const cudaError_t e = launch_accept(a, static_cast<char*>(workspace), l, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
@@ -738,25 +875,27 @@ extern "C" int specb200_probabilities(const float* logits, int rows, int V, floa
 // Some callers cannot hand this library a workspace: a serving runtime that reserves all of
 // HBM for weights and KV pages at start-up and treats any later cudaMalloc as an error, or a
 // plugin host whose operator interface passes only input and output buffers. For them the
-// accept kernel's scratch (one ticket counter per row and the per-row statistics) lives in
-// g_accept_scratch, a file-scope device array of fixed size that every GPU loading this
-// library holds until the process exits. Limits: B <= kNoAllocMaxB rows and k <= 15.
+// accept kernel's scratch (the work queue, tickets and flags, the per-row statistics and the
+// residual chunk sums) lives in g_accept_scratch, a file-scope device array of fixed size
+// (about 600 KB) that every GPU loading this library holds until the process exits. Limits:
+// B <= kNoAllocMaxB rows and k <= 15.
 //
 // Host code cannot use g_accept_scratch as an address (on the host the name is only a
 // stand-in for the device symbol), so the first call on each device, with that device
 // current, looks the address up with cudaGetSymbolAddress and caches it; make that first call
 // before any stream capture. All calls share the array and it keeps the last call's contents:
-// the counters that must start at zero are cleared by every call, and two calls that overlap
-// on the GPU (different streams, or different host threads) race on it.
+// the queue, tickets and flags that must start at zero are zero when the library is loaded
+// and every call leaves them at zero when its kernel ends, and two calls that overlap on the
+// GPU (different streams, or different host threads) race on it.
 // ---------------------------------------------------------------------------------------
 #include <mutex>
 
 namespace {
 constexpr int kNoAllocMaxB = 512;
 constexpr int kNoAllocMaxK = 15;
-// accept_layout(kNoAllocMaxB, kNoAllocMaxK, V) for the largest V: tickets, statistics, the
-// accepted lengths, 16 residual chunk sums per row and the chunked-row partials (~342 KB)
-constexpr size_t kNoAllocScratchBytes = accept_layout(kNoAllocMaxB, kNoAllocMaxK, kMaxSegs * kSeg).total;
+// accept_layout(kNoAllocMaxB, kNoAllocMaxK): queue, tickets, flags, statistics, the chunked-row
+// partials, the accepted lengths and 16 residual chunk sums per row (~575 KB)
+constexpr size_t kNoAllocScratchBytes = accept_layout(kNoAllocMaxB, kNoAllocMaxK).total;
 
 static __device__ __align__(256) unsigned char g_accept_scratch[kNoAllocScratchBytes];
 
@@ -822,9 +961,9 @@ extern "C" int specb200_accept_noalloc(const float* p, const float* q, const int
   a.n_accepted = n_accepted;
   a.next_token = next_token;
   a.status = status;
-  const AcceptLayout l = accept_layout(B, k, V);
+  const AcceptLayout l = accept_layout(B, k);
   if (l.total > kNoAllocScratchBytes) return specb200_set_error(SPECB200_ERR_ARG, "accept_noalloc: scratch too small");
-  // the array keeps old tickets: launch_accept clears the counters first
+  // the array holds zero tickets and flags: every call leaves them so
   const cudaError_t e = launch_accept(a, static_cast<char*>(scratch), l, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
   return SPECB200_OK;
