@@ -202,9 +202,12 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
   float* attn_parts = reinterpret_cast<float*>(ws + cv.attn_parts);
   int32_t* status = bt.status;
 
-  CUtensorMap x_hidden{}, x_attn{}, x_act{}, x_final{};
+  // One token-operand map per GEMM shape: the box height is that GEMM's token tile, which
+  // the plan sizes per output width (q/k/v and gate/up both read xbuf, with their own tiles).
+  CUtensorMap x_hidden{}, x_mlp{}, x_attn{}, x_act{}, x_final{};
   if (tc) {
     bool ok = make_tmap_bf16_2d(&x_hidden, xbuf, c.hidden, M, kTileK, cv.g_qkv.BN) &&
+              make_tmap_bf16_2d(&x_mlp, xbuf, c.hidden, M, kTileK, cv.g_gu.BN) &&
               make_tmap_bf16_2d(&x_attn, attn, qd, M, kTileK, cv.g_o.BN) &&
               make_tmap_bf16_2d(&x_act, act, c.intermediate, M, kTileK, cv.g_down.BN) &&
               make_tmap_bf16_2d(&x_final, xbuf, c.hidden, rows_out, kTileK, cv.g_head.BN);
@@ -359,7 +362,7 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     eg.out = act;
     eg.ldo = c.intermediate;
     rc = cv.gemv ? gemv(cv.v_gu, L.w_gate_up, hidden, L.mlp_norm, eg, 2 * c.intermediate, c.hidden)
-                 : gemm(cv.g_gu, mp ? &mp->gu : nullptr, &x_hidden, L.w_gate_up, xbuf, eg);
+                 : gemm(cv.g_gu, mp ? &mp->gu : nullptr, &x_mlp, L.w_gate_up, xbuf, eg);
     if (rc) return rc;
     rc = cv.gemv ? gemv(cv.v_down, L.w_down, act, nullptr, er, c.hidden, c.intermediate)
                  : gemm(cv.g_down, mp ? &mp->down : nullptr, &x_act, L.w_down, act, cv.defer ? ep : er);

@@ -29,11 +29,14 @@
 // limit; a wait that gives up records SPECB200_ERR_TIMEOUT, raises the launch's abort flag and
 // every CTA then drains its copies in flight and leaves.
 #include <algorithm>
+#include <cstdio>
 #include <mutex>
 
 #include "attn_mma.cuh"
 #include "kernels.cuh"
 #include "resident.cuh"
+
+extern "C" int specb200_set_error(int code, const char* msg);
 
 namespace specb200 {
 namespace {
@@ -868,17 +871,33 @@ bool resident_prepare() {
   static std::once_flag once;
   static bool ok = false;
   std::call_once(once, [] {
-    int dev = 0;
-    ok = cudaGetDevice(&dev) == cudaSuccess &&
-         cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
-         cudaFuncSetAttribute(resident_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024) ==
-             cudaSuccess &&
-         cudaFuncSetAttribute(resident_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                              cudaSharedmemCarveoutMaxShared) == cudaSuccess;
-    int blocks = 0;
-    ok = ok && cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, resident_kernel, kResThreads, 200 * 1024) ==
-                   cudaSuccess &&
-         blocks >= 1;
+    int dev = 0, blocks = 0;
+    const char* step = "cudaGetDevice";
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e == cudaSuccess) {
+      step = "multiprocessor count";
+      e = cudaDeviceGetAttribute(&g_sms, cudaDevAttrMultiProcessorCount, dev);
+    }
+    if (e == cudaSuccess) {
+      step = "shared-memory limit";
+      e = cudaFuncSetAttribute(resident_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    }
+    if (e == cudaSuccess) {
+      step = "carveout";
+      e = cudaFuncSetAttribute(resident_kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                               cudaSharedmemCarveoutMaxShared);
+    }
+    if (e == cudaSuccess) {
+      step = "occupancy";
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, resident_kernel, kResThreads, 200 * 1024);
+    }
+    ok = e == cudaSuccess && blocks >= 1;
+    if (!ok) {
+      char msg[256];
+      std::snprintf(msg, sizeof(msg), "resident kernel unavailable (%s: %s, %d blocks per SM)", step,
+                    cudaGetErrorString(e), blocks);
+      specb200_set_error(SPECB200_ERR_CUDA, msg);
+    }
   });
   return ok;
 }
