@@ -696,6 +696,9 @@ def main() -> None:
     ap.add_argument("--config", type=int, choices=sorted(WORKLOADS), default=2,
                     help="BASELINE workload: 2 (default; 1.7B + 135M draft, B=1), 4 (32 requests per GPU, k=8, "
                          "T=0.8) or 5 (8k-token prompts, n-gram drafter)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="requests per GPU, overriding the workload's (e.g. --config 2 --batch 64 for the metric's "
+                         "@B64 point)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true",
                     help="config 2: skip the accept microbench, latency, plain-decode and noisy-draft lines")
@@ -713,7 +716,12 @@ def main() -> None:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
-    w = WORKLOADS[args.config]
+    w = dict(WORKLOADS[args.config])
+    if args.batch > 0 and args.batch != w["B"]:
+        w["B"] = args.batch
+        w["metric"] = w["metric"].replace("@B1 ", f"@B{args.batch} ").replace("@B32 ", f"@B{args.batch} ")
+        w["workload"] = w["workload"].replace("B=1 per GPU", f"B={args.batch} per GPU").replace(
+            "32 requests per GPU", f"{args.batch} requests per GPU")
     B = w["B"]
     config = {"workload": w["workload"], "global_batch": B * world, "seq_len": w["prompt"] + w["new"],
               "parallelism": f"requests sharded x{world}",
