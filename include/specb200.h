@@ -63,7 +63,10 @@ const char* specb200_last_error(void);
  * Outputs n_accepted [B] and next_token [B], int64. k = 0 samples one token per row from
  * p[:, 0] (the first-token / plain-decode sampler). With SPECB200_ACCEPT_DECIDE_ONLY only
  * n_accepted is written. status: device int32, set to a SPECB200_ERR_* code by the kernel
- * (zero draft mass, draft id out of range); the call clears it first. */
+ * (zero draft mass, draft id out of range); the call clears it first.
+ * workspace: specb200_accept_workspace_bytes(B, k) bytes, zero-filled before its first use
+ * (the kernel's work queue and tickets start at zero and every call leaves them at zero), and
+ * used by one call at a time. */
 #define SPECB200_ACCEPT_LOGITS 1
 #define SPECB200_ACCEPT_Q_ONEHOT 2
 #define SPECB200_ACCEPT_DECIDE_ONLY 4
