@@ -25,9 +25,11 @@
 //     last chunk of b (ticket) scans the chunk sums in order and then the elements of the
 //     chunk holding the crossing.
 // Sequences finish in queue order, so the residual passes of early sequences overlap the
-// statistics of later ones. Tickets, flags and the queue return to zero by the end of every
-// call (the last CTA clears the queue and the flags), so the workspace needs no clearing
-// between calls. Decisions therefore cost one HBM pass over p and q.
+// statistics of later ones. Every word a call writes into the workspace is back to zero when
+// its kernel ends (tickets by their last arriver, partial and row statistics, accepted lengths
+// and chunk sums once read, flags and the queue by the last CTA), so one zero-filled workspace
+// serves calls of any (B, k) with no clearing in between. Decisions therefore cost one HBM
+// pass over p and q.
 #include <algorithm>
 
 #include "common.cuh"
@@ -73,24 +75,22 @@ struct AcceptArgs {
   int units_stat, units_total;
 };
 
-// Statistics chunks: about 8192 elements (32 KB: one batch of eight 128-bit loads per thread),
-// shorter when rows are few so that the queue still holds about two units per SM, longer when
-// the partials would not fit their region.
-constexpr int kStatChunkMax = 8192;
+// Statistics units: whole rows when there are enough rows to give every SM two (a row per
+// unit, no partials, as at config 3); otherwise rows are cut into column chunks of at least
+// 2048 elements so that the few rows of small batches and of the draft sampler still spread
+// over the SMs (at most kMaxStatParts partials in all).
 constexpr int kStatChunkMin = 2048;
 constexpr int kMaxStatParts = 8192;
 inline void stat_chunks(int rows, int V, bool logits, int* nrc, int* len) {
-  if (!logits) {  // probability rows: one load at the drafted token
-    *nrc = 1;
-    *len = V;
-    return;
+  int n = 1;
+  if (logits && rows < 296) {  // probability rows need one load at the drafted token
+    n = (592 + rows - 1) / rows;
+    const int by_len = V / kStatChunkMin;
+    n = n < by_len ? n : by_len;
+    if (n * rows > kMaxStatParts) n = kMaxStatParts / rows;
+    n = n < 1 ? 1 : n;
   }
-  long long want = (static_cast<long long>(V) * rows + 295) / 296;
-  want = (want + 1023) / 1024 * 1024;
-  int l = static_cast<int>(want < kStatChunkMin ? kStatChunkMin : (want > kStatChunkMax ? kStatChunkMax : want));
-  int n = (V + l - 1) / l;
-  if (static_cast<long long>(n) * rows > kMaxStatParts) n = kMaxStatParts / rows > 1 ? kMaxStatParts / rows : 1;
-  l = ((V + n - 1) / n + 3) / 4 * 4;
+  const int l = n == 1 ? V : ((V + n - 1) / n + 3) / 4 * 4;
   *nrc = (V + l - 1) / l;
   *len = l;
 }
@@ -194,23 +194,35 @@ __device__ void chunk_statistics(const AcceptArgs& a, int b, int r, int x0, int 
     return;
   }
   // softmax statistics of z = x / T, online per thread: groups of kU float4 with one rescale
-  // per group, the next group's loads in flight while this one is reduced; at T == 1 the
-  // division is skipped (x / 1 is exact). The per-element exponentials of these sums use the
-  // fast intrinsic (the decisions below use expf on the few values they need).
+  // per group, double-buffered so that the next group's loads are in flight while this one is
+  // reduced; at T == 1 the division is skipped (x / 1 is exact). The per-element exponentials
+  // of these sums use the fast intrinsic (the decisions use expf on the few values they need).
   const float T = a.temperature;
   const bool unit_t = (T == 1.f);
   float m = -INFINITY, s = 0.f;
   if (vec) {
     const float4* r4 = reinterpret_cast<const float4*>(row);
     const int n4 = x1 / 4;
-    constexpr int kU = 8;  // 8 float4 per thread in flight: 32 KB per CTA, 128 KB per SM
-    for (int j0 = x0 / 4 + tid; j0 < n4; j0 += kU * kAcceptThreads) {
+    constexpr int kU = 4;  // 2 x 4 float4 per thread in flight: 32 KB per CTA, 128 KB per SM
+    const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    float4 cur[kU], nxt[kU];
+    int j0 = x0 / 4 + tid;
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int j = j0 + u * kAcceptThreads;
+      cur[u] = j < n4 ? __ldg(r4 + j) : ninf;
+    }
+    for (; j0 < n4; j0 += kU * kAcceptThreads) {
+      const int jn = j0 + kU * kAcceptThreads;
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int j = jn + u * kAcceptThreads;
+        nxt[u] = j < n4 ? __ldg(r4 + j) : ninf;
+      }
       float z[kU * 4];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
-        const int j = j0 + u * kAcceptThreads;
-        const float4 v = j < n4 ? __ldg(r4 + j) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-        z[4 * u] = v.x; z[4 * u + 1] = v.y; z[4 * u + 2] = v.z; z[4 * u + 3] = v.w;
+        z[4 * u] = cur[u].x; z[4 * u + 1] = cur[u].y; z[4 * u + 2] = cur[u].z; z[4 * u + 3] = cur[u].w;
       }
       float mx = m;
 #pragma unroll
@@ -225,6 +237,8 @@ __device__ void chunk_statistics(const AcceptArgs& a, int b, int r, int x0, int 
         s = acc;
         m = mx;
       }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) cur[u] = nxt[u];
     }
   } else {
     for (int j = x0 + tid; j < x1; j += kAcceptThreads) {
@@ -518,6 +532,9 @@ __device__ void decide(const AcceptArgs& a, int b) {
     sst[threadIdx.x] = v;
   }
   __syncthreads();
+  const bool sampling = !a.greedy && !a.decide_only;
+  // statistics that nothing reads any more go back to zero (sampling rows: after the residual)
+  if (!sampling && threadIdx.x < a.R) a.stats[static_cast<int64_t>(b) * a.R + threadIdx.x] = RowStat{0.f, 0.f, 0.f, 0};
   if (threadIdx.x == 0) {
     a.seq_tickets[b] = 0;  // ready for the next call
     int n = 0;
@@ -544,9 +561,9 @@ __device__ void decide(const AcceptArgs& a, int b) {
       if (run && acc) ++n; else run = false;
     }
     a.n_accepted[b] = n;
-    a.nsel[b] = n;
     if (a.greedy && !a.decide_only) a.next_token[b] = sst[n].amax;
-    if (!a.greedy && !a.decide_only) {
+    if (sampling) {
+      a.nsel[b] = n;
       __threadfence();
       st_release(a.ready + b, 1);
     }
@@ -601,6 +618,8 @@ __device__ void stat_unit(const AcceptArgs& a, int u) {
         st[r] = t;
         a.row_tickets[rb] = 0;
       }
+      __syncwarp();
+      for (int j = lane; j < a.nrc; j += 32) part[j] = RowStat{0.f, 0.f, 0.f, 0};  // read: back to zero
     }
   }
   __threadfence();
@@ -610,6 +629,17 @@ __device__ void stat_unit(const AcceptArgs& a, int u) {
   if (!sh_last) return;
   __threadfence();
   decide(a, b);
+}
+
+// The last residual chunk of sequence b, after every unit of b has read them: b's row
+// statistics, accepted length and chunk sums go back to zero (the workspace is all zero
+// between calls, whatever (B, k) the next call has). All threads of the CTA call it.
+__device__ void residual_clear(const AcceptArgs& a, int b, double* sums) {
+  __syncthreads();
+  const int tid = threadIdx.x;
+  if (tid < a.R) a.stats[static_cast<int64_t>(b) * a.R + tid] = RowStat{0.f, 0.f, 0.f, 0};
+  if (tid < 2 * a.C) sums[tid] = 0.0;
+  if (tid == 0) a.nsel[b] = 0;
 }
 
 // Residual unit v: chunk c of the residual row of sequence b (after b's decisions). The last
@@ -643,6 +673,7 @@ __device__ void residual_unit(const AcceptArgs& a, int v) {
   if (tid == 0) a.res_tickets[b] = 0;  // ready for the next call
   if (!ok) {
     if (tid == 0) a.next_token[b] = a.V - 1;
+    residual_clear(a, b, sums);
     return;
   }
   double total = 0.0;
@@ -675,6 +706,7 @@ __device__ void residual_unit(const AcceptArgs& a, int v) {
     base += __ldcg(sums + 2 * i + use_p);
   }
   if (tid == 0) a.next_token[b] = tok;
+  residual_clear(a, b, sums);
 }
 
 // Persistent CTAs: take units from the queue until it is empty; the next unit's number is

@@ -198,9 +198,6 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
     const int r = (kend - kbeg) + (idx >> 4), part = idx & 15, isv = part >> 3, cc = part & 7;
     *reinterpret_cast<uint4*>((isv ? v_s : k_s) + am_swz(r, cc * 8)) = make_uint4(0, 0, 0, 0);
   }
-  if (tid == 0)
-    l2_prefetch_share(a.l2_ahead, a.l2_ahead_bytes, blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z),
-                      gridDim.x * gridDim.y * gridDim.z);
   if (pdl) pdl_wait();
   stamp(1);
   if (a.qkv_parts) {

@@ -133,24 +133,6 @@ SPECB200_DEVINL bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int32_t* sta
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// ---------------------------------------------------------------- L2 look-ahead
-// Part `part` of `parts` equal shares of [base, base + bytes) fetched into L2 with bulk
-// prefetches of at most 64 KB (one thread; nothing waits on them). base and bytes are
-// multiples of 16. Kernels of a weight-streaming chain use it to pull a later kernel's
-// weights into L2 while the chain is latency-bound and HBM would otherwise idle.
-SPECB200_DEVINL void l2_prefetch_share(const void* base, size_t bytes, int part, int parts) {
-  if (!base || bytes == 0 || parts <= 0) return;
-  const size_t per = ((bytes + parts - 1) / parts + 15) / 16 * 16;
-  const size_t lo = per * static_cast<size_t>(part);
-  const size_t hi = lo + per < bytes ? lo + per : bytes;
-  const char* p = static_cast<const char*>(base);
-  for (size_t off = lo; off < hi; off += 65536) {
-    const uint32_t n = static_cast<uint32_t>(hi - off < 65536 ? hi - off : 65536);
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(reinterpret_cast<uint64_t>(p + off)), "r"(n)
-                 : "memory");
-  }
-}
-
 // ---------------------------------------------------------------- TMA (no multicast anywhere)
 SPECB200_DEVINL void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

@@ -238,20 +238,9 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
   // With a trace buffer, tensor-core GEMM launch i (4 per layer, then the head) records its
   // CTAs' timing (GemmScratch::trace).
   int gemm_slot = 0;
-  // Weight-streaming shapes (at most 64 token rows on the tensor-core kernels): each launch
-  // pulls a later launch's weights into L2 before its wait, while the chain's dependent links
-  // (norms, attention) leave HBM idle -- q/k/v fetches o, the attention fetches gate/up,
-  // gate/up fetches down, down fetches the next layer's q/k/v.
-  const bool ahead = tc && !cv.gemv && M <= 64;
-  const void* ahead_w = nullptr;
-  size_t ahead_bytes = 0;
   auto gemm = [&](const GemmShape& sh, const CUtensorMap* wmap, const CUtensorMap* xmap, const void* w, const T* x,
                   const Epilogue& e) -> int {
     GemmScratch g = gscr;
-    if (ahead) {
-      g.l2_ahead = ahead_w;
-      g.l2_ahead_bytes = ahead_bytes;
-    }
     if (bt.trace) {
       g.trace = reinterpret_cast<unsigned long long*>(bt.trace);
       g.trace_slot = gemm_slot++;
@@ -311,8 +300,6 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     eqp.op = EPI_PARTIAL;
     eqp.out = ws + cv.qkv_parts;
     eqp.ldo = m.qkv_n;
-    ahead_w = L.w_o;
-    ahead_bytes = static_cast<size_t>(c.hidden) * qd * sizeof(T);
     rc = cv.gemv ? gemv(cv.v_qkv, L.w_qkv, hidden, L.attn_norm, eq, m.qkv_n, c.hidden)
                  : gemm(cv.g_qkv, mp ? &mp->qkv : nullptr, &x_hidden, L.w_qkv, xbuf, cv.defer_qkv ? eqp : eq);
     if (rc) return rc;
@@ -347,10 +334,6 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
                  static_cast<size_t>(4 * c.n_layers + 1) * (cv.gemv ? kGemvTraceCtas * kGemvTraceStamps : kGemmTraceCtas * 8);
       aa.trace_slot = l;
     }
-    if (ahead) {
-      aa.l2_ahead = L.w_gate_up;
-      aa.l2_ahead_bytes = static_cast<size_t>(2 * c.intermediate) * c.hidden * sizeof(T);
-    }
     if ((rc = launch_attention<T>(aa, cv.ap, attn_counters, attn_parts, s, pdl))) return rc;
 
     Epilogue er = {};
@@ -361,8 +344,6 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     ep.op = EPI_PARTIAL;
     ep.out = resid_parts;
     ep.ldo = c.hidden;
-    ahead_w = nullptr;
-    ahead_bytes = 0;
     rc = cv.gemv ? gemv(cv.v_o, L.w_o, attn, nullptr, er, c.hidden, qd)
                  : gemm(cv.g_o, mp ? &mp->o : nullptr, &x_attn, L.w_o, attn, cv.defer ? ep : er);
     if (rc) return rc;
@@ -380,13 +361,9 @@ int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve&
     eg.op = EPI_SILU_MUL;
     eg.out = act;
     eg.ldo = c.intermediate;
-    ahead_w = L.w_down;
-    ahead_bytes = static_cast<size_t>(c.hidden) * c.intermediate * sizeof(T);
     rc = cv.gemv ? gemv(cv.v_gu, L.w_gate_up, hidden, L.mlp_norm, eg, 2 * c.intermediate, c.hidden)
                  : gemm(cv.g_gu, mp ? &mp->gu : nullptr, &x_mlp, L.w_gate_up, xbuf, eg);
     if (rc) return rc;
-    ahead_w = l + 1 < c.n_layers ? m.layers[l + 1].w_qkv : nullptr;
-    ahead_bytes = l + 1 < c.n_layers ? static_cast<size_t>(m.qkv_n) * c.hidden * sizeof(T) : 0;
     rc = cv.gemv ? gemv(cv.v_down, L.w_down, act, nullptr, er, c.hidden, c.intermediate)
                  : gemm(cv.g_down, mp ? &mp->down : nullptr, &x_act, L.w_down, act, cv.defer ? ep : er);
     if (rc) return rc;

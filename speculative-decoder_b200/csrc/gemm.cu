@@ -181,9 +181,6 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         mbar_arrive_expect_tx(&full[i], stage_bytes);
         tma_load_2d_hint(smem + i * stage_bytes, &w_map, &full[i], (kb0 + i) * kTileK, n_tile * kTileN, pol_w);
       }
-      l2_prefetch_share(scratch.l2_ahead, scratch.l2_ahead_bytes,
-                        blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z),
-                        gridDim.x * gridDim.y * gridDim.z);
       pdl_wait();
       stamp(1);
       for (int i = 0; i < pre; ++i)

@@ -62,10 +62,6 @@ struct GemmScratch {
   // partial published (after the fence), the ticket taken, the partials summed.
   unsigned long long* trace = nullptr;
   int trace_slot = 0;
-  // Optional: bytes of a later kernel's weights this launch pulls into L2 before its own
-  // griddepcontrol.wait (each CTA an equal share; l2_prefetch_share).
-  const void* l2_ahead = nullptr;
-  size_t l2_ahead_bytes = 0;
 };
 constexpr int kGemmTraceCtas = 512;
 size_t gemm_partials_bytes(const GemmShape& s);

@@ -71,10 +71,6 @@ struct AttnArgs {
   // partials [qkv_splits][B T][qkv_n] (EPI_PARTIAL) instead of q and the pool; the kernel sums
   // them in split order, applies the EPI_QKV rounding and RoPE, and the first CTA of each
   // cluster writes the new keys and values to the pool.
-  // Optional: bytes of a later kernel's weights this launch pulls into L2 before its wait (each
-  // CTA an equal share; l2_prefetch_share).
-  const void* l2_ahead = nullptr;
-  size_t l2_ahead_bytes = 0;
   const float* qkv_parts = nullptr;
   int qkv_splits = 0, qkv_n = 0;
   const float* rope_cos = nullptr;

@@ -204,14 +204,14 @@ SPECB200_DEVINL bool pk_wait(const ResArgs& a, const ResShared& s, const uint4* 
   }
 }
 
-// Packets i = tid, tid + 256, ... < n of the compute warps: the loads of up to four go out
+// Packets i = tid, tid + 256, ... < n of the compute warps: the loads of up to two go out
 // together (one round trip when they have all arrived), and only the ones whose epoch has not
 // arrived yet are then waited for. use(i, v, ok) consumes packet i (ok false after a wait gave
 // up or the launch was aborted).
 template <class At, class Use>
 SPECB200_DEVINL void pk_gather(const ResArgs& a, const ResShared& s, int n, uint32_t ep, unsigned* ctl, At&& at,
                                Use&& use) {
-  constexpr int kBatch = 4;
+  constexpr int kBatch = 2;
   for (int base = threadIdx.x; base < n; base += kBatch * kResConsumers) {
     uint4 v[kBatch];
 #pragma unroll
@@ -610,8 +610,9 @@ SPECB200_DEVINL void write_rows(const ResArgs& a, const ResShared& s, uint4* dst
 }
 
 // ---------------------------------------------------------------- the kernel
-// 288 threads, one CTA per SM: up to 216 registers a thread (62,208 of the SM's 65,536).
-__global__ void __maxnreg__(216) resident_kernel(const __grid_constant__ ResArgs a) {
+// 288 threads (nine warps), one CTA per SM: at most 168 registers a thread, since three of the
+// warps share one of the SM's four 16,384-register partitions.
+__global__ void __launch_bounds__(kResThreads, 1) resident_kernel(const __grid_constant__ ResArgs a) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int cta = blockIdx.x, S = a.p.slots;
