@@ -36,7 +36,7 @@ extern "C" {
 #define SPECB200_ERR_CUDA 4         /* a CUDA runtime call failed                        */
 #define SPECB200_ERR_TIMEOUT 5      /* a bounded device-side wait gave up                */
 #define SPECB200_ERR_UNSUPPORTED 6  /* model shape or dtype the kernels do not handle    */
-#define SPECB200_ERR_WORKSPACE 7    /* workspace smaller than the *_workspace_bytes size */
+#define SPECB200_ERR_WORKSPACE 7    /* workspace smaller than the *_workspace_bytes size, or (accept) not zero-filled */
 
 /* ---- element types ------------------------------------------------------------------ */
 #define SPECB200_F32 0

@@ -650,7 +650,16 @@ __device__ void residual_clear(const AcceptArgs& a, int b, double* sums) {
 __device__ void residual_unit(const AcceptArgs& a, int v) {
   __shared__ int sh_ok, sh_last;
   const int b = v / a.C, c = v % a.C, tid = threadIdx.x;
-  if (tid == 0) sh_ok = wait_flag(a.ready + b, a.status) ? 1 : 0;
+  if (tid == 0) {
+    sh_ok = wait_flag(a.ready + b, a.status) ? 1 : 0;
+    // the accepted length indexes the rows: a value outside 0..k (workspace not zero-filled
+    // before its first use) is reported, never used
+    const int n = sh_ok ? __ldcg(a.nsel + b) : 0;
+    if (sh_ok && (n < 0 || n > a.k)) {
+      set_status(a.status, SPECB200_ERR_WORKSPACE);
+      sh_ok = 0;
+    }
+  }
   __syncthreads();
   const bool ok = sh_ok;
   double* sums = a.chunk_sums + static_cast<int64_t>(b) * a.C * 2;

@@ -134,6 +134,8 @@ def check_status(status: torch.Tensor, where: str) -> None:
         raise IndexError(f"{where}: a token id, position or pool slot is out of range")
     if code == ERR_TIMEOUT:
         raise RuntimeError(f"{where}: a device-side wait gave up (timeout)")
+    if code == ERR_WORKSPACE:
+        raise RuntimeError(f"{where}: the workspace held stale state (it must be zero-filled before its first use)")
     if code != OK:
         raise RuntimeError(f"{where}: device status {code}")
 
