@@ -55,7 +55,9 @@ def accept_reject(p: np.ndarray, q: np.ndarray, draft: np.ndarray, u_accept: np.
         raise ValueError("a drafted token has zero draft probability; q is not what it was sampled from")
     accepted = np.asarray(u_accept, dtype=p.dtype) * q_x < p_x
     n = np.cumprod(accepted.astype(np.int64), axis=-1).sum(axis=-1)
-    q_padded = np.concatenate([q, np.zeros_like(q[:, :1])], axis=1)
+    # the bonus row is a zero-q row (spec/accept.py pads with zeros shaped like one q row; the
+    # explicit shape also covers k = 0, the plain sampler: the residual of p and 0 is p)
+    q_padded = np.concatenate([q, np.zeros((b, 1, p.shape[-1]), dtype=q.dtype)], axis=1)
     r = residual_distribution(p[rows, n], q_padded[rows, n])
     return n.astype(np.int64), sample_inverse_cdf(r, u_residual)
 

@@ -205,6 +205,46 @@ def test_accept_config3_size_matches_oracle(temperature):
     assert len(mismatched_rows) <= 2
 
 
+def test_accept_calls_of_different_shapes_share_one_workspace():
+    """One zero-filled workspace serves accept calls of any (B, k) and mode in turn (the
+    engine's round alternates k = 0 samplers with the (B, k) accept on one buffer): every call
+    matches the oracle's decisions and greedy tokens, and leaves the whole workspace zero."""
+    from specb200 import _ffi
+
+    lib = _ffi.lib()
+    nbytes = max(lib.specb200_accept_workspace_bytes(b, k) for b, k in ((7, 4), (1, 0), (3, 2), (64, 4)))
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    g = torch.Generator().manual_seed(91)
+    for B, K, V, temp in ((7, 4, 4096, 0.0), (1, 0, 49152, 1.0), (3, 2, 1000, 0.7), (64, 4, 4096, 1.0),
+                          (1, 0, 49152, 0.0), (7, 4, 4096, 1.0), (3, 2, 1000, 0.0)):
+        pl = torch.randn(B, K + 1, V, generator=g) * 2.0
+        ql = pl[:, :K] + torch.randn(B, K, V, generator=g)
+        qp = oacc.probabilities(ql.numpy(), temp)
+        draft = (torch.from_numpy(qp.argmax(-1)) if temp == 0 else
+                 torch.multinomial(torch.from_numpy(qp).reshape(-1, V), 1, generator=g).reshape(B, K)) if K else \
+            torch.zeros(B, 1, dtype=torch.int64)
+        ua, ur = torch.rand(B, max(K, 1), generator=g), torch.rand(B, generator=g)
+        d = {n: t.to(DEV).contiguous() for n, t in (("p", pl), ("q", ql), ("d", draft), ("ua", ua), ("ur", ur))}
+        n_acc = torch.empty(B, dtype=torch.int64, device=DEV)
+        nxt = torch.empty(B, dtype=torch.int64, device=DEV)
+        rc = lib.specb200_accept(d["p"].data_ptr(), d["q"].data_ptr() if K else None, d["d"].data_ptr(),
+                                 d["ua"].data_ptr(), d["ur"].data_ptr(), B, K, V, _ffi.ACCEPT_LOGITS, temp,
+                                 n_acc.data_ptr(), nxt.data_ptr(), status.data_ptr(), ws.data_ptr(), ws.numel(),
+                                 torch.cuda.current_stream().cuda_stream)
+        assert rc == 0
+        torch.cuda.synchronize()
+        assert int(status.item()) == 0
+        assert int(torch.count_nonzero(ws).item()) == 0, (B, K, V, temp)
+        on, onxt = oacc.accept_reject_logits(pl.numpy(), ql.numpy(), draft.numpy()[:, :K], ua.numpy()[:, :K],
+                                             ur.numpy(), temp)
+        got_n, got_t = n_acc.cpu().numpy(), nxt.cpu().numpy()
+        if temp == 0:
+            assert np.array_equal(got_n, on) and np.array_equal(got_t, onxt), (B, K, V)
+        else:  # sampled: decisions and tokens agree except at the 1e-5 boundaries (config-3 test)
+            assert (got_n != on).sum() + (got_t != onxt).sum() <= 1, (B, K, V)
+
+
 # ---------------------------------------------------------------- n-gram (K9)
 def test_ngram_matches_reference_golden(golden_ngram):
     from spec.ngram import lookup
