@@ -396,32 +396,6 @@ def gemv_trace_summary(trace: torch.Tensor, n_layers: int) -> dict:
     return out
 
 
-def resident_trace_summary(t: torch.Tensor, n_layers: int) -> dict:
-    """The resident kernel's phase stamps ([9 L + 3][grid] globaltimer ns, see resident.cuh):
-    per phase, medians over layers (us) of the phase's critical-path length (latest stamp of the
-    phase minus latest stamp of the phase before it) and of the spread of its stamps over CTAs
-    (latest minus median)."""
-    t = t.cpu().to(torch.float64) / 1e3
-    t0 = float(t[9 * n_layers + 2].min())
-    late = t.max(dim=1).values - t0
-    med = t.median(dim=1).values - t0
-    names = ["input", "qkv", "attention", "gather", "o", "mlp_norm", "gate_up", "act_read", "down"]
-    out = {"total_us": round(float(late[9 * n_layers + 1]), 1),
-           "entry_spread_us": round(float(t[9 * n_layers + 2].max()) - t0, 2)}
-
-    def prev(l: int, j: int):
-        if j > 0:
-            return late[9 * l + j - 1]
-        return late[9 * (l - 1) + 8] if l > 0 else late[9 * n_layers + 2]
-
-    for j, name in enumerate(names):
-        seg = [float(late[9 * l + j] - prev(l, j)) for l in range(n_layers)]
-        spread = [float(late[9 * l + j] - med[9 * l + j]) for l in range(n_layers)]
-        out[name] = [round(statistics.median(seg), 2), round(statistics.median(spread), 2)]
-    out["head"] = round(float(late[9 * n_layers + 1] - late[9 * n_layers]), 2)
-    return out
-
-
 def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30, trace: bool = False,
                     tokens: int = 1) -> dict:
     """One draft-model forward (135M architecture, B=1) of `tokens` new tokens, CUDA graph: 1 as
@@ -467,13 +441,6 @@ def time_draft_step(draft, cache_cls, device, context_len: int, reps: int = 30, 
     r = {"us": st.elapsed_time(en) / reps * 1e3,
          "bytes": weight_bytes(spec) + kv_bytes_per_token(spec) * context_len, "context": context_len,
          "layers": spec["num_hidden_layers"]}
-    if trace and eng.schedule(1, tokens) == "resident":
-        L = spec["num_hidden_layers"]
-        grid = torch.cuda.get_device_properties(device).multi_processor_count
-        tr = torch.zeros((9 * L + 3) * grid, dtype=torch.int64, device=device)
-        eng.forward_device(cache, ids, one, pastt, table, cap, True, logits, status, ws, trace=tr)
-        torch.cuda.synchronize()
-        r["trace"] = resident_trace_summary(tr.view(9 * L + 3, grid), L)
     if trace and eng.schedule(1, tokens) == "gemv":
         L = spec["num_hidden_layers"]
         tr = torch.zeros((4 * L + 1) * 296 * 8 + L * 512 * 8, dtype=torch.int64, device=device)

@@ -220,21 +220,20 @@ typedef struct specb200_batch {
 } specb200_batch;
 
 size_t specb200_forward_workspace_bytes(void* model, int B, int T, int max_kv_len);
-/* Which schedule a call with B rows of T tokens runs (for contexts of up to 1024 keys):
- * 4 = decode steps of at most 4 token rows of a draft-class model (hidden <= 1024) as ONE
- * cooperative launch with one CTA per SM (the resident kernel), 3 = decode steps of at most 4
- * token rows of a model whose layer weights fit on chip, on the GEMV kernels with the norms
- * folded in (2 + 5 n_layers launches, 3 + 5 n_layers with a tensor-core LM head), 0 = one
- * kernel per layer op (3 + 7 n_layers launches). No reference counterpart. */
+/* Which schedule a call with B rows of T tokens runs: 3 = decode steps of at most 4 token rows
+ * of a model whose layer weights fit on chip, on the GEMV kernels with the norms folded in
+ * (2 + 5 n_layers launches, 3 + 5 n_layers with a tensor-core LM head), 0 = one kernel per
+ * layer op (3 + 7 n_layers launches). No reference counterpart. */
 int specb200_forward_schedule(void* model, int B, int T);
 
-/* Clock cycles a device-side wait for data produced by other CTAs of the same launch may spin
- * before it gives up (the resident kernel's packet waits): the waiting kernel then records
- * SPECB200_ERR_TIMEOUT in the call's status word, every CTA drains its own copies in flight and
- * returns, and the call's outputs are undefined. Applies to launches made after the call (a CUDA
- * graph keeps the limit it was captured with). cycles <= 0 restores the default (about two
- * seconds). Returns the previous limit. No reference counterpart (the reference has no device
- * waits); its use is fault testing on the host side: a small limit makes every wait give up. */
+/* Clock cycles a device-side wait for a flag raised by another CTA of the same launch may spin
+ * before it gives up (the accept kernel's residual units waiting for their sequence's
+ * decisions): the waiting CTA then records SPECB200_ERR_TIMEOUT in the call's status word and
+ * finishes without that data, and the call's sampled tokens are undefined (the workspace is
+ * still left zero-filled). Applies to launches made after the call (a CUDA graph keeps the limit
+ * it was captured with). cycles <= 0 restores the default (about two seconds). Returns the
+ * previous limit. No reference counterpart (the reference has no device waits); its use is
+ * fault testing on the host side: a small limit makes such waits give up. */
 long long specb200_set_wait_limit(long long cycles);
 /* Kernel launches one forward call with B rows of T tokens makes (no reference counterpart;
  * used to count launches). */

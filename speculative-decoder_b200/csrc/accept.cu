@@ -31,6 +31,7 @@
 // serves calls of any (B, k) with no clearing in between. Decisions therefore cost one HBM
 // pass over p and q.
 #include <algorithm>
+#include <atomic>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -73,6 +74,7 @@ struct AcceptArgs {
   int nrc, rclen;      // statistics chunks per row and their length (a multiple of 4)
   int C, chunk;        // residual chunks per sequence and their length (a multiple of 1024)
   int units_stat, units_total;
+  long long wait_limit;  // clock cycles a wait for another CTA's flag may spin before it gives up
 };
 
 // Statistics units: whole rows when there are enough rows to give every SM two (a row per
@@ -495,14 +497,14 @@ SPECB200_DEVINL void st_release(int* p, int v) {
 }
 
 // Bounded wait for a flag another CTA raises (set while it runs a unit taken from the queue
-// earlier): false, with SPECB200_ERR_TIMEOUT in the status word, once the limit ran out.
-SPECB200_DEVINL bool wait_flag(const int* flag, int32_t* status) {
+// earlier): false, with SPECB200_ERR_TIMEOUT in the status word, once `limit` cycles ran out.
+SPECB200_DEVINL bool wait_flag(const int* flag, int32_t* status, long long limit) {
   if (ld_acquire(flag)) return true;
   const long long t0 = clock64();
   while (true) {
     __nanosleep(32);
     if (ld_acquire(flag)) return true;
-    if (clock64() - t0 > SPECB200_SPIN_LIMIT_CYCLES) {
+    if (clock64() - t0 > limit) {
       set_status(status, SPECB200_ERR_TIMEOUT);
       return false;
     }
@@ -651,7 +653,7 @@ __device__ void residual_unit(const AcceptArgs& a, int v) {
   __shared__ int sh_ok, sh_last;
   const int b = v / a.C, c = v % a.C, tid = threadIdx.x;
   if (tid == 0) {
-    sh_ok = wait_flag(a.ready + b, a.status) ? 1 : 0;
+    sh_ok = wait_flag(a.ready + b, a.status, a.wait_limit) ? 1 : 0;
     // the accepted length indexes the rows: a value outside 0..k (workspace not zero-filled
     // before its first use) is reported, never used
     const int n = sh_ok ? __ldcg(a.nsel + b) : 0;
@@ -813,6 +815,7 @@ using namespace specb200;
 namespace specb200 {
 namespace {
 int g_sm_count[64] = {};
+std::atomic<long long> g_wait_limit{SPECB200_SPIN_LIMIT_CYCLES};
 
 // Streaming multiprocessors of the current device (looked up once per device).
 int sm_count() {
@@ -844,6 +847,7 @@ cudaError_t launch_accept(AcceptArgs& a, char* ws, const AcceptLayout& l, cudaSt
   a.units_stat = a.B * a.R * a.nrc;
   a.units_total = a.units_stat + (sampling ? a.B * a.C : 0);
   const int ctas = std::min(a.units_total, kAcceptCtasPerSm * sm_count());
+  a.wait_limit = g_wait_limit.load();
   cudaError_t e = cudaSuccess;
   if (a.status) e = cudaMemsetAsync(a.status, 0, sizeof(int32_t), s);
   if (e != cudaSuccess) return e;
@@ -899,6 +903,11 @@ extern "C" int specb200_accept(const float* p, const float* q, const int64_t* dr
   const cudaError_t e = launch_accept(a, static_cast<char*>(workspace), l, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
   return SPECB200_OK;
+}
+
+extern "C" long long specb200_set_wait_limit(long long cycles) {
+  if (cycles <= 0) cycles = SPECB200_SPIN_LIMIT_CYCLES;
+  return g_wait_limit.exchange(cycles);
 }
 
 extern "C" int specb200_probabilities(const float* logits, int rows, int V, float temperature, float* out, void* stream) {

@@ -18,7 +18,6 @@
 #include "gemm.cuh"
 #include "gemv.cuh"
 #include "kernels.cuh"
-#include "resident.cuh"
 
 namespace specb200 {
 namespace {
@@ -35,15 +34,13 @@ struct Model {
   CUtensorMap head;
   int qkv_n;
   bool gemv_ok = false;  // bf16 weights usable by the decode-step GEMV kernels (gemv.cu)
-  bool res_ok = false;   // bf16 weights usable by the resident decode kernel (resident.cu)
 };
 
-std::atomic<long long> g_wait_limit{SPECB200_SPIN_LIMIT_CYCLES};
 
 size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 struct Carve {
-  size_t gemm_counters, attn_counters, res_region, hidden, xbuf, qbuf, attn, act, pos, slot, gemm_parts, attn_parts, resid_parts,
+  size_t gemm_counters, attn_counters, hidden, xbuf, qbuf, attn, act, pos, slot, gemm_parts, attn_parts, resid_parts,
       qkv_parts, total;
   // per-layer schedule: the o and down GEMMs store split partials (EPI_PARTIAL) and the RMSNorm
   // launch that follows each adds them to the residual stream (launch_residual_norm)
@@ -52,8 +49,6 @@ struct Carve {
   // writes to the pool itself (no ticket, no epilogue tail in the GEMM)
   bool defer_qkv;
   GemmShape g_qkv, g_o, g_gu, g_down, g_head;
-  bool resident;  // decode steps on the resident kernel (one cooperative launch)
-  ResPlan rp;
   bool gemv;  // decode-step schedule: the per-layer order with GEMV kernels and fused norms
   bool gemv_head;  // ... and the LM head as a GEMV with the final norm folded in
   GemvPlan v_qkv, v_o, v_gu, v_down, v_head;
@@ -98,10 +93,8 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
     r.g_down.splits = std::min(r.g_down.splits, 8);
     r.defer = residual_norm_fits(r.g_o.splits, c.hidden) && residual_norm_fits(r.g_down.splits, c.hidden);
   }
-  r.resident = m.res_ok && plan_resident(c.n_layers, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim, c.intermediate,
-                                         c.vocab, B, T, max_kv_len, &r.rp);
-  r.gemv = !r.resident && use_gemv(m, M, rows_out, &r.v_qkv, &r.v_o, &r.v_gu, &r.v_down, &r.v_head, &r.gemv_head);
-  r.defer = r.defer && !r.gemv && !r.resident;
+  r.gemv = use_gemv(m, M, rows_out, &r.v_qkv, &r.v_o, &r.v_gu, &r.v_down, &r.v_head, &r.gemv_head);
+  r.defer = r.defer && !r.gemv;
   r.ap = plan_attention(B, T, c.n_heads, c.n_kv_heads, max_kv_len, tc && c.head_dim == 64);
   r.defer_qkv = r.defer && r.ap.mma == 2 && c.head_dim == 64 && r.g_qkv.splits <= kQkvMaxSplits;
   // The two ticket-counter regions sit at fixed offsets so that they stay zero across calls
@@ -109,9 +102,6 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   size_t off = 0;
   r.gemm_counters = off; off += align256(kGemmCounterBytes);
   r.attn_counters = off; off += align256(kAttnCounterBytes);
-  // the resident kernel's packets and control words: one fixed region for every shape and
-  // model sharing the workspace (its generation counter must survive calls of other shapes)
-  r.res_region = off; off += kResRegionBytes;
   r.hidden = off; off += align256(static_cast<size_t>(M) * c.hidden * el);
   r.xbuf = off; off += align256(static_cast<size_t>(M) * c.hidden * el);
   r.qbuf = off; off += align256(static_cast<size_t>(M) * qd * el);
@@ -135,52 +125,6 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
 template <typename T>
 int run_head(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv, cudaStream_t s,
              const CUtensorMap* x_final);
-
-// A decode step of at most kResMaxRows token rows as one cooperative launch (resident.cu).
-int run_resident(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv, cudaStream_t s) {
-  const specb200_model_config& c = m.cfg;
-  ResArgs a = {};
-  a.L = c.n_layers;
-  a.H = c.hidden;
-  a.Hq = c.n_heads;
-  a.Hkv = c.n_kv_heads;
-  a.I = c.intermediate;
-  a.V = c.vocab;
-  a.max_positions = c.max_positions;
-  a.eps = c.rms_eps;
-  a.scale = 1.0f / sqrtf(static_cast<float>(c.head_dim));
-  a.embed = static_cast<const __nv_bfloat16*>(m.w.embed);
-  a.final_norm = static_cast<const __nv_bfloat16*>(m.w.final_norm);
-  a.head = static_cast<const __nv_bfloat16*>(m.w.lm_head);
-  a.rope_cos = m.w.rope_cos;
-  a.rope_sin = m.w.rope_sin;
-  for (int l = 0; l < c.n_layers; ++l) {
-    const specb200_layer_weights& L = m.layers[l];
-    a.layers[l] = {static_cast<const __nv_bfloat16*>(L.attn_norm), static_cast<const __nv_bfloat16*>(L.w_qkv),
-                   static_cast<const __nv_bfloat16*>(L.w_o), static_cast<const __nv_bfloat16*>(L.mlp_norm),
-                   static_cast<const __nv_bfloat16*>(L.w_gate_up), static_cast<const __nv_bfloat16*>(L.w_down)};
-  }
-  a.B = bt.B;
-  a.T = bt.T;
-  a.M = bt.B * bt.T;
-  a.last_only = bt.last_only;
-  a.ids = bt.input_ids;
-  a.n_new = bt.n_new;
-  a.past = bt.past_len;
-  a.table = bt.block_table;
-  a.table_stride = bt.table_stride;
-  a.bs = bt.block_size;
-  a.num_slots = bt.num_slots;
-  a.k_pool = static_cast<__nv_bfloat16*>(bt.k_pool);
-  a.v_pool = static_cast<__nv_bfloat16*>(bt.v_pool);
-  a.logits = bt.logits;
-  a.region = reinterpret_cast<uint8_t*>(ws + cv.res_region);
-  a.status = bt.status;
-  a.wait_limit = g_wait_limit.load();
-  a.trace = reinterpret_cast<unsigned long long*>(bt.trace);
-  a.p = cv.rp;
-  return launch_resident(a, s);
-}
 
 template <typename T>
 int run_forward(const Model& m, const specb200_batch& bt, char* ws, const Carve& cv, cudaStream_t s) {
@@ -452,14 +396,6 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
   norm_prepare();
   // Decode-step GEMV schedule: bf16 weights, 16-byte aligned rows.
   auto al16 = [](const void* p) { return p && (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-  // Resident decode kernel: the same alignment (its bulk copies read whole weight rows), d = 64.
-  m->res_ok = c.dtype == SPECB200_BF16 && c.head_dim == 64 && c.n_layers <= kResMaxLayers && al16(weights->lm_head) &&
-              al16(weights->embed) && al16(weights->final_norm) && resident_prepare();
-  for (int l = 0; l < c.n_layers && m->res_ok; ++l) {
-    const specb200_layer_weights& L = weights->layers[l];
-    m->res_ok = al16(L.w_qkv) && al16(L.w_o) && al16(L.w_gate_up) && al16(L.w_down) && al16(L.attn_norm) &&
-                al16(L.mlp_norm);
-  }
   m->gemv_ok = c.dtype == SPECB200_BF16 && al16(weights->lm_head) &&
                al16(weights->final_norm) && gemv_prepare();
   for (int l = 0; l < c.n_layers && m->gemv_ok; ++l) {
@@ -487,18 +423,13 @@ extern "C" int specb200_model_create(const specb200_model_config* config, const 
   return SPECB200_OK;
 }
 
-// Kernel launches of one forward call: 1 for the resident kernel, 2 + 5 L for the GEMV schedule
+// Kernel launches of one forward call: 2 + 5 L for the GEMV schedule
 // (prep, 5 per layer, head; one more when the head is RMSNorm + the tensor-core GEMM), and for
 // the per-layer kernels 3 + 7 L (prep, RMSNorm + 5 GEMM / attention launches + RMSNorm per
 // layer, final norm, head). Counted for contexts of up to 1024 keys.
 extern "C" int specb200_forward_launches(void* model, int B, int T) {
   if (!model || B <= 0 || T <= 0) return 0;
   const Model& m = *static_cast<Model*>(model);
-  const specb200_model_config& c = m.cfg;
-  ResPlan rp;
-  if (m.res_ok && plan_resident(c.n_layers, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim, c.intermediate, c.vocab, B, T,
-                                1024, &rp))
-    return 1;
   GemvPlan v[5];
   bool head_gemv = false;
   if (use_gemv(m, B * T, B, &v[0], &v[1], &v[2], &v[3], &v[4], &head_gemv))
@@ -506,16 +437,10 @@ extern "C" int specb200_forward_launches(void* model, int B, int T) {
   return 3 + 7 * m.cfg.n_layers;
 }
 
-// Which schedule a call runs (contexts of up to 1024 keys): 4 = the resident decode kernel,
-// 3 = the decode-step GEMV kernels, 0 = one kernel per layer op.
+// Which schedule a call runs: 3 = the decode-step GEMV kernels, 0 = one kernel per layer op.
 extern "C" int specb200_forward_schedule(void* model, int B, int T) {
   if (!model || B <= 0 || T <= 0) return 0;
   const Model& m = *static_cast<Model*>(model);
-  const specb200_model_config& c = m.cfg;
-  ResPlan rp;
-  if (m.res_ok && plan_resident(c.n_layers, c.hidden, c.n_heads, c.n_kv_heads, c.head_dim, c.intermediate, c.vocab, B, T,
-                                1024, &rp))
-    return 4;
   GemvPlan v[5];
   bool head_gemv = false;
   return use_gemv(m, B * T, B, &v[0], &v[1], &v[2], &v[3], &v[4], &head_gemv) ? 3 : 0;
@@ -545,8 +470,7 @@ extern "C" int specb200_forward(void* model, const specb200_batch* batch, void* 
   if (workspace_bytes < cv.total) return specb200_set_error(SPECB200_ERR_WORKSPACE, "forward: workspace too small");
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (bt.status) cudaMemsetAsync(bt.status, 0, sizeof(int32_t), s);
-  int rc = cv.resident ? run_resident(m, bt, static_cast<char*>(workspace), cv, s)
-           : m.cfg.dtype == SPECB200_BF16 ? run_forward<__nv_bfloat16>(m, bt, static_cast<char*>(workspace), cv, s)
+  int rc = m.cfg.dtype == SPECB200_BF16 ? run_forward<__nv_bfloat16>(m, bt, static_cast<char*>(workspace), cv, s)
                                           : run_forward<float>(m, bt, static_cast<char*>(workspace), cv, s);
   if (rc != SPECB200_OK) {
     cudaError_t e = cudaGetLastError();
@@ -555,7 +479,3 @@ extern "C" int specb200_forward(void* model, const specb200_batch* batch, void* 
   return SPECB200_OK;
 }
 
-extern "C" long long specb200_set_wait_limit(long long cycles) {
-  if (cycles <= 0) cycles = SPECB200_SPIN_LIMIT_CYCLES;
-  return g_wait_limit.exchange(cycles);
-}

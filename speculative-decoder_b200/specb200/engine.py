@@ -119,12 +119,11 @@ class Engine:
         return lib().specb200_forward_launches(self.handle, b, t)
 
     def schedule(self, b: int, t: int) -> str:
-        """The schedule a forward call of B rows x T tokens runs (contexts up to 1024 keys):
-        "resident" (decode steps of at most 4 token rows of a draft-class model: the whole step
-        as one cooperative launch), "gemv" (decode steps of at most 4 token rows: a kernel per
-        linear with the norms folded in) or "layers" (a kernel per op)."""
+        """The schedule a forward call of B rows x T tokens runs: "gemv" (decode steps of at
+        most 4 token rows: a kernel per linear with the norms folded in) or "layers" (a kernel
+        per op)."""
         code = lib().specb200_forward_schedule(self.handle, b, t)
-        return {4: "resident", 3: "gemv"}.get(code, "layers")
+        return {3: "gemv"}.get(code, "layers")
 
     def workspace_bytes(self, b: int, t: int, max_kv_len: int) -> int:
         return lib().specb200_forward_workspace_bytes(self.handle, b, t, max_kv_len)

@@ -324,28 +324,22 @@ def _gemv_steps(eng, model, prompt_len: int = 300, pad_to: int = 0):
 @pytest.mark.parametrize("dims", [(576, 2, 9, 3, 1536, 49152), (256, 2, 4, 4, 512, 49152),
                                   (128, 2, 4, 2, 256, 512)])
 def test_decode_schedules_match_per_layer_kernels(dims):
-    """Decode-sized calls (at most 4 token rows) against the same tokens padded to 5 per row,
-    which run on the tensor-core per-layer kernels. The 135M draft width runs the resident
-    kernel (the whole step as one cooperative launch); a narrow model with the same vocabulary
-    and a head_dim-32 model with a small one (whose LM head is a GEMV too) run the GEMV kernels
-    (their gate/up widths leave some SMs without work, which the resident kernel needs); 2
-    layers each. The schedules sum in different orders, so logits agree to bf16 noise (1e-2 of
-    the logit scale, argmax equal except at near ties) and the KV entries the calls wrote to
-    one bf16 ulp of their scale."""
+    """Decode-sized calls (at most 4 token rows) on the GEMV kernels against the same tokens
+    padded to 5 per row, which run on the tensor-core per-layer kernels: the 135M draft width, a
+    narrow model with the same vocabulary and a head_dim-32 model with a small one (whose LM
+    head is a GEMV too); 2 layers each. The schedules sum in different orders, so logits agree
+    to bf16 noise (1e-2 of the logit scale, argmax equal except at near ties) and the KV entries
+    the calls wrote to one bf16 ulp of their scale."""
     from specb200.engine import Engine
 
     model = _bf16_model(*dims, seed=8, theta=100000.0).to(DEV)
     eng = Engine(model)
-    decode = "resident" if dims[0] == 576 else "gemv"
-    assert eng.schedule(1, 1) == decode and eng.schedule(2, 2) == decode and eng.schedule(1, 3) == decode
+    assert eng.schedule(1, 1) == "gemv" and eng.schedule(2, 2) == "gemv" and eng.schedule(1, 3) == "gemv"
     assert eng.schedule(1, 5) == "layers" and eng.schedule(2, 5) == "layers"
-    if decode == "resident":
-        assert eng.launches(1, 1) == 1
-    else:
-        # prep, 5 per layer, then the LM head: a GEMV with the final norm folded in (small
-        # vocabulary) or the final norm and the tensor-core GEMM
-        head_launches = 1 if dims[-1] <= 4096 else 2
-        assert eng.launches(1, 1) == 1 + head_launches + 5 * 2
+    # prep, 5 per layer, then the LM head: a GEMV with the final norm folded in (small
+    # vocabulary) or the final norm and the tensor-core GEMM
+    head_launches = 1 if dims[-1] <= 4096 else 2
+    assert eng.launches(1, 1) == 1 + head_launches + 5 * 2
     assert eng.launches(1, 5) == 3 + 7 * 2
     (la, ca), (lb, cb) = _gemv_steps(eng, model, pad_to=5), _gemv_steps(eng, model)
     for a, b in zip(la, lb):
@@ -361,8 +355,8 @@ def test_decode_schedules_match_per_layer_kernels(dims):
 
 @pytest.mark.parametrize("dims", [(576, 2, 9, 3, 1536, 49152), (128, 2, 4, 2, 256, 512)])
 def test_decode_schedules_match_oracle(dims):
-    """The decode schedules (resident kernel at the 135M width, GEMV kernels at a narrow width)
-    against the bf16 oracle: after a prefill, 1-token steps of one and of two sequences and a
+    """The decode-step GEMV schedule (at the 135M width and at a narrow width) against the bf16
+    oracle: after a prefill, 1-token steps of one and of two sequences and a
     3-token step, logits within rtol 2e-2 of the largest logit."""
     from lm.forward import forward
     from specb200.engine import engine_for
@@ -371,7 +365,7 @@ def test_decode_schedules_match_oracle(dims):
     w = ofw.weights_from_model(model)
     prec = ofw.Precision("bf16")
     model = model.to(DEV)
-    assert engine_for(model).schedule(1, 1) == ("resident" if dims[0] == 576 else "gemv")
+    assert engine_for(model).schedule(1, 1) == "gemv"
     cache = new_cache(model, block_size=16)
     ocache = ofw.Cache(w, 4096, 16, prec)
     for s in range(2):
