@@ -62,7 +62,7 @@ struct AcceptArgs {
   int64_t* n_accepted;
   int64_t* next_token;
   int32_t* status;
-  int* ctl;            // [0] unit queue, [1] CTAs finished
+  int* ctl;            // [0] unit queue, [1] CTAs finished, [2] a wait gave up
   int* row_tickets;    // [B, R]: chunks of the row done
   int* seq_tickets;    // [B]: rows of the sequence done
   int* res_tickets;    // [B]: residual chunks of the sequence done
@@ -195,36 +195,24 @@ __device__ void chunk_statistics(const AcceptArgs& a, int b, int r, int x0, int 
     }
     return;
   }
-  // softmax statistics of z = x / T, online per thread: groups of kU float4 with one rescale
-  // per group, double-buffered so that the next group's loads are in flight while this one is
-  // reduced; at T == 1 the division is skipped (x / 1 is exact). The per-element exponentials
-  // of these sums use the fast intrinsic (the decisions use expf on the few values they need).
+  // softmax statistics of z = x / T, online per thread: groups of kU float4 whose loads are all
+  // in flight together, one rescale per group; at T == 1 the division is skipped (x / 1 is
+  // exact). The per-element exponentials of these sums use the fast intrinsic (the decisions
+  // use expf on the few values they need).
   const float T = a.temperature;
   const bool unit_t = (T == 1.f);
   float m = -INFINITY, s = 0.f;
   if (vec) {
     const float4* r4 = reinterpret_cast<const float4*>(row);
     const int n4 = x1 / 4;
-    constexpr int kU = 4;  // 2 x 4 float4 per thread in flight: 32 KB per CTA, 128 KB per SM
-    const float4 ninf = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-    float4 cur[kU], nxt[kU];
-    int j0 = x0 / 4 + tid;
-#pragma unroll
-    for (int u = 0; u < kU; ++u) {
-      const int j = j0 + u * kAcceptThreads;
-      cur[u] = j < n4 ? __ldg(r4 + j) : ninf;
-    }
-    for (; j0 < n4; j0 += kU * kAcceptThreads) {
-      const int jn = j0 + kU * kAcceptThreads;
-#pragma unroll
-      for (int u = 0; u < kU; ++u) {
-        const int j = jn + u * kAcceptThreads;
-        nxt[u] = j < n4 ? __ldg(r4 + j) : ninf;
-      }
+    constexpr int kU = 8;  // 8 float4 per thread in flight: 32 KB per CTA, 128 KB per SM
+    for (int j0 = x0 / 4 + tid; j0 < n4; j0 += kU * kAcceptThreads) {
       float z[kU * 4];
 #pragma unroll
       for (int u = 0; u < kU; ++u) {
-        z[4 * u] = cur[u].x; z[4 * u + 1] = cur[u].y; z[4 * u + 2] = cur[u].z; z[4 * u + 3] = cur[u].w;
+        const int j = j0 + u * kAcceptThreads;
+        const float4 v = j < n4 ? __ldg(r4 + j) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        z[4 * u] = v.x; z[4 * u + 1] = v.y; z[4 * u + 2] = v.z; z[4 * u + 3] = v.w;
       }
       float mx = m;
 #pragma unroll
@@ -239,8 +227,6 @@ __device__ void chunk_statistics(const AcceptArgs& a, int b, int r, int x0, int 
         s = acc;
         m = mx;
       }
-#pragma unroll
-      for (int u = 0; u < kU; ++u) cur[u] = nxt[u];
     }
   } else {
     for (int j = x0 + tid; j < x1; j += kAcceptThreads) {
@@ -683,7 +669,12 @@ __device__ void residual_unit(const AcceptArgs& a, int v) {
   __threadfence();
   if (tid == 0) a.res_tickets[b] = 0;  // ready for the next call
   if (!ok) {
-    if (tid == 0) a.next_token[b] = a.V - 1;
+    // a unit of b gave up: b's decisions may still land after this, so the last CTA of the
+    // launch clears every sequence's statistics, lengths and sums (ctl[2] asks it to)
+    if (tid == 0) {
+      a.next_token[b] = a.V - 1;
+      atomicExch(a.ctl + 2, 1);
+    }
     residual_clear(a, b, sums);
     return;
   }
@@ -746,10 +737,18 @@ __global__ void __launch_bounds__(kAcceptThreads, kAcceptCtasPerSm) accept_kerne
   }
   __syncthreads();
   if (sh_end) {
+    __threadfence();
     for (int b = tid; b < a.B; b += kAcceptThreads) a.ready[b] = 0;
+    if (__ldcg(a.ctl + 2)) {  // after a wait gave up: everything the call may have left behind
+      for (int i = tid; i < a.B * a.R; i += kAcceptThreads) a.stats[i] = RowStat{0.f, 0.f, 0.f, 0};
+      for (int i = tid; i < a.B; i += kAcceptThreads) a.nsel[i] = 0;
+      for (int i = tid; i < a.B * a.C * 2; i += kAcceptThreads) a.chunk_sums[i] = 0.0;
+    }
+    __syncthreads();
     if (tid == 0) {
       a.ctl[0] = 0;
       a.ctl[1] = 0;
+      a.ctl[2] = 0;
     }
   }
 }
