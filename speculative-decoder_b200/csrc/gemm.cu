@@ -364,11 +364,11 @@ namespace {
 int tc_stages(int BN, size_t* smem_bytes) {
   const size_t stage = kWTileBytes + static_cast<size_t>(BN) * kTileK * 2;
   const size_t tile = static_cast<size_t>(BN) * kEpiPitch * 4;
-  // Decode and verify shapes (16 tokens): about 110 KB of ring lets a CTA of the next GEMM
-  // share the SM and prefetch its weights (measured 1.343 vs 1.361 ms per verify with the
-  // 200 KB ring). Larger token tiles (prefill, large batches) keep one CTA per SM with a deep
-  // ring, since their operand tiles are large and the GEMMs long.
-  const size_t budget = BN <= 16 ? 110 * 1024 : 200 * 1024;
+  // Weight-bound shapes (token tiles up to 48: decode, verify, small batches): about 110 KB of
+  // ring lets a CTA of the next GEMM share the SM and prefetch its weights (measured 1.343 vs
+  // 1.361 ms per verify with the 200 KB ring). Large token tiles (prefill, large batches) keep
+  // one CTA per SM with a deep ring, since their operand tiles are large and the GEMMs long.
+  const size_t budget = BN <= 48 ? 110 * 1024 : 200 * 1024;
   int stages = static_cast<int>(std::min<size_t>(8, budget / stage));
   while (static_cast<size_t>(stages) * stage < tile) ++stages;
   stages = std::max(stages, 2);
