@@ -50,6 +50,15 @@ struct RowStat {
   int amax;    // first index of the maximum (greedy rows)
 };
 
+// Published by the decisions of a sampling sequence for its residual units (one 32-byte load):
+// the accepted length n, the drafted token at n (-1 at the bonus row) and the softmax
+// statistics of target row n and draft row n.
+struct __align__(16) ResDesc {
+  int n, dn;
+  float p_m, p_s, q_m, q_s;
+  int pad[2];
+};
+
 struct AcceptArgs {
   const float* p;
   const float* q;
@@ -62,14 +71,14 @@ struct AcceptArgs {
   int64_t* n_accepted;
   int64_t* next_token;
   int32_t* status;
-  int* ctl;            // [0] unit queue, [1] CTAs finished, [2] a wait gave up
+  int* ctl;            // [0] unit queue (units past each CTA's first)
   int* row_tickets;    // [B, R]: chunks of the row done
   int* seq_tickets;    // [B]: rows of the sequence done
   int* res_tickets;    // [B]: residual chunks of the sequence done
-  int* ready;          // [B]: decisions made (sampling rows)
+  int* ready;          // [B]: 1 = decisions made (sampling rows), 2 = the residual units gave up
   RowStat* stats;      // [B, R]
   RowStat* cstats;     // [B, R, nrc]: chunk statistics of chunked rows
-  int* nsel;           // [B] accepted length n (the residual row)
+  ResDesc* desc;       // [B]: what the residual units of b need from its decisions
   double* chunk_sums;  // [B, C, 2]: residual and p sums of each residual chunk
   int nrc, rclen;      // statistics chunks per row and their length (a multiple of 4)
   int C, chunk;        // residual chunks per sequence and their length (a multiple of 1024)
@@ -96,10 +105,11 @@ inline void stat_chunks(int rows, int V, bool logits, int* nrc, int* len) {
   *nrc = (V + l - 1) / l;
   *len = l;
 }
-// Residual chunks: at most 16 per sequence, at least 4096 elements (16 per thread).
+// Residual chunks: at most 16 per sequence, at least 6144 elements (24 per thread), so that a
+// config-3 call's residual units (8 per sequence) fit one wave of the grid.
 constexpr int kResChunks = 16;
 inline void residual_chunks(int V, int* C, int* len) {
-  int c = (V + 4095) / 4096;
+  int c = (V + 6143) / 6144;
   c = c < kResChunks ? c : kResChunks;
   *len = ((V + c - 1) / c + 1023) / 1024 * 1024;
   *C = (V + *len - 1) / *len;
@@ -107,7 +117,7 @@ inline void residual_chunks(int V, int* C, int* len) {
 
 // Workspace carve, shared by the caller-workspace and the allocation-free entry points.
 struct AcceptLayout {
-  size_t ctl, row_tickets, seq_tickets, res_tickets, ready, stats, cstats, nsel, sums, total;
+  size_t ctl, row_tickets, seq_tickets, res_tickets, ready, stats, cstats, desc, sums, total;
 };
 constexpr AcceptLayout accept_layout(int B, int k) {
   auto al = [](size_t x) { return (x + 255) / 256 * 256; };
@@ -120,8 +130,8 @@ constexpr AcceptLayout accept_layout(int B, int k) {
   l.ready = l.res_tickets + al(static_cast<size_t>(B) * sizeof(int));
   l.stats = l.ready + al(static_cast<size_t>(B) * sizeof(int));
   l.cstats = l.stats + al(static_cast<size_t>(B) * R * sizeof(RowStat));
-  l.nsel = l.cstats + al(static_cast<size_t>(kMaxStatParts) * sizeof(RowStat));
-  l.sums = l.nsel + al(static_cast<size_t>(B) * sizeof(int));
+  l.desc = l.cstats + al(static_cast<size_t>(kMaxStatParts) * sizeof(RowStat));
+  l.sums = l.desc + al(static_cast<size_t>(B) * sizeof(ResDesc));
   l.total = l.sums + al(static_cast<size_t>(B) * kResChunks * 2 * sizeof(double));
   return l;
 }
@@ -170,16 +180,25 @@ __device__ void chunk_statistics(const AcceptArgs& a, int b, int r, int x0, int 
     if (vec) {
       const float4* r4 = reinterpret_cast<const float4*>(row);
       const int n4 = x1 / 4;
-#pragma unroll 8
-      for (int j = x0 / 4 + tid; j < n4; j += kAcceptThreads) {
-        const float4 v = __ldg(r4 + j);
-        const float gm = fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w));
-        const bool nan = (v.x != v.x) || (v.y != v.y) || (v.z != v.z) || (v.w != v.w);
-        if (gm >= best || nan || best != best) {
-          argmax_merge(best, bi, v.x, 4 * j);
-          argmax_merge(best, bi, v.y, 4 * j + 1);
-          argmax_merge(best, bi, v.z, 4 * j + 2);
-          argmax_merge(best, bi, v.w, 4 * j + 3);
+      constexpr int kU = 8;  // the loads of 8 float4 per thread in flight together, then merged in order
+      for (int j0 = x0 / 4 + tid; j0 < n4; j0 += kU * kAcceptThreads) {
+        float4 v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int j = j0 + u * kAcceptThreads;
+          v[u] = j < n4 ? __ldg(r4 + j) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int j = j0 + u * kAcceptThreads;
+          const float gm = fmaxf(fmaxf(v[u].x, v[u].y), fmaxf(v[u].z, v[u].w));
+          const bool nan = (v[u].x != v[u].x) || (v[u].y != v[u].y) || (v[u].z != v[u].z) || (v[u].w != v[u].w);
+          if (j < n4 && (gm >= best || nan || best != best)) {
+            argmax_merge(best, bi, v[u].x, 4 * j);
+            argmax_merge(best, bi, v[u].y, 4 * j + 1);
+            argmax_merge(best, bi, v[u].z, 4 * j + 2);
+            argmax_merge(best, bi, v[u].w, 4 * j + 3);
+          }
         }
       }
     } else {
@@ -311,25 +330,33 @@ struct ResidualRow {
   bool q_row, q_hot;
   int64_t dn;
 };
-__device__ ResidualRow residual_row(const AcceptArgs& a, int b, int n) {
+__device__ ResidualRow residual_row(const AcceptArgs& a, int b, const ResDesc& d) {
   ResidualRow r;
-  const RowStat* st = a.stats + static_cast<int64_t>(b) * a.R;
+  const int n = d.n;
   r.prow = row_ptr(a, b, n);
-  r.ps.m = __ldcg(&st[n].m);
-  r.ps.s = __ldcg(&st[n].s);
+  r.ps = RowStat{d.p_m, d.p_s, 0.f, 0};
   r.p_inv = 1.0f / r.ps.s;
   const bool bonus = n >= a.k;  // the bonus row uses q = 0
   r.q_row = a.q_present && !a.q_onehot && !bonus;
   r.q_hot = a.q_present && a.q_onehot && !bonus;
-  r.dn = bonus ? -1 : a.draft[static_cast<int64_t>(b) * a.k + n];
+  r.dn = d.dn;
   r.qrow = r.q_row ? row_ptr(a, b, a.k + 1 + n) : nullptr;
-  r.qs = RowStat{0.f, 1.f, 0.f, 0};
-  if (r.q_row) {
-    r.qs.m = __ldcg(&st[a.k + 1 + n].m);
-    r.qs.s = __ldcg(&st[a.k + 1 + n].s);
-  }
+  r.qs = RowStat{r.q_row ? d.q_m : 0.f, r.q_row ? d.q_s : 1.f, 0.f, 0};
   r.q_inv = 1.0f / r.qs.s;
   return r;
+}
+
+SPECB200_DEVINL ResDesc load_desc(const ResDesc* p) {
+  ResDesc d;
+  const int4 lo = __ldcg(reinterpret_cast<const int4*>(p));
+  d.n = lo.x;
+  d.dn = lo.y;
+  d.p_m = __int_as_float(lo.z);
+  d.p_s = __int_as_float(lo.w);
+  const int4 hi = __ldcg(reinterpret_cast<const int4*>(p) + 1);
+  d.q_m = __int_as_float(hi.x);
+  d.q_s = __int_as_float(hi.y);
+  return d;
 }
 
 // Double sums over [x0, x1) (x0 % 4 == 0), block-wide, of the residual max(0, p - q) and of p
@@ -521,8 +548,8 @@ __device__ void decide(const AcceptArgs& a, int b) {
   }
   __syncthreads();
   const bool sampling = !a.greedy && !a.decide_only;
-  // statistics that nothing reads any more go back to zero (sampling rows: after the residual)
-  if (!sampling && threadIdx.x < a.R) a.stats[static_cast<int64_t>(b) * a.R + threadIdx.x] = RowStat{0.f, 0.f, 0.f, 0};
+  // the row statistics are read: back to zero (the residual units get theirs in a descriptor)
+  if (threadIdx.x < a.R) a.stats[static_cast<int64_t>(b) * a.R + threadIdx.x] = RowStat{0.f, 0.f, 0.f, 0};
   if (threadIdx.x == 0) {
     a.seq_tickets[b] = 0;  // ready for the next call
     int n = 0;
@@ -551,9 +578,22 @@ __device__ void decide(const AcceptArgs& a, int b) {
     a.n_accepted[b] = n;
     if (a.greedy && !a.decide_only) a.next_token[b] = sst[n].amax;
     if (sampling) {
-      a.nsel[b] = n;
+      const bool qr = a.q_present && !a.q_onehot && n < a.k;
+      ResDesc d{};
+      d.n = n;
+      d.dn = n < a.k ? static_cast<int>(sdraft[n]) : -1;
+      d.p_m = sst[n].m;
+      d.p_s = sst[n].s;
+      d.q_m = qr ? sst[a.k + 1 + n].m : 0.f;
+      d.q_s = qr ? sst[a.k + 1 + n].s : 1.f;
+      a.desc[b] = d;
       __threadfence();
-      st_release(a.ready + b, 1);
+      // 1: decisions made. 2 (left by the residual units' last chunk) means they have all given
+      // up waiting already: nothing will read the descriptor, so it goes back to zero here.
+      if (atomicExch(a.ready + b, 1) == 2) {
+        a.desc[b] = ResDesc{};
+        a.ready[b] = 0;
+      }
     }
   }
   __syncthreads();
@@ -619,15 +659,21 @@ __device__ void stat_unit(const AcceptArgs& a, int u) {
   decide(a, b);
 }
 
-// The last residual chunk of sequence b, after every unit of b has read them: b's row
-// statistics, accepted length and chunk sums go back to zero (the workspace is all zero
-// between calls, whatever (B, k) the next call has). All threads of the CTA call it.
-__device__ void residual_clear(const AcceptArgs& a, int b, double* sums) {
+// The last residual chunk of sequence b, after every unit of b has read them: b's chunk sums
+// go back to zero, and (when `decided`: b's decisions are in) its descriptor and ready flag;
+// otherwise the flag is left at 2 for the decisions to clear behind themselves. The workspace
+// is thus all zero between calls, whatever (B, k) the next call has. All threads call it.
+__device__ void residual_clear(const AcceptArgs& a, int b, double* sums, bool decided) {
   __syncthreads();
   const int tid = threadIdx.x;
-  if (tid < a.R) a.stats[static_cast<int64_t>(b) * a.R + tid] = RowStat{0.f, 0.f, 0.f, 0};
   if (tid < 2 * a.C) sums[tid] = 0.0;
-  if (tid == 0) a.nsel[b] = 0;
+  if (tid == 0) {
+    if (!decided && atomicExch(a.ready + b, 2) == 1) decided = true;  // they landed meanwhile
+    if (decided) {
+      a.desc[b] = ResDesc{};
+      a.ready[b] = 0;
+    }
+  }
 }
 
 // Residual unit v: chunk c of the residual row of sequence b (after b's decisions). The last
@@ -637,15 +683,19 @@ __device__ void residual_clear(const AcceptArgs& a, int b, double* sums) {
 // clamped).
 __device__ void residual_unit(const AcceptArgs& a, int v) {
   __shared__ int sh_ok, sh_last;
+  __shared__ ResDesc sh_desc;
   const int b = v / a.C, c = v % a.C, tid = threadIdx.x;
   if (tid == 0) {
     sh_ok = wait_flag(a.ready + b, a.status, a.wait_limit) ? 1 : 0;
-    // the accepted length indexes the rows: a value outside 0..k (workspace not zero-filled
-    // before its first use) is reported, never used
-    const int n = sh_ok ? __ldcg(a.nsel + b) : 0;
-    if (sh_ok && (n < 0 || n > a.k)) {
-      set_status(a.status, SPECB200_ERR_WORKSPACE);
-      sh_ok = 0;
+    if (sh_ok) {
+      // the accepted length and token index rows and the vocabulary: values out of range (a
+      // workspace that was not zero-filled before its first use) are reported, never used
+      const ResDesc d = load_desc(a.desc + b);
+      if (d.n < 0 || d.n > a.k || d.dn < -1 || d.dn >= a.V) {
+        set_status(a.status, SPECB200_ERR_WORKSPACE);
+        sh_ok = 0;
+      }
+      sh_desc = d;
     }
   }
   __syncthreads();
@@ -653,7 +703,7 @@ __device__ void residual_unit(const AcceptArgs& a, int v) {
   double* sums = a.chunk_sums + static_cast<int64_t>(b) * a.C * 2;
   ResidualRow r{};
   if (ok) {
-    r = residual_row(a, b, __ldcg(a.nsel + b));
+    r = residual_row(a, b, sh_desc);
     double sr, sp;
     residual_block_sums(a, r, c * a.chunk, min(a.V, (c + 1) * a.chunk), sr, sp);
     if (tid == 0) {
@@ -669,13 +719,8 @@ __device__ void residual_unit(const AcceptArgs& a, int v) {
   __threadfence();
   if (tid == 0) a.res_tickets[b] = 0;  // ready for the next call
   if (!ok) {
-    // a unit of b gave up: b's decisions may still land after this, so the last CTA of the
-    // launch clears every sequence's statistics, lengths and sums (ctl[2] asks it to)
-    if (tid == 0) {
-      a.next_token[b] = a.V - 1;
-      atomicExch(a.ctl + 2, 1);
-    }
-    residual_clear(a, b, sums);
+    if (tid == 0) a.next_token[b] = a.V - 1;
+    residual_clear(a, b, sums, false);
     return;
   }
   double total = 0.0;
@@ -708,48 +753,36 @@ __device__ void residual_unit(const AcceptArgs& a, int v) {
     base += __ldcg(sums + 2 * i + use_p);
   }
   if (tid == 0) a.next_token[b] = tok;
-  residual_clear(a, b, sums);
+  residual_clear(a, b, sums, true);
 }
 
-// Persistent CTAs: take units from the queue until it is empty; the next unit's number is
-// fetched while the current one runs. The last CTA to finish clears the queue and the flags.
+// Persistent CTAs: CTA i runs unit i first (no queue access on the critical start), then takes
+// units gridDim.x, gridDim.x + 1, ... from the queue in the order CTAs ask, the next number
+// fetched while the current unit runs. The CTA that makes the call's last fetch (every CTA
+// makes exactly one fetch past the end, so the fetches number units_total in all) clears the
+// queue. Units a CTA waits on -- a sequence's statistics, for its residual units -- come before
+// them in the queue and never wait, so every wait ends (each CTA's first unit is a statistics
+// unit, or a residual unit of the first sequences when the grid outnumbers them, and the grid
+// is sized to be resident at once).
 __global__ void __launch_bounds__(kAcceptThreads, kAcceptCtasPerSm) accept_kernel(AcceptArgs a) {
-  __shared__ int sh_unit, sh_end;
+  __shared__ int sh_unit;
   pdl_wait();
   pdl_launch_dependents();
   const int tid = threadIdx.x;
-  if (tid == 0) sh_unit = atomicAdd(a.ctl, 1);
-  __syncthreads();
-  int u = sh_unit;
+  const int grid = static_cast<int>(gridDim.x);
+  int u = blockIdx.x;
   while (u < a.units_total) {
-    int nxt = 0;
-    if (tid == 0) nxt = atomicAdd(a.ctl, 1);
+    int q = 0;
+    if (tid == 0) q = atomicAdd(a.ctl, 1);
     if (u < a.units_stat) stat_unit(a, u);
     else residual_unit(a, u - a.units_stat);
     __syncthreads();
-    if (tid == 0) sh_unit = nxt;
+    if (tid == 0) {
+      if (q == a.units_total - 1) a.ctl[0] = 0;  // the last fetch of the call
+      sh_unit = q + grid;
+    }
     __syncthreads();
     u = sh_unit;
-  }
-  if (tid == 0) {
-    __threadfence();
-    sh_end = (atomicAdd(a.ctl + 1, 1) == static_cast<int>(gridDim.x) - 1);
-  }
-  __syncthreads();
-  if (sh_end) {
-    __threadfence();
-    for (int b = tid; b < a.B; b += kAcceptThreads) a.ready[b] = 0;
-    if (__ldcg(a.ctl + 2)) {  // after a wait gave up: everything the call may have left behind
-      for (int i = tid; i < a.B * a.R; i += kAcceptThreads) a.stats[i] = RowStat{0.f, 0.f, 0.f, 0};
-      for (int i = tid; i < a.B; i += kAcceptThreads) a.nsel[i] = 0;
-      for (int i = tid; i < a.B * a.C * 2; i += kAcceptThreads) a.chunk_sums[i] = 0.0;
-    }
-    __syncthreads();
-    if (tid == 0) {
-      a.ctl[0] = 0;
-      a.ctl[1] = 0;
-      a.ctl[2] = 0;
-    }
   }
 }
 
@@ -838,7 +871,7 @@ cudaError_t launch_accept(AcceptArgs& a, char* ws, const AcceptLayout& l, cudaSt
   a.ready = reinterpret_cast<int*>(ws + l.ready);
   a.stats = reinterpret_cast<RowStat*>(ws + l.stats);
   a.cstats = reinterpret_cast<RowStat*>(ws + l.cstats);
-  a.nsel = reinterpret_cast<int*>(ws + l.nsel);
+  a.desc = reinterpret_cast<ResDesc*>(ws + l.desc);
   a.chunk_sums = reinterpret_cast<double*>(ws + l.sums);
   stat_chunks(a.B * a.R, a.V, a.logits != 0, &a.nrc, &a.rclen);
   residual_chunks(a.V, &a.C, &a.chunk);
