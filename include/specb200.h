@@ -86,6 +86,11 @@ int specb200_accept(const float* p, const float* q, const int64_t* draft, const 
  * calls return SPECB200_ERR_ARG. The first call on each device looks up the array's device
  * address with that device current: make it before any stream capture. Every call shares the
  * array: calls that overlap on the GPU race, so serialise them (one stream per process). */
+/* Profiling only (no reference counterpart): accept launches made after the call record, per
+ * work unit u, trace[4 u + 0..3] = the CTA that ran it and globaltimer stamps (start, end of
+ * its wait for the sequence's decisions -- residual units only -- and end); NULL turns the
+ * record off. The buffer must hold 4 entries per unit of the calls it observes. */
+void specb200_set_accept_trace(unsigned long long* trace);
 size_t specb200_accept_noalloc_max_rows(void);
 int specb200_accept_noalloc(const float* p, const float* q, const int64_t* draft, const float* u_accept,
                             const float* u_residual, int B, int k, int V, int flags, float temperature,

@@ -84,6 +84,9 @@ struct AcceptArgs {
   int C, chunk;        // residual chunks per sequence and their length (a multiple of 1024)
   int units_stat, units_total;
   long long wait_limit;  // clock cycles a wait for another CTA's flag may spin before it gives up
+  // Optional unit record (profiling, globaltimer ns): unit u writes trace[4 u ..] = CTA, start,
+  // end of its wait (residual units; start otherwise), end.
+  unsigned long long* trace;
 };
 
 // Statistics units: whole rows when there are enough rows to give every SM two (a row per
@@ -500,6 +503,12 @@ __device__ int residual_block_find(const AcceptArgs& a, const ResidualRow& r, in
   return hit == 0x7fffffff ? -1 : hit;
 }
 
+SPECB200_DEVINL unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
 SPECB200_DEVINL int ld_acquire(const int* p) {
   int v;
   asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -687,6 +696,7 @@ __device__ void residual_unit(const AcceptArgs& a, int v) {
   const int b = v / a.C, c = v % a.C, tid = threadIdx.x;
   if (tid == 0) {
     sh_ok = wait_flag(a.ready + b, a.status, a.wait_limit) ? 1 : 0;
+    if (a.trace) a.trace[4 * (a.units_stat + v) + 2] = globaltimer();
     if (sh_ok) {
       // the accepted length and token index rows and the vocabulary: values out of range (a
       // workspace that was not zero-filled before its first use) are reported, never used
@@ -774,9 +784,14 @@ __global__ void __launch_bounds__(kAcceptThreads, kAcceptCtasPerSm) accept_kerne
   while (u < a.units_total) {
     int q = 0;
     if (tid == 0) q = atomicAdd(a.ctl, 1);
+    if (a.trace && tid == 0) {
+      a.trace[4 * u] = blockIdx.x;
+      a.trace[4 * u + 1] = globaltimer();
+    }
     if (u < a.units_stat) stat_unit(a, u);
     else residual_unit(a, u - a.units_stat);
     __syncthreads();
+    if (a.trace && tid == 0) a.trace[4 * u + 3] = globaltimer();
     if (tid == 0) {
       if (q == a.units_total - 1) a.ctl[0] = 0;  // the last fetch of the call
       sh_unit = q + grid;
@@ -848,6 +863,7 @@ namespace specb200 {
 namespace {
 int g_sm_count[64] = {};
 std::atomic<long long> g_wait_limit{SPECB200_SPIN_LIMIT_CYCLES};
+std::atomic<unsigned long long*> g_accept_trace{nullptr};
 
 // Streaming multiprocessors of the current device (looked up once per device).
 int sm_count() {
@@ -880,6 +896,7 @@ cudaError_t launch_accept(AcceptArgs& a, char* ws, const AcceptLayout& l, cudaSt
   a.units_total = a.units_stat + (sampling ? a.B * a.C : 0);
   const int ctas = std::min(a.units_total, kAcceptCtasPerSm * sm_count());
   a.wait_limit = g_wait_limit.load();
+  a.trace = g_accept_trace.load();
   cudaError_t e = cudaSuccess;
   if (a.status) e = cudaMemsetAsync(a.status, 0, sizeof(int32_t), s);
   if (e != cudaSuccess) return e;
@@ -936,6 +953,10 @@ extern "C" int specb200_accept(const float* p, const float* q, const int64_t* dr
   if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
   return SPECB200_OK;
 }
+
+// Profiling only: accept launches made after the call record their units into `trace`
+// (4 uint64 per unit, see AcceptArgs::trace), or nothing with NULL.
+extern "C" void specb200_set_accept_trace(unsigned long long* trace) { g_accept_trace.store(trace); }
 
 extern "C" long long specb200_set_wait_limit(long long cycles) {
   if (cycles <= 0) cycles = SPECB200_SPIN_LIMIT_CYCLES;
