@@ -41,7 +41,7 @@ namespace {
 
 constexpr int kAcceptThreads = 256;
 constexpr int kAcceptWarps = kAcceptThreads / 32;
-constexpr int kAcceptCtasPerSm = 4;
+constexpr int kAcceptCtasPerSm = 3;  // 80 registers a thread, none spilled
 
 struct RowStat {
   float m;     // max of z = x / T (logit rows)
@@ -79,7 +79,7 @@ struct AcceptArgs {
   RowStat* stats;      // [B, R]
   RowStat* cstats;     // [B, R, nrc]: chunk statistics of chunked rows
   ResDesc* desc;       // [B]: what the residual units of b need from its decisions
-  double* chunk_sums;  // [B, C, 2]: residual and p sums of each residual chunk
+  double* chunk_sums;  // [B, C, 8, 2]: residual and p sums of each residual sub-chunk (one per warp)
   int nrc, rclen;      // statistics chunks per row and their length (a multiple of 4)
   int C, chunk;        // residual chunks per sequence and their length (a multiple of 1024)
   int units_stat, units_total;
@@ -89,16 +89,16 @@ struct AcceptArgs {
   unsigned long long* trace;
 };
 
-// Statistics units: whole rows when there are enough rows to give every SM two (a row per
-// unit, no partials, as at config 3); otherwise rows are cut into column chunks of at least
-// 2048 elements so that the few rows of small batches and of the draft sampler still spread
-// over the SMs (at most kMaxStatParts partials in all).
+// Statistics units: rows cut into nrc column chunks of at least 2048 elements so that the
+// queue holds about two units per CTA of the grid (config 3: 576 rows in halves for 444 CTAs;
+// the draft sampler: one row in 24 chunks), at most kMaxStatParts partials in all. Probability
+// rows need one load at the drafted token: one unit each.
 constexpr int kStatChunkMin = 2048;
 constexpr int kMaxStatParts = 8192;
-inline void stat_chunks(int rows, int V, bool logits, int* nrc, int* len) {
+inline void stat_chunks(int rows, int V, bool logits, int grid, int* nrc, int* len) {
   int n = 1;
-  if (logits && rows < 296) {  // probability rows need one load at the drafted token
-    n = (592 + rows - 1) / rows;
+  if (logits) {
+    n = (2 * grid + rows - 1) / rows;
     const int by_len = V / kStatChunkMin;
     n = n < by_len ? n : by_len;
     if (n * rows > kMaxStatParts) n = kMaxStatParts / rows;
@@ -108,8 +108,8 @@ inline void stat_chunks(int rows, int V, bool logits, int* nrc, int* len) {
   *nrc = (V + l - 1) / l;
   *len = l;
 }
-// Residual chunks: at most 16 per sequence, at least 6144 elements (24 per thread), so that a
-// config-3 call's residual units (8 per sequence) fit one wave of the grid.
+// Residual chunks: at most 16 per sequence, at least 6144 elements (24 per thread: 8 warp
+// sub-chunks of 768), 8 per sequence at V = 49,152.
 constexpr int kResChunks = 16;
 inline void residual_chunks(int V, int* C, int* len) {
   int c = (V + 6143) / 6144;
@@ -135,7 +135,7 @@ constexpr AcceptLayout accept_layout(int B, int k) {
   l.cstats = l.stats + al(static_cast<size_t>(B) * R * sizeof(RowStat));
   l.desc = l.cstats + al(static_cast<size_t>(kMaxStatParts) * sizeof(RowStat));
   l.sums = l.desc + al(static_cast<size_t>(B) * sizeof(ResDesc));
-  l.total = l.sums + al(static_cast<size_t>(B) * kResChunks * 2 * sizeof(double));
+  l.total = l.sums + al(static_cast<size_t>(B) * kResChunks * 8 * 2 * sizeof(double));
   return l;
 }
 
@@ -227,7 +227,7 @@ __device__ void chunk_statistics(const AcceptArgs& a, int b, int r, int x0, int 
   if (vec) {
     const float4* r4 = reinterpret_cast<const float4*>(row);
     const int n4 = x1 / 4;
-    constexpr int kU = 8;  // 8 float4 per thread in flight: 32 KB per CTA, 128 KB per SM
+    constexpr int kU = 8;  // 8 float4 per thread in flight: 32 KB per CTA, 96 KB per SM
     for (int j0 = x0 / 4 + tid; j0 < n4; j0 += kU * kAcceptThreads) {
       float z[kU * 4];
 #pragma unroll
@@ -277,51 +277,11 @@ __device__ void chunk_statistics(const AcceptArgs& a, int b, int r, int x0, int 
   }
 }
 
-// Residual sampling at row n: r = max(0, p_n - q_n); sample by inverse CDF with u.
-// Pass A: the row is cut into 128-element segments (one warp x 4 consecutive elements per
-// lane); every warp sums its segments (float4 loads, several segments in flight) into
-// shared memory. The total gives the target u * total; warp 0 scans the segment sums to find
-// the segment holding the crossing, then scans that segment element by element (pass B).
-// Sums accumulate in double so both passes agree except within a few ulps of a boundary.
+// Residual sampling at row n: r = max(0, p_n - q_n); sample by inverse CDF with u. Elements
+// go in groups of 4 (x % 4 == 0): res_load fetches a group's p and q words, res_values turns
+// them into residual values (or p when use_p), 0 past V.
 constexpr int kSeg = 128;
 constexpr int kMaxSegs = 4096;  // V <= kMaxSegs * kSeg = 524288 (argument check)
-SPECB200_DEVINL void seg_values(const AcceptArgs& a, const float* prow, const RowStat& ps, float p_inv,
-                                const float* qrow, const RowStat& qs, float q_inv, bool q_row, bool q_hot,
-                                int64_t dn, int use_p, int x0, float (&v)[4]) {
-  // 4 consecutive elements x0..x0+3 (x0 % 4 == 0); out-of-range elements are 0
-  float pv[4], qv[4] = {0.f, 0.f, 0.f, 0.f};
-  const bool full = x0 + 3 < a.V;
-  const bool vec = full && (a.V % 4 == 0);
-  if (vec) {
-    const float4 t = *reinterpret_cast<const float4*>(prow + x0);
-    pv[0] = t.x; pv[1] = t.y; pv[2] = t.z; pv[3] = t.w;
-    if (q_row && !use_p) {
-      const float4 u = *reinterpret_cast<const float4*>(qrow + x0);
-      qv[0] = u.x; qv[1] = u.y; qv[2] = u.z; qv[3] = u.w;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      pv[j] = x0 + j < a.V ? prow[x0 + j] : -INFINITY;
-      if (q_row && !use_p) qv[j] = x0 + j < a.V ? qrow[x0 + j] : -INFINITY;
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    if (x0 + j >= a.V) { v[j] = 0.f; continue; }
-    float px = pv[j];
-    if (a.logits) px = __expf((a.temperature == 1.f ? px : px / a.temperature) - ps.m) * p_inv;
-    if (use_p) { v[j] = px; continue; }
-    float qx = 0.f;
-    if (q_row) {
-      qx = qv[j];
-      if (a.logits) qx = __expf((a.temperature == 1.f ? qx : qx / a.temperature) - qs.m) * q_inv;
-    } else if (q_hot) {
-      qx = (x0 + j == dn) ? 1.f : 0.f;
-    }
-    v[j] = fmaxf(px - qx, 0.f);  // torch.clamp(p - q, min=0)
-  }
-}
 
 // The residual row of sequence b at its accepted length n: row pointers, statistics and the
 // q form of row n.
@@ -362,145 +322,116 @@ SPECB200_DEVINL ResDesc load_desc(const ResDesc* p) {
   return d;
 }
 
-// Double sums over [x0, x1) (x0 % 4 == 0), block-wide, of the residual max(0, p - q) and of p
-// (the fallback when the residual sums to zero), in one pass with the arithmetic of
-// seg_values. Groups of 4 elements go to threads round-robin, the loads of four groups per
-// thread in flight together; warp totals are added in warp order.
-__device__ void residual_block_sums(const AcceptArgs& a, const ResidualRow& r, int x0, int x1, double& res,
-                                    double& pr) {
-  __shared__ double sh_part[2][kAcceptWarps];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const bool vec = (a.V % 4 == 0);
-  double acc = 0.0, accp = 0.0;
-  for (int xb = x0; xb < x1; xb += 16 * kAcceptThreads) {
-    float4 pv[4], qv[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int x = xb + 4 * (tid + i * kAcceptThreads);
-      pv[i] = qv[i] = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      if (x < x1 && vec && x + 3 < a.V) {
-        pv[i] = *reinterpret_cast<const float4*>(r.prow + x);
-        if (r.q_row) qv[i] = *reinterpret_cast<const float4*>(r.qrow + x);
-      } else if (x < x1) {
-        float* pp = &pv[i].x;
-        float* qq = &qv[i].x;
-        for (int j = 0; j < 4 && x + j < x1; ++j) {
-          pp[j] = r.prow[x + j];
-          if (r.q_row) qq[j] = r.qrow[x + j];
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int x = xb + 4 * (tid + i * kAcceptThreads);
-      const float* pp = &pv[i].x;
-      const float* qq = &qv[i].x;
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        if (x + j >= x1) continue;
-        float px = pp[j];
-        if (a.logits) px = __expf((a.temperature == 1.f ? px : px / a.temperature) - r.ps.m) * r.p_inv;
-        float qx = 0.f;
-        if (r.q_row) {
-          qx = qq[j];
-          if (a.logits) qx = __expf((a.temperature == 1.f ? qx : qx / a.temperature) - r.qs.m) * r.q_inv;
-        } else if (r.q_hot) {
-          qx = (x + j == r.dn) ? 1.f : 0.f;
-        }
-        acc += static_cast<double>(fmaxf(px - qx, 0.f));  // torch.clamp(p - q, min=0)
-        accp += static_cast<double>(px);
-      }
+SPECB200_DEVINL void res_load(const AcceptArgs& a, const ResidualRow& r, int x, float4& pv, float4& qv) {
+  pv = qv = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+  if (x >= a.V) return;
+  if (x + 3 < a.V && a.V % 4 == 0) {
+    pv = *reinterpret_cast<const float4*>(r.prow + x);
+    if (r.q_row) qv = *reinterpret_cast<const float4*>(r.qrow + x);
+  } else {
+    float* pp = &pv.x;
+    float* qq = &qv.x;
+    for (int j = 0; j < 4 && x + j < a.V; ++j) {
+      pp[j] = r.prow[x + j];
+      if (r.q_row) qq[j] = r.qrow[x + j];
     }
   }
-  acc = warp_sum_d(acc);
-  accp = warp_sum_d(accp);
-  if (lane == 0) {
-    sh_part[0][warp] = acc;
-    sh_part[1][warp] = accp;
-  }
-  __syncthreads();
-  res = 0.0;
-  pr = 0.0;
-  for (int w = 0; w < kAcceptWarps; ++w) {  // fixed order
-    res += sh_part[0][w];
-    pr += sh_part[1][w];
-  }
-  __syncthreads();
 }
 
-// First index x in [x0, x1) (x0 % 4 == 0) where base + cumsum passes target, or -1; base is the
-// running sum before x0. Thread t takes a contiguous run of groups; their totals are scanned
-// across the block (warp shuffles, then the warp totals) to give each run its starting sum.
-__device__ int residual_block_find(const AcceptArgs& a, const ResidualRow& r, int use_p, int x0, int x1, double base,
-                                   double target) {
-  __shared__ double sh_warp[kAcceptWarps];
-  __shared__ int sh_hit;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int n4 = (x1 - x0 + 3) / 4;
-  const int per = (n4 + kAcceptThreads - 1) / kAcceptThreads;  // groups of 4 per thread
-  const int g0 = tid * per, g1 = min(n4, g0 + per);
-  // up to kKeep groups per thread stay in registers for the crossing scan below (one load
-  // round trip for the whole chunk); longer runs are recomputed there
-  constexpr int kKeep = 4;
-  float keep[kKeep][4];
-  double run = 0.0;
+// probabilities (lm/sampling.py:13-18) of the loaded words, then torch.clamp(p - q, min=0)
+// (spec/accept.py:18-26); p itself with use_p.
+SPECB200_DEVINL void res_values(const AcceptArgs& a, const ResidualRow& r, int use_p, int x, const float4& pv,
+                                const float4& qv, float (&v)[4]) {
+  const float* pp = &pv.x;
+  const float* qq = &qv.x;
 #pragma unroll
-  for (int q = 0; q < kKeep; ++q) {
-    keep[q][0] = keep[q][1] = keep[q][2] = keep[q][3] = 0.f;
-    const int gi = g0 + q;
-    if (gi < g1) seg_values(a, r.prow, r.ps, r.p_inv, r.qrow, r.qs, r.q_inv, r.q_row, r.q_hot, r.dn, use_p, x0 + 4 * gi, keep[q]);
+  for (int j = 0; j < 4; ++j) {
+    if (x + j >= a.V) { v[j] = 0.f; continue; }
+    float px = pp[j];
+    if (a.logits) px = __expf((a.temperature == 1.f ? px : px / a.temperature) - r.ps.m) * r.p_inv;
+    if (use_p) { v[j] = px; continue; }
+    float qx = 0.f;
+    if (r.q_row) {
+      qx = qq[j];
+      if (a.logits) qx = __expf((a.temperature == 1.f ? qx : qx / a.temperature) - r.qs.m) * r.q_inv;
+    } else if (r.q_hot) {
+      qx = (x + j == r.dn) ? 1.f : 0.f;
+    }
+    v[j] = fmaxf(px - qx, 0.f);
   }
+}
+
+// A residual chunk is 8 sub-chunks of sub = chunk / 8 elements (a multiple of 128), one per
+// warp; lane l of a warp takes elements sub_start + 128 i + 4 l .. + 3 for i = 0, 1, ... (the
+// element order is i, then lane, then j). Per warp: the double sums of the residual and of p
+// over its sub-chunk, loads of kResBatch steps in flight together.
+constexpr int kResBatch = 2;
+SPECB200_DEVINL void res_warp_sums(const AcceptArgs& a, const ResidualRow& r, int sub_start, int sub, double& res,
+                                   double& pr) {
+  const int lane = threadIdx.x & 31;
+  const int steps = sub / 128;
+  double acc = 0.0, accp = 0.0;
+  for (int i0 = 0; i0 < steps; i0 += kResBatch) {
+    float4 pv[kResBatch], qv[kResBatch];
 #pragma unroll
-  for (int q = 0; q < kKeep; ++q)
-    for (int j = 0; j < 4; ++j) run += (g0 + q < g1 && x0 + 4 * (g0 + q) + j < x1) ? keep[q][j] : 0.f;
-  for (int gi = g0 + kKeep; gi < g1; ++gi) {
-    float v[4];
-    seg_values(a, r.prow, r.ps, r.p_inv, r.qrow, r.qs, r.q_inv, r.q_row, r.q_hot, r.dn, use_p, x0 + 4 * gi, v);
-    for (int j = 0; j < 4; ++j) run += (x0 + 4 * gi + j < x1) ? v[j] : 0.f;
-  }
-  double incl = run;
+    for (int i = 0; i < kResBatch; ++i)
+      if (i0 + i < steps) res_load(a, r, sub_start + 128 * (i0 + i) + 4 * lane, pv[i], qv[i]);
 #pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const double t = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += t;
-  }
-  if (lane == 31) sh_warp[warp] = incl;
-  if (tid == 0) sh_hit = 0x7fffffff;
-  __syncthreads();
-  double before = base;
-  for (int w = 0; w < warp; ++w) before += sh_warp[w];
-  before += incl - run;  // exclusive prefix of this thread's run
-  if (before + run > target) {
-    double c = before;
-    for (int gi = g0; gi < g1; ++gi) {
-      float v[4];
-      if (gi - g0 < kKeep) {
+    for (int i = 0; i < kResBatch; ++i) {
+      if (i0 + i >= steps) break;
+      const int x = sub_start + 128 * (i0 + i) + 4 * lane;
+      float v[4], w[4];
+      res_values(a, r, 0, x, pv[i], qv[i], v);
+      res_values(a, r, 1, x, pv[i], qv[i], w);
 #pragma unroll
-        for (int q = 0; q < kKeep; ++q)
-          if (q == gi - g0) {
-            v[0] = keep[q][0]; v[1] = keep[q][1]; v[2] = keep[q][2]; v[3] = keep[q][3];
-          }
-      } else {
-        seg_values(a, r.prow, r.ps, r.p_inv, r.qrow, r.qs, r.q_inv, r.q_row, r.q_hot, r.dn, use_p, x0 + 4 * gi, v);
-      }
-      bool found = false;
       for (int j = 0; j < 4; ++j) {
-        const int x = x0 + 4 * gi + j;
-        if (x >= x1) break;
-        c += v[j];
-        if (c > target) {
-          atomicMin(&sh_hit, x);
-          found = true;
-          break;
-        }
+        acc += static_cast<double>(v[j]);
+        accp += static_cast<double>(w[j]);
       }
-      if (found) break;
     }
   }
-  __syncthreads();
-  const int hit = sh_hit;
-  __syncthreads();
-  return hit == 0x7fffffff ? -1 : hit;
+  res = warp_sum_d(acc);
+  pr = warp_sum_d(accp);
+}
+
+// First element x of sub-chunk [sub_start, sub_start + sub) where base + the running sum (in
+// element order) passes target, or -1 with base advanced past the sub-chunk. One warp.
+SPECB200_DEVINL int res_warp_find(const AcceptArgs& a, const ResidualRow& r, int use_p, int sub_start, int sub,
+                                  double& base, double target) {
+  const int lane = threadIdx.x & 31;
+  for (int i = 0; i < sub / 128; ++i) {
+    const int x = sub_start + 128 * i + 4 * lane;
+    float4 pv, qv;
+    res_load(a, r, x, pv, qv);
+    float v[4];
+    res_values(a, r, use_p, x, pv, qv, v);
+    const double mine = static_cast<double>(v[0]) + v[1] + v[2] + v[3];
+    double incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, base + incl > target);
+    if (hit) {
+      const int first = __ffs(hit) - 1;
+      int found = -1;
+      if (lane == first) {
+        double c = base + incl - mine;  // running sum before this lane's four
+        for (int j = 0; j < 4; ++j) {
+          c += v[j];
+          if (c > target) {
+            found = x + j;
+            break;
+          }
+        }
+        if (found < 0) found = min(x + 3, a.V - 1);  // the lane's total passed it: its last element
+      }
+      return __shfl_sync(0xffffffffu, found, first);
+    }
+    base += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  return -1;
 }
 
 SPECB200_DEVINL unsigned long long globaltimer() {
@@ -675,7 +606,7 @@ __device__ void stat_unit(const AcceptArgs& a, int u) {
 __device__ void residual_clear(const AcceptArgs& a, int b, double* sums, bool decided) {
   __syncthreads();
   const int tid = threadIdx.x;
-  if (tid < 2 * a.C) sums[tid] = 0.0;
+  for (int i = tid; i < 16 * a.C; i += kAcceptThreads) sums[i] = 0.0;
   if (tid == 0) {
     if (!decided && atomicExch(a.ready + b, 2) == 1) decided = true;  // they landed meanwhile
     if (decided) {
@@ -710,15 +641,16 @@ __device__ void residual_unit(const AcceptArgs& a, int v) {
   }
   __syncthreads();
   const bool ok = sh_ok;
-  double* sums = a.chunk_sums + static_cast<int64_t>(b) * a.C * 2;
+  double* sums = a.chunk_sums + static_cast<int64_t>(b) * a.C * 16;
+  const int warp = tid >> 5, lane = tid & 31, sub = a.chunk / 8;
   ResidualRow r{};
   if (ok) {
     r = residual_row(a, b, sh_desc);
     double sr, sp;
-    residual_block_sums(a, r, c * a.chunk, min(a.V, (c + 1) * a.chunk), sr, sp);
-    if (tid == 0) {
-      sums[2 * c] = sr;
-      sums[2 * c + 1] = sp;
+    res_warp_sums(a, r, c * a.chunk + warp * sub, sub, sr, sp);
+    if (lane == 0) {
+      sums[(c * 8 + warp) * 2] = sr;
+      sums[(c * 8 + warp) * 2 + 1] = sp;
     }
   }
   __threadfence();
@@ -733,36 +665,54 @@ __device__ void residual_unit(const AcceptArgs& a, int v) {
     residual_clear(a, b, sums, false);
     return;
   }
-  double total = 0.0;
-  for (int i = 0; i < a.C; ++i) total += __ldcg(sums + 2 * i);  // chunk order
-  int use_p = 0;
-  if (!(total > 0.0)) {  // residual sums to 0: residual_distribution falls back to p
-    use_p = 1;
-    total = 0.0;
-    for (int i = 0; i < a.C; ++i) total += __ldcg(sums + 2 * i + 1);
-  }
-  const double target = static_cast<double>(a.u_residual[b]) * total;
-  double base = 0.0;
-  int first = a.C;
-  for (int i = 0; i < a.C; ++i) {
-    const double si = __ldcg(sums + 2 * i + use_p);
-    if (base + si > target) {
-      first = i;
-      break;
+  // The sample: the residual total over the sub-chunks in element order (p when it is zero),
+  // u times it, the first sub-chunk whose running sum passes that, then its elements (later
+  // sub-chunks too, if rounding put the crossing past its end); past the end: V - 1
+  // (searchsorted(right=True), clamped).
+  __shared__ double sh_sub[2 * 8 * kResChunks];
+  __shared__ double sh_base, sh_target;
+  __shared__ int sh_first, sh_usep;
+  for (int i = tid; i < 16 * a.C; i += kAcceptThreads) sh_sub[i] = __ldcg(sums + i);
+  __syncthreads();
+  if (tid == 0) {
+    const int S = 8 * a.C;
+    double total = 0.0;
+    for (int i = 0; i < S; ++i) total += sh_sub[2 * i];
+    int use_p = 0;
+    if (!(total > 0.0)) {  // residual sums to 0: residual_distribution falls back to p
+      use_p = 1;
+      total = 0.0;
+      for (int i = 0; i < S; ++i) total += sh_sub[2 * i + 1];
     }
-    base += si;
-  }
-  int64_t tok = a.V - 1;
-  for (int i = first; i < a.C; ++i) {
-    const int lo = i * a.chunk, hi = min(a.V, lo + a.chunk);
-    const int x = residual_block_find(a, r, use_p, lo, hi, base, target);
-    if (x >= 0) {
-      tok = x;
-      break;
+    const double target = static_cast<double>(a.u_residual[b]) * total;
+    double base = 0.0;
+    int first = S;
+    for (int i = 0; i < S; ++i) {
+      const double si = sh_sub[2 * i + use_p];
+      if (base + si > target) {
+        first = i;
+        break;
+      }
+      base += si;
     }
-    base += __ldcg(sums + 2 * i + use_p);
+    sh_base = base;
+    sh_target = target;
+    sh_first = first;
+    sh_usep = use_p;
   }
-  if (tid == 0) a.next_token[b] = tok;
+  __syncthreads();
+  if (warp == 0) {
+    int64_t tok = a.V - 1;
+    double base = sh_base;
+    for (int i = sh_first; i < 8 * a.C; ++i) {
+      const int x = res_warp_find(a, r, sh_usep, (i / 8) * a.chunk + (i % 8) * sub, sub, base, sh_target);
+      if (x >= 0) {
+        tok = x;
+        break;
+      }
+    }
+    if (lane == 0) a.next_token[b] = tok;
+  }
   residual_clear(a, b, sums, true);
 }
 
@@ -889,12 +839,13 @@ cudaError_t launch_accept(AcceptArgs& a, char* ws, const AcceptLayout& l, cudaSt
   a.cstats = reinterpret_cast<RowStat*>(ws + l.cstats);
   a.desc = reinterpret_cast<ResDesc*>(ws + l.desc);
   a.chunk_sums = reinterpret_cast<double*>(ws + l.sums);
-  stat_chunks(a.B * a.R, a.V, a.logits != 0, &a.nrc, &a.rclen);
+  const int grid_cap = kAcceptCtasPerSm * sm_count();
+  stat_chunks(a.B * a.R, a.V, a.logits != 0, grid_cap, &a.nrc, &a.rclen);
   residual_chunks(a.V, &a.C, &a.chunk);
   const bool sampling = !a.greedy && !a.decide_only;
   a.units_stat = a.B * a.R * a.nrc;
   a.units_total = a.units_stat + (sampling ? a.B * a.C : 0);
-  const int ctas = std::min(a.units_total, kAcceptCtasPerSm * sm_count());
+  const int ctas = std::min(a.units_total, grid_cap);
   a.wait_limit = g_wait_limit.load();
   a.trace = g_accept_trace.load();
   cudaError_t e = cudaSuccess;
