@@ -86,11 +86,6 @@ int specb200_accept(const float* p, const float* q, const int64_t* draft, const 
  * calls return SPECB200_ERR_ARG. The first call on each device looks up the array's device
  * address with that device current: make it before any stream capture. Every call shares the
  * array: calls that overlap on the GPU race, so serialise them (one stream per process). */
-/* Profiling only (no reference counterpart): accept launches made after the call record, per
- * work unit u, trace[4 u + 0..3] = the CTA that ran it and globaltimer stamps (start, end of
- * its wait for the sequence's decisions -- residual units only -- and end); NULL turns the
- * record off. The buffer must hold 4 entries per unit of the calls it observes. */
-void specb200_set_accept_trace(unsigned long long* trace);
 size_t specb200_accept_noalloc_max_rows(void);
 int specb200_accept_noalloc(const float* p, const float* q, const int64_t* draft, const float* u_accept,
                             const float* u_residual, int B, int k, int V, int flags, float temperature,
@@ -231,15 +226,6 @@ size_t specb200_forward_workspace_bytes(void* model, int B, int T, int max_kv_le
  * layer op (3 + 7 n_layers launches). No reference counterpart. */
 int specb200_forward_schedule(void* model, int B, int T);
 
-/* Clock cycles a device-side wait for a flag raised by another CTA of the same launch may spin
- * before it gives up (the accept kernel's residual units waiting for their sequence's
- * decisions): the waiting CTA then records SPECB200_ERR_TIMEOUT in the call's status word and
- * finishes without that data, and the call's sampled tokens are undefined (the workspace is
- * still left zero-filled). Applies to launches made after the call (a CUDA graph keeps the limit
- * it was captured with). cycles <= 0 restores the default (about two seconds). Returns the
- * previous limit. No reference counterpart (the reference has no device waits); its use is
- * fault testing on the host side: a small limit makes such waits give up. */
-long long specb200_set_wait_limit(long long cycles);
 /* Kernel launches one forward call with B rows of T tokens makes (no reference counterpart;
  * used to count launches). */
 int specb200_forward_launches(void* model, int B, int T);

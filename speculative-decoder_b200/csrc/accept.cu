@@ -10,28 +10,23 @@
 //   spec/accept.py:29-35        sample_inverse_cdf(): first index whose cdf exceeds u * total,
 //                               clamped to V - 1
 //
-// One persistent launch (a few CTAs per SM) that takes work units from a queue in the order
-// the CTAs ask for them (an atomic counter, so a unit is only ever waited on by units taken
-// after it, whichever CTAs are resident):
-//   statistics units (sequence-major): a column chunk of one input row (R = k+1 target rows,
-//     plus k draft rows when q is a real tensor) streamed once from HBM with 128-bit loads,
-//     leaving the chunk's softmax statistics (max and sum of exp), its argmax and, in the
-//     chunk holding the drafted token, the value there. The last chunk of a row (ticket)
-//     combines them; the last row of a sequence (ticket) makes the accept decisions: n, and
-//     for greedy rows the next token. Sampling rows then raise the sequence's ready flag.
-//   residual units (sampling only, after every statistics unit): chunk c of the residual row
-//     max(0, p_n - q_n) of sequence b -- it waits (bounded) for the sequence's ready flag,
-//     re-reads its chunk of the two rows from L2 and sums the residual and p in double. The
-//     last chunk of b (ticket) scans the chunk sums in order and then the elements of the
-//     chunk holding the crossing.
-// Sequences finish in queue order, so the residual passes of early sequences overlap the
-// statistics of later ones. Every word a call writes into the workspace is back to zero when
-// its kernel ends (tickets by their last arriver, partial and row statistics, accepted lengths
-// and chunk sums once read, flags and the queue by the last CTA), so one zero-filled workspace
-// serves calls of any (B, k) with no clearing in between. Decisions therefore cost one HBM
-// pass over p and q.
+// Two launches, the second chained with programmatic dependent launch:
+//   accept_kernel: one CTA per statistics unit -- a whole input row (R = k+1 target rows, plus
+//     k draft rows when q is a real tensor) when rows are many, else a column chunk of one --
+//     streamed once from HBM with 128-bit loads: the softmax statistics (max and sum of exp),
+//     the first argmax and, in the unit holding the drafted token, the value there. The last
+//     chunk of a row (ticket) combines the chunks; the last row of a sequence (ticket) makes the
+//     accept decisions: n, and for greedy rows the next token; sampling rows leave a 32-byte
+//     record (n, the drafted token, the statistics of target and draft row n) for:
+//   residual_kernel (sampling only): one CTA per chunk of the residual row max(0, p_n - q_n) of
+//     each sequence, each warp summing a sub-chunk of it (and of p) in double; the sequence's
+//     last chunk (ticket) finds the sub-chunk holding the crossing from those sums and scans its
+//     elements with one warp.
+// Every word a call writes into the workspace is back to zero when its kernels end (tickets by
+// their last arriver, partial and row statistics, decision records and sums once read), so one
+// zero-filled workspace serves calls of any (B, k) with no clearing in between. Decisions
+// therefore cost one HBM pass over p and q.
 #include <algorithm>
-#include <atomic>
 
 #include "common.cuh"
 #include "kernels.cuh"
@@ -41,7 +36,7 @@ namespace {
 
 constexpr int kAcceptThreads = 256;
 constexpr int kAcceptWarps = kAcceptThreads / 32;
-constexpr int kAcceptCtasPerSm = 3;  // 80 registers a thread, none spilled
+constexpr int kStatCtas = 4 * 148;  // statistics CTAs aimed for when rows are few (one wave at 4 per SM)
 
 struct RowStat {
   float m;     // max of z = x / T (logit rows)
@@ -71,34 +66,27 @@ struct AcceptArgs {
   int64_t* n_accepted;
   int64_t* next_token;
   int32_t* status;
-  int* ctl;            // [0] unit queue (units past each CTA's first)
   int* row_tickets;    // [B, R]: chunks of the row done
   int* seq_tickets;    // [B]: rows of the sequence done
   int* res_tickets;    // [B]: residual chunks of the sequence done
-  int* ready;          // [B]: 1 = decisions made (sampling rows), 2 = the residual units gave up
   RowStat* stats;      // [B, R]
   RowStat* cstats;     // [B, R, nrc]: chunk statistics of chunked rows
   ResDesc* desc;       // [B]: what the residual units of b need from its decisions
   double* chunk_sums;  // [B, C, 8, 2]: residual and p sums of each residual sub-chunk (one per warp)
   int nrc, rclen;      // statistics chunks per row and their length (a multiple of 4)
   int C, chunk;        // residual chunks per sequence and their length (a multiple of 1024)
-  int units_stat, units_total;
-  long long wait_limit;  // clock cycles a wait for another CTA's flag may spin before it gives up
-  // Optional unit record (profiling, globaltimer ns): unit u writes trace[4 u ..] = CTA, start,
-  // end of its wait (residual units; start otherwise), end.
-  unsigned long long* trace;
 };
 
-// Statistics units: rows cut into nrc column chunks of at least 2048 elements so that the
-// queue holds about two units per CTA of the grid (config 3: 576 rows in halves for 444 CTAs;
-// the draft sampler: one row in 24 chunks), at most kMaxStatParts partials in all. Probability
-// rows need one load at the drafted token: one unit each.
+// Statistics units: whole rows when there are at least half as many rows as kStatCtas (config
+// 3: 576 rows, one wave at 4 CTAs per SM); fewer rows are cut into column chunks of at least
+// 2048 elements, about kStatCtas units in all (the draft sampler: one row in 24 chunks), at
+// most kMaxStatParts partials. Probability rows need one load at the drafted token.
 constexpr int kStatChunkMin = 2048;
 constexpr int kMaxStatParts = 8192;
-inline void stat_chunks(int rows, int V, bool logits, int grid, int* nrc, int* len) {
+inline void stat_chunks(int rows, int V, bool logits, int* nrc, int* len) {
   int n = 1;
-  if (logits) {
-    n = (2 * grid + rows - 1) / rows;
+  if (logits && 2 * rows < kStatCtas) {
+    n = (kStatCtas + rows - 1) / rows;
     const int by_len = V / kStatChunkMin;
     n = n < by_len ? n : by_len;
     if (n * rows > kMaxStatParts) n = kMaxStatParts / rows;
@@ -120,18 +108,16 @@ inline void residual_chunks(int V, int* C, int* len) {
 
 // Workspace carve, shared by the caller-workspace and the allocation-free entry points.
 struct AcceptLayout {
-  size_t ctl, row_tickets, seq_tickets, res_tickets, ready, stats, cstats, desc, sums, total;
+  size_t row_tickets, seq_tickets, res_tickets, stats, cstats, desc, sums, total;
 };
 constexpr AcceptLayout accept_layout(int B, int k) {
   auto al = [](size_t x) { return (x + 255) / 256 * 256; };
   const size_t R = 2 * static_cast<size_t>(k) + 1;
   AcceptLayout l{};
-  l.ctl = 0;
-  l.row_tickets = 256;
+  l.row_tickets = 0;
   l.seq_tickets = l.row_tickets + al(static_cast<size_t>(B) * R * sizeof(int));
   l.res_tickets = l.seq_tickets + al(static_cast<size_t>(B) * sizeof(int));
-  l.ready = l.res_tickets + al(static_cast<size_t>(B) * sizeof(int));
-  l.stats = l.ready + al(static_cast<size_t>(B) * sizeof(int));
+  l.stats = l.res_tickets + al(static_cast<size_t>(B) * sizeof(int));
   l.cstats = l.stats + al(static_cast<size_t>(B) * R * sizeof(RowStat));
   l.desc = l.cstats + al(static_cast<size_t>(kMaxStatParts) * sizeof(RowStat));
   l.sums = l.desc + al(static_cast<size_t>(B) * sizeof(ResDesc));
@@ -227,7 +213,7 @@ __device__ void chunk_statistics(const AcceptArgs& a, int b, int r, int x0, int 
   if (vec) {
     const float4* r4 = reinterpret_cast<const float4*>(row);
     const int n4 = x1 / 4;
-    constexpr int kU = 8;  // 8 float4 per thread in flight: 32 KB per CTA, 96 KB per SM
+    constexpr int kU = 8;  // 8 float4 per thread in flight: 32 KB per CTA, 128 KB per SM
     for (int j0 = x0 / 4 + tid; j0 < n4; j0 += kU * kAcceptThreads) {
       float z[kU * 4];
 #pragma unroll
@@ -434,39 +420,9 @@ SPECB200_DEVINL int res_warp_find(const AcceptArgs& a, const ResidualRow& r, int
   return -1;
 }
 
-SPECB200_DEVINL unsigned long long globaltimer() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-SPECB200_DEVINL int ld_acquire(const int* p) {
-  int v;
-  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-SPECB200_DEVINL void st_release(int* p, int v) {
-  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-// Bounded wait for a flag another CTA raises (set while it runs a unit taken from the queue
-// earlier): false, with SPECB200_ERR_TIMEOUT in the status word, once `limit` cycles ran out.
-SPECB200_DEVINL bool wait_flag(const int* flag, int32_t* status, long long limit) {
-  if (ld_acquire(flag)) return true;
-  const long long t0 = clock64();
-  while (true) {
-    __nanosleep(32);
-    if (ld_acquire(flag)) return true;
-    if (clock64() - t0 > limit) {
-      set_status(status, SPECB200_ERR_TIMEOUT);
-      return false;
-    }
-  }
-}
-
 // Decisions for sequence b once all its row statistics are in the workspace (the caller is
 // the CTA that finished its last row): n accepted drafts, then the greedy next token, or the
-// ready flag that lets the residual units of b start. All threads of the CTA call it.
+// record the residual kernel reads. All threads of the CTA call it.
 __device__ void decide(const AcceptArgs& a, int b) {
   __shared__ RowStat sst[32];
   __shared__ int64_t sdraft[16];
@@ -527,13 +483,6 @@ __device__ void decide(const AcceptArgs& a, int b) {
       d.q_m = qr ? sst[a.k + 1 + n].m : 0.f;
       d.q_s = qr ? sst[a.k + 1 + n].s : 1.f;
       a.desc[b] = d;
-      __threadfence();
-      // 1: decisions made. 2 (left by the residual units' last chunk) means they have all given
-      // up waiting already: nothing will read the descriptor, so it goes back to zero here.
-      if (atomicExch(a.ready + b, 1) == 2) {
-        a.desc[b] = ResDesc{};
-        a.ready[b] = 0;
-      }
     }
   }
   __syncthreads();
@@ -599,45 +548,32 @@ __device__ void stat_unit(const AcceptArgs& a, int u) {
   decide(a, b);
 }
 
-// The last residual chunk of sequence b, after every unit of b has read them: b's chunk sums
-// go back to zero, and (when `decided`: b's decisions are in) its descriptor and ready flag;
-// otherwise the flag is left at 2 for the decisions to clear behind themselves. The workspace
-// is thus all zero between calls, whatever (B, k) the next call has. All threads call it.
-__device__ void residual_clear(const AcceptArgs& a, int b, double* sums, bool decided) {
+// The last residual chunk of sequence b, after every chunk of b has read them: b's chunk sums
+// and decision record go back to zero. All threads of the CTA call it.
+__device__ void residual_clear(const AcceptArgs& a, int b, double* sums) {
   __syncthreads();
   const int tid = threadIdx.x;
   for (int i = tid; i < 16 * a.C; i += kAcceptThreads) sums[i] = 0.0;
-  if (tid == 0) {
-    if (!decided && atomicExch(a.ready + b, 2) == 1) decided = true;  // they landed meanwhile
-    if (decided) {
-      a.desc[b] = ResDesc{};
-      a.ready[b] = 0;
-    }
-  }
+  if (tid == 0) a.desc[b] = ResDesc{};
 }
 
-// Residual unit v: chunk c of the residual row of sequence b (after b's decisions). The last
-// chunk of b draws the sample: the residual total (chunk order; p when it is zero) times u,
-// the first chunk whose running sum passes it, then that chunk's elements (later chunks too,
-// if rounding put the crossing past the chunk's end); past the end: V - 1 (searchsorted,
-// clamped).
-__device__ void residual_unit(const AcceptArgs& a, int v) {
+// Grid C * B (1-D, b-major): chunk c of the residual row of sequence b. The sequence's last
+// chunk draws the sample.
+__global__ void __launch_bounds__(kAcceptThreads) residual_kernel(AcceptArgs a) {
   __shared__ int sh_ok, sh_last;
   __shared__ ResDesc sh_desc;
-  const int b = v / a.C, c = v % a.C, tid = threadIdx.x;
+  const int b = blockIdx.x / a.C, c = blockIdx.x % a.C, tid = threadIdx.x;
+  pdl_wait();
   if (tid == 0) {
-    sh_ok = wait_flag(a.ready + b, a.status, a.wait_limit) ? 1 : 0;
-    if (a.trace) a.trace[4 * (a.units_stat + v) + 2] = globaltimer();
-    if (sh_ok) {
-      // the accepted length and token index rows and the vocabulary: values out of range (a
-      // workspace that was not zero-filled before its first use) are reported, never used
-      const ResDesc d = load_desc(a.desc + b);
-      if (d.n < 0 || d.n > a.k || d.dn < -1 || d.dn >= a.V) {
-        set_status(a.status, SPECB200_ERR_WORKSPACE);
-        sh_ok = 0;
-      }
-      sh_desc = d;
+    // the accepted length and token index rows and the vocabulary: values out of range (a
+    // workspace that was not zero-filled before its first use) are reported, never used
+    const ResDesc d = load_desc(a.desc + b);
+    sh_ok = 1;
+    if (d.n < 0 || d.n > a.k || d.dn < -1 || d.dn >= a.V || !(d.p_s > 0.f)) {
+      set_status(a.status, SPECB200_ERR_WORKSPACE);
+      sh_ok = 0;
     }
+    sh_desc = d;
   }
   __syncthreads();
   const bool ok = sh_ok;
@@ -662,7 +598,7 @@ __device__ void residual_unit(const AcceptArgs& a, int v) {
   if (tid == 0) a.res_tickets[b] = 0;  // ready for the next call
   if (!ok) {
     if (tid == 0) a.next_token[b] = a.V - 1;
-    residual_clear(a, b, sums, false);
+    residual_clear(a, b, sums);
     return;
   }
   // The sample: the residual total over the sub-chunks in element order (p when it is zero),
@@ -713,42 +649,15 @@ __device__ void residual_unit(const AcceptArgs& a, int v) {
     }
     if (lane == 0) a.next_token[b] = tok;
   }
-  residual_clear(a, b, sums, true);
+  residual_clear(a, b, sums);
 }
 
-// Persistent CTAs: CTA i runs unit i first (no queue access on the critical start), then takes
-// units gridDim.x, gridDim.x + 1, ... from the queue in the order CTAs ask, the next number
-// fetched while the current unit runs. The CTA that makes the call's last fetch (every CTA
-// makes exactly one fetch past the end, so the fetches number units_total in all) clears the
-// queue. Units a CTA waits on -- a sequence's statistics, for its residual units -- come before
-// them in the queue and never wait, so every wait ends (each CTA's first unit is a statistics
-// unit, or a residual unit of the first sequences when the grid outnumbers them, and the grid
-// is sized to be resident at once).
-__global__ void __launch_bounds__(kAcceptThreads, kAcceptCtasPerSm) accept_kernel(AcceptArgs a) {
-  __shared__ int sh_unit;
+// One CTA per statistics unit (b-major, then row, then column chunk: a sequence's CTAs run
+// together). The residual kernel may start its prologue; it waits for this grid.
+__global__ void __launch_bounds__(kAcceptThreads, 4) accept_kernel(AcceptArgs a) {
   pdl_wait();
   pdl_launch_dependents();
-  const int tid = threadIdx.x;
-  const int grid = static_cast<int>(gridDim.x);
-  int u = blockIdx.x;
-  while (u < a.units_total) {
-    int q = 0;
-    if (tid == 0) q = atomicAdd(a.ctl, 1);
-    if (a.trace && tid == 0) {
-      a.trace[4 * u] = blockIdx.x;
-      a.trace[4 * u + 1] = globaltimer();
-    }
-    if (u < a.units_stat) stat_unit(a, u);
-    else residual_unit(a, u - a.units_stat);
-    __syncthreads();
-    if (a.trace && tid == 0) a.trace[4 * u + 3] = globaltimer();
-    if (tid == 0) {
-      if (q == a.units_total - 1) a.ctl[0] = 0;  // the last fetch of the call
-      sh_unit = q + grid;
-    }
-    __syncthreads();
-    u = sh_unit;
-  }
+  stat_unit(a, blockIdx.x);
 }
 
 // probabilities() of lm/sampling.py:13-18, materialised: one-hot of the first maximum at
@@ -811,48 +720,27 @@ using namespace specb200;
 
 namespace specb200 {
 namespace {
-int g_sm_count[64] = {};
-std::atomic<long long> g_wait_limit{SPECB200_SPIN_LIMIT_CYCLES};
-std::atomic<unsigned long long*> g_accept_trace{nullptr};
-
-// Streaming multiprocessors of the current device (looked up once per device).
-int sm_count() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  int n = __atomic_load_n(&g_sm_count[dev], __ATOMIC_RELAXED);
-  if (n <= 0) {
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    __atomic_store_n(&g_sm_count[dev], n, __ATOMIC_RELAXED);
-  }
-  return n;
-}
-
-// One launch on `s` (after clearing the caller's status word). The workspace's tickets,
-// flags and queue are zero on entry and on exit. Returns the first CUDA error met.
+// Both kernels on `s` (after clearing the caller's status word); the residual kernel follows
+// with programmatic dependent launch. The workspace's tickets are zero on entry and on exit.
+// Returns the first CUDA error met.
 cudaError_t launch_accept(AcceptArgs& a, char* ws, const AcceptLayout& l, cudaStream_t s) {
-  a.ctl = reinterpret_cast<int*>(ws + l.ctl);
   a.row_tickets = reinterpret_cast<int*>(ws + l.row_tickets);
   a.seq_tickets = reinterpret_cast<int*>(ws + l.seq_tickets);
   a.res_tickets = reinterpret_cast<int*>(ws + l.res_tickets);
-  a.ready = reinterpret_cast<int*>(ws + l.ready);
   a.stats = reinterpret_cast<RowStat*>(ws + l.stats);
   a.cstats = reinterpret_cast<RowStat*>(ws + l.cstats);
   a.desc = reinterpret_cast<ResDesc*>(ws + l.desc);
   a.chunk_sums = reinterpret_cast<double*>(ws + l.sums);
-  const int grid_cap = kAcceptCtasPerSm * sm_count();
-  stat_chunks(a.B * a.R, a.V, a.logits != 0, grid_cap, &a.nrc, &a.rclen);
+  stat_chunks(a.B * a.R, a.V, a.logits != 0, &a.nrc, &a.rclen);
   residual_chunks(a.V, &a.C, &a.chunk);
-  const bool sampling = !a.greedy && !a.decide_only;
-  a.units_stat = a.B * a.R * a.nrc;
-  a.units_total = a.units_stat + (sampling ? a.B * a.C : 0);
-  const int ctas = std::min(a.units_total, grid_cap);
-  a.wait_limit = g_wait_limit.load();
-  a.trace = g_accept_trace.load();
   cudaError_t e = cudaSuccess;
   if (a.status) e = cudaMemsetAsync(a.status, 0, sizeof(int32_t), s);
   if (e != cudaSuccess) return e;
-  accept_kernel<<<ctas, kAcceptThreads, 0, s>>>(a);
-  return cudaGetLastError();
+  accept_kernel<<<static_cast<unsigned>(a.B) * a.R * a.nrc, kAcceptThreads, 0, s>>>(a);
+  e = cudaGetLastError();
+  if (e == cudaSuccess && !a.greedy && !a.decide_only)
+    e = launch_kernel(residual_kernel, dim3(static_cast<unsigned>(a.C) * a.B), dim3(kAcceptThreads), 0, s, true, a);
+  return e;
 }
 }  // namespace
 }  // namespace specb200
@@ -903,15 +791,6 @@ extern "C" int specb200_accept(const float* p, const float* q, const int64_t* dr
   const cudaError_t e = launch_accept(a, static_cast<char*>(workspace), l, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return specb200_set_error(SPECB200_ERR_CUDA, cudaGetErrorString(e));
   return SPECB200_OK;
-}
-
-// Profiling only: accept launches made after the call record their units into `trace`
-// (4 uint64 per unit, see AcceptArgs::trace), or nothing with NULL.
-extern "C" void specb200_set_accept_trace(unsigned long long* trace) { g_accept_trace.store(trace); }
-
-extern "C" long long specb200_set_wait_limit(long long cycles) {
-  if (cycles <= 0) cycles = SPECB200_SPIN_LIMIT_CYCLES;
-  return g_wait_limit.exchange(cycles);
 }
 
 extern "C" int specb200_probabilities(const float* logits, int rows, int V, float temperature, float* out, void* stream) {

@@ -72,8 +72,6 @@ PROTOTYPES: dict[str, tuple] = {
     "specb200_forward_workspace_bytes": (c_size_t, [c_void_p, c_int, c_int, c_int]),
     "specb200_forward_schedule": (c_int, [c_void_p, c_int, c_int]),
     "specb200_forward_launches": (c_int, [c_void_p, c_int, c_int]),
-    "specb200_set_wait_limit": (ctypes.c_longlong, [ctypes.c_longlong]),
-    "specb200_set_accept_trace": (None, [ctypes.c_void_p]),
     "specb200_forward": (c_int, [c_void_p, ctypes.POINTER(Batch), c_void_p, c_size_t, c_void_p]),
     "specb200_rmsnorm": (c_int, [c_int, c_void_p, c_void_p, c_int, c_int, c_float, c_void_p, c_void_p]),
     "specb200_linear_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),

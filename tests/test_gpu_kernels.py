@@ -245,50 +245,6 @@ def test_accept_calls_of_different_shapes_share_one_workspace():
             assert (got_n != on).sum() + (got_t != onxt).sum() <= 1, (B, K, V)
 
 
-def test_accept_wait_limit_times_out_and_recovers():
-    """The accept kernel's only waits are its residual units waiting for their sequence's
-    decisions. For the k = 0 sampler of one 49,152-id row every unit (24 statistics chunks, 12
-    residual chunks) is taken at launch, so the residual units always start waiting before the
-    decision exists: with a wait limit of 200 cycles (about 0.1 us) they give up, the call
-    reports SPECB200_ERR_TIMEOUT through its status word and still leaves the workspace
-    zero-filled. With the default limit restored, the same call on the same workspace samples
-    exactly what an undisturbed call sampled before."""
-    from specb200 import _ffi
-
-    lib = _ffi.lib()
-    V = 49152
-    g = torch.Generator().manual_seed(5)
-    logits = (torch.randn(1, 1, V, generator=g) * 2.0).to(DEV)
-    ur = torch.rand(1, generator=g).to(DEV)
-    dummy = torch.zeros(1, 1, dtype=torch.int64, device=DEV)
-    ua = torch.zeros(1, 1, device=DEV)
-    ws = torch.zeros(lib.specb200_accept_workspace_bytes(1, 0), dtype=torch.uint8, device=DEV)
-    status = torch.zeros(1, dtype=torch.int32, device=DEV)
-    stream = torch.cuda.current_stream().cuda_stream
-
-    def call():
-        n_acc = torch.empty(1, dtype=torch.int64, device=DEV)
-        nxt = torch.empty(1, dtype=torch.int64, device=DEV)
-        rc = lib.specb200_accept(logits.data_ptr(), None, dummy.data_ptr(), ua.data_ptr(), ur.data_ptr(), 1, 0, V,
-                                 _ffi.ACCEPT_LOGITS, 1.0, n_acc.data_ptr(), nxt.data_ptr(), status.data_ptr(),
-                                 ws.data_ptr(), ws.numel(), stream)
-        assert rc == 0
-        torch.cuda.synchronize()
-        return int(nxt.item()), int(status.item())
-
-    want, st = call()
-    assert st == 0
-    prev = lib.specb200_set_wait_limit(200)
-    try:
-        _, st = call()
-    finally:
-        lib.specb200_set_wait_limit(prev)
-    assert st == _ffi.ERR_TIMEOUT
-    assert int(torch.count_nonzero(ws).item()) == 0
-    got, st = call()
-    assert st == 0 and got == want
-
-
 # ---------------------------------------------------------------- n-gram (K9)
 def test_ngram_matches_reference_golden(golden_ngram):
     from spec.ngram import lookup
