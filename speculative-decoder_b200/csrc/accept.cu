@@ -351,7 +351,7 @@ SPECB200_DEVINL void res_values(const AcceptArgs& a, const ResidualRow& r, int u
 // warp; lane l of a warp takes elements sub_start + 128 i + 4 l .. + 3 for i = 0, 1, ... (the
 // element order is i, then lane, then j). Per warp: the double sums of the residual and of p
 // over its sub-chunk, loads of kResBatch steps in flight together.
-constexpr int kResBatch = 2;
+constexpr int kResBatch = 6;  // a 768-element sub-chunk (6 steps) in one round trip
 SPECB200_DEVINL void res_warp_sums(const AcceptArgs& a, const ResidualRow& r, int sub_start, int sub, double& res,
                                    double& pr) {
   const int lane = threadIdx.x & 31;
@@ -385,37 +385,44 @@ SPECB200_DEVINL void res_warp_sums(const AcceptArgs& a, const ResidualRow& r, in
 SPECB200_DEVINL int res_warp_find(const AcceptArgs& a, const ResidualRow& r, int use_p, int sub_start, int sub,
                                   double& base, double target) {
   const int lane = threadIdx.x & 31;
-  for (int i = 0; i < sub / 128; ++i) {
-    const int x = sub_start + 128 * i + 4 * lane;
-    float4 pv, qv;
-    res_load(a, r, x, pv, qv);
-    float v[4];
-    res_values(a, r, use_p, x, pv, qv, v);
-    const double mine = static_cast<double>(v[0]) + v[1] + v[2] + v[3];
-    double incl = mine;
+  const int steps = sub / 128;
+  for (int i0 = 0; i0 < steps; i0 += kResBatch) {
+    float4 pv[kResBatch], qv[kResBatch];
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const double t = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += t;
-    }
-    const unsigned hit = __ballot_sync(0xffffffffu, base + incl > target);
-    if (hit) {
-      const int first = __ffs(hit) - 1;
-      int found = -1;
-      if (lane == first) {
-        double c = base + incl - mine;  // running sum before this lane's four
-        for (int j = 0; j < 4; ++j) {
-          c += v[j];
-          if (c > target) {
-            found = x + j;
-            break;
-          }
-        }
-        if (found < 0) found = min(x + 3, a.V - 1);  // the lane's total passed it: its last element
+    for (int i = 0; i < kResBatch; ++i)  // the loads of the batch first, all in flight together
+      if (i0 + i < steps) res_load(a, r, sub_start + 128 * (i0 + i) + 4 * lane, pv[i], qv[i]);
+#pragma unroll
+    for (int i = 0; i < kResBatch; ++i) {
+      if (i0 + i >= steps) break;
+      const int x = sub_start + 128 * (i0 + i) + 4 * lane;
+      float v[4];
+      res_values(a, r, use_p, x, pv[i], qv[i], v);
+      const double mine = static_cast<double>(v[0]) + v[1] + v[2] + v[3];
+      double incl = mine;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
       }
-      return __shfl_sync(0xffffffffu, found, first);
+      const unsigned hit = __ballot_sync(0xffffffffu, base + incl > target);
+      if (hit) {
+        const int first = __ffs(hit) - 1;
+        int found = -1;
+        if (lane == first) {
+          double c = base + incl - mine;  // running sum before this lane's four
+          for (int j = 0; j < 4; ++j) {
+            c += v[j];
+            if (c > target) {
+              found = x + j;
+              break;
+            }
+          }
+          if (found < 0) found = min(x + 3, a.V - 1);  // the lane's total passed it: its last element
+        }
+        return __shfl_sync(0xffffffffu, found, first);
+      }
+      base += __shfl_sync(0xffffffffu, incl, 31);
     }
-    base += __shfl_sync(0xffffffffu, incl, 31);
   }
   return -1;
 }
@@ -559,7 +566,7 @@ __device__ void residual_clear(const AcceptArgs& a, int b, double* sums) {
 
 // Grid C * B (1-D, b-major): chunk c of the residual row of sequence b. The sequence's last
 // chunk draws the sample.
-__global__ void __launch_bounds__(kAcceptThreads) residual_kernel(AcceptArgs a) {
+__global__ void __launch_bounds__(kAcceptThreads, 3) residual_kernel(AcceptArgs a) {
   __shared__ int sh_ok, sh_last;
   __shared__ ResDesc sh_desc;
   const int b = blockIdx.x / a.C, c = blockIdx.x % a.C, tid = threadIdx.x;
@@ -569,7 +576,7 @@ __global__ void __launch_bounds__(kAcceptThreads) residual_kernel(AcceptArgs a) 
     // workspace that was not zero-filled before its first use) are reported, never used
     const ResDesc d = load_desc(a.desc + b);
     sh_ok = 1;
-    if (d.n < 0 || d.n > a.k || d.dn < -1 || d.dn >= a.V || !(d.p_s > 0.f)) {
+    if (d.n < 0 || d.n > a.k || d.dn < -1 || d.dn >= a.V) {
       set_status(a.status, SPECB200_ERR_WORKSPACE);
       sh_ok = 0;
     }
