@@ -97,11 +97,15 @@ inline void stat_chunks(int rows, int V, bool logits, int* nrc, int* len) {
   *len = l;
 }
 // Residual chunks: at most 16 per sequence, at least 6144 elements (24 per thread: 8 warp
-// sub-chunks of 768), 8 per sequence at V = 49,152.
+// sub-chunks of 768), and no more CTAs than one wave holds (3 per SM): 8 per sequence at
+// V = 49,152 for a few sequences, 6 of 8192 elements at B = 64.
 constexpr int kResChunks = 16;
-inline void residual_chunks(int V, int* C, int* len) {
+constexpr int kResWave = 3 * 148;
+inline void residual_chunks(int V, int B, int* C, int* len) {
   int c = (V + 6143) / 6144;
   c = c < kResChunks ? c : kResChunks;
+  const int wave = kResWave / (B > 0 ? B : 1);
+  c = c < wave ? c : (wave > 1 ? wave : 1);
   *len = ((V + c - 1) / c + 1023) / 1024 * 1024;
   *C = (V + *len - 1) / *len;
 }
@@ -325,16 +329,17 @@ SPECB200_DEVINL void res_load(const AcceptArgs& a, const ResidualRow& r, int x, 
 }
 
 // probabilities (lm/sampling.py:13-18) of the loaded words, then torch.clamp(p - q, min=0)
-// (spec/accept.py:18-26); p itself with use_p.
+// (spec/accept.py:18-26) into v (p itself with use_p); p into w as well.
 SPECB200_DEVINL void res_values(const AcceptArgs& a, const ResidualRow& r, int use_p, int x, const float4& pv,
-                                const float4& qv, float (&v)[4]) {
+                                const float4& qv, float (&v)[4], float (&w)[4]) {
   const float* pp = &pv.x;
   const float* qq = &qv.x;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    if (x + j >= a.V) { v[j] = 0.f; continue; }
+    if (x + j >= a.V) { v[j] = w[j] = 0.f; continue; }
     float px = pp[j];
     if (a.logits) px = __expf((a.temperature == 1.f ? px : px / a.temperature) - r.ps.m) * r.p_inv;
+    w[j] = px;
     if (use_p) { v[j] = px; continue; }
     float qx = 0.f;
     if (r.q_row) {
@@ -362,19 +367,21 @@ SPECB200_DEVINL void res_warp_sums(const AcceptArgs& a, const ResidualRow& r, in
 #pragma unroll
     for (int i = 0; i < kResBatch; ++i)
       if (i0 + i < steps) res_load(a, r, sub_start + 128 * (i0 + i) + 4 * lane, pv[i], qv[i]);
+    float bs = 0.f, bp = 0.f;  // the batch's at most 4 kResBatch values per lane in fp32, then one double add
 #pragma unroll
     for (int i = 0; i < kResBatch; ++i) {
       if (i0 + i >= steps) break;
       const int x = sub_start + 128 * (i0 + i) + 4 * lane;
       float v[4], w[4];
-      res_values(a, r, 0, x, pv[i], qv[i], v);
-      res_values(a, r, 1, x, pv[i], qv[i], w);
+      res_values(a, r, 0, x, pv[i], qv[i], v, w);
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        acc += static_cast<double>(v[j]);
-        accp += static_cast<double>(w[j]);
+        bs += v[j];
+        bp += w[j];
       }
     }
+    acc += static_cast<double>(bs);
+    accp += static_cast<double>(bp);
   }
   res = warp_sum_d(acc);
   pr = warp_sum_d(accp);
@@ -395,8 +402,8 @@ SPECB200_DEVINL int res_warp_find(const AcceptArgs& a, const ResidualRow& r, int
     for (int i = 0; i < kResBatch; ++i) {
       if (i0 + i >= steps) break;
       const int x = sub_start + 128 * (i0 + i) + 4 * lane;
-      float v[4];
-      res_values(a, r, use_p, x, pv[i], qv[i], v);
+      float v[4], w[4];
+      res_values(a, r, use_p, x, pv[i], qv[i], v, w);
       const double mine = static_cast<double>(v[0]) + v[1] + v[2] + v[3];
       double incl = mine;
 #pragma unroll
@@ -739,7 +746,7 @@ cudaError_t launch_accept(AcceptArgs& a, char* ws, const AcceptLayout& l, cudaSt
   a.desc = reinterpret_cast<ResDesc*>(ws + l.desc);
   a.chunk_sums = reinterpret_cast<double*>(ws + l.sums);
   stat_chunks(a.B * a.R, a.V, a.logits != 0, &a.nrc, &a.rclen);
-  residual_chunks(a.V, &a.C, &a.chunk);
+  residual_chunks(a.V, a.B, &a.C, &a.chunk);
   cudaError_t e = cudaSuccess;
   if (a.status) e = cudaMemsetAsync(a.status, 0, sizeof(int32_t), s);
   if (e != cudaSuccess) return e;
