@@ -1,4 +1,4 @@
-// K8/K10: fused probabilities + accept-reject + residual sampling (one launch).
+// K8/K10: fused probabilities + accept-reject + residual sampling (two launches).
 //
 // Restates, as one kernel over logit or probability rows:
 //   lm/sampling.py:13-18        probabilities(): T == 0 -> one-hot of the first maximum,
@@ -19,9 +19,10 @@
 //     accept decisions: n, and for greedy rows the next token; sampling rows leave a 32-byte
 //     record (n, the drafted token, the statistics of target and draft row n) for:
 //   residual_kernel (sampling only): one CTA per chunk of the residual row max(0, p_n - q_n) of
-//     each sequence, each warp summing a sub-chunk of it (and of p) in double; the sequence's
-//     last chunk (ticket) finds the sub-chunk holding the crossing from those sums and scans its
-//     elements with one warp.
+//     each sequence (16 of 3072 elements at V = 49,152), each warp summing a 384-element
+//     sub-chunk of it (and of p) in double; the sequence's last chunk (ticket) finds the
+//     sub-chunk holding the crossing from those sums with a warp scan and scans its elements
+//     with the same warp.
 // Every word a call writes into the workspace is back to zero when its kernels end (tickets by
 // their last arriver, partial and row statistics, decision records and sums once read), so one
 // zero-filled workspace serves calls of any (B, k) with no clearing in between. Decisions
@@ -96,16 +97,13 @@ inline void stat_chunks(int rows, int V, bool logits, int* nrc, int* len) {
   *nrc = (V + l - 1) / l;
   *len = l;
 }
-// Residual chunks: at most 16 per sequence, at least 6144 elements (24 per thread: 8 warp
-// sub-chunks of 768), and no more CTAs than one wave holds (3 per SM): 8 per sequence at
-// V = 49,152 for a few sequences, 6 of 8192 elements at B = 64.
+// Residual chunks: at most 16 per sequence, at least 3072 elements (12 per thread: 8 warp
+// sub-chunks of 384), 16 per sequence at V = 49,152.
 constexpr int kResChunks = 16;
-constexpr int kResWave = 3 * 148;
 inline void residual_chunks(int V, int B, int* C, int* len) {
-  int c = (V + 6143) / 6144;
+  (void)B;
+  int c = (V + 3071) / 3072;
   c = c < kResChunks ? c : kResChunks;
-  const int wave = kResWave / (B > 0 ? B : 1);
-  c = c < wave ? c : (wave > 1 ? wave : 1);
   *len = ((V + c - 1) / c + 1023) / 1024 * 1024;
   *C = (V + *len - 1) / *len;
 }
@@ -356,7 +354,7 @@ SPECB200_DEVINL void res_values(const AcceptArgs& a, const ResidualRow& r, int u
 // warp; lane l of a warp takes elements sub_start + 128 i + 4 l .. + 3 for i = 0, 1, ... (the
 // element order is i, then lane, then j). Per warp: the double sums of the residual and of p
 // over its sub-chunk, loads of kResBatch steps in flight together.
-constexpr int kResBatch = 6;  // a 768-element sub-chunk (6 steps) in one round trip
+constexpr int kResBatch = 3;  // a 384-element sub-chunk (3 steps) in one round trip
 SPECB200_DEVINL void res_warp_sums(const AcceptArgs& a, const ResidualRow& r, int sub_start, int sub, double& res,
                                    double& pr) {
   const int lane = threadIdx.x & 31;
@@ -573,7 +571,7 @@ __device__ void residual_clear(const AcceptArgs& a, int b, double* sums) {
 
 // Grid C * B (1-D, b-major): chunk c of the residual row of sequence b. The sequence's last
 // chunk draws the sample.
-__global__ void __launch_bounds__(kAcceptThreads, 3) residual_kernel(AcceptArgs a) {
+__global__ void __launch_bounds__(kAcceptThreads, 4) residual_kernel(AcceptArgs a) {
   __shared__ int sh_ok, sh_last;
   __shared__ ResDesc sh_desc;
   const int b = blockIdx.x / a.C, c = blockIdx.x % a.C, tid = threadIdx.x;
@@ -620,42 +618,57 @@ __global__ void __launch_bounds__(kAcceptThreads, 3) residual_kernel(AcceptArgs 
   // sub-chunks too, if rounding put the crossing past its end); past the end: V - 1
   // (searchsorted(right=True), clamped).
   __shared__ double sh_sub[2 * 8 * kResChunks];
-  __shared__ double sh_base, sh_target;
-  __shared__ int sh_first, sh_usep;
   for (int i = tid; i < 16 * a.C; i += kAcceptThreads) sh_sub[i] = __ldcg(sums + i);
   __syncthreads();
-  if (tid == 0) {
-    const int S = 8 * a.C;
-    double total = 0.0;
-    for (int i = 0; i < S; ++i) total += sh_sub[2 * i];
-    int use_p = 0;
-    if (!(total > 0.0)) {  // residual sums to 0: residual_distribution falls back to p
-      use_p = 1;
-      total = 0.0;
-      for (int i = 0; i < S; ++i) total += sh_sub[2 * i + 1];
-    }
-    const double target = static_cast<double>(a.u_residual[b]) * total;
-    double base = 0.0;
-    int first = S;
-    for (int i = 0; i < S; ++i) {
-      const double si = sh_sub[2 * i + use_p];
-      if (base + si > target) {
-        first = i;
-        break;
-      }
-      base += si;
-    }
-    sh_base = base;
-    sh_target = target;
-    sh_first = first;
-    sh_usep = use_p;
-  }
-  __syncthreads();
   if (warp == 0) {
+    // lane l holds sub-chunks 4 l .. 4 l + 3 (at most 128 = 8 x kResChunks); the total, the
+    // choice of residual or p, the target and the crossing sub-chunk by a warp scan
+    const int S = 8 * a.C;
+    double rs[4], ps[4], lr = 0.0, lp = 0.0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = 4 * lane + j;
+      rs[j] = i < S ? sh_sub[2 * i] : 0.0;
+      ps[j] = i < S ? sh_sub[2 * i + 1] : 0.0;
+      lr += rs[j];
+      lp += ps[j];
+    }
+    const double total_r = warp_sum_d(lr);
+    const int use_p = !(total_r > 0.0);  // residual sums to 0: residual_distribution falls back to p
+    const double total = use_p ? warp_sum_d(lp) : total_r;
+    const double target = static_cast<double>(a.u_residual[b]) * total;
+    const double mine = use_p ? lp : lr;
+    double incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const unsigned hit = __ballot_sync(0xffffffffu, incl > target);
+    int first = S;
+    double base = 0.0;
+    if (hit) {  // warp-uniform: every lane computes the same first / base
+      const int hl = __ffs(hit) - 1;
+      double c = __shfl_sync(0xffffffffu, incl - mine, hl);  // running sum before lane hl's four
+      bool found = false;
+      first = 4 * hl + 3;  // lane hl's total passed the target: its last sub-chunk at the latest
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const double v = __shfl_sync(0xffffffffu, use_p ? ps[j] : rs[j], hl);
+        if (!found) {
+          if (c + v > target) {
+            first = 4 * hl + j;
+            found = true;
+          } else {
+            c += v;
+          }
+        }
+      }
+      base = c;
+    }
     int64_t tok = a.V - 1;
-    double base = sh_base;
-    for (int i = sh_first; i < 8 * a.C; ++i) {
-      const int x = res_warp_find(a, r, sh_usep, (i / 8) * a.chunk + (i % 8) * sub, sub, base, sh_target);
+    for (int i = first; i < S; ++i) {
+      const int x = res_warp_find(a, r, use_p, (i / 8) * a.chunk + (i % 8) * sub, sub, base, target);
       if (x >= 0) {
         tok = x;
         break;

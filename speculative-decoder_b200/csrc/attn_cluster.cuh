@@ -184,11 +184,15 @@ static __device__ void attention_cluster_cta(const AttnKernelArgs& ka, int b, in
   for (int i = tid; i < ntab; i += kAcThreads) tab[i] = table[tb0 + i];
   __syncthreads();
   auto load_keys = [&](int lo, int hi) {
-    for (int idx = tid; idx < (hi - lo) * 16; idx += kAcThreads) {
-      const int key = lo + (idx >> 4), part = idx & 15, isv = part >> 3, cc = part & 7;
+    // one task per (key, K or V, row half): one slot lookup per four 16-byte copies
+    for (int idx = tid; idx < (hi - lo) * 4; idx += kAcThreads) {
+      const int key = lo + (idx >> 2), isv = (idx >> 1) & 1, c0 = (idx & 1) * 4;
       const int r = key - kbeg;
       const int64_t sl = static_cast<int64_t>(tab[key / a.bs - tb0]) * a.bs + key % a.bs;
-      cp_async_16((isv ? v_s : k_s) + am_swz(r, cc * 8), (isv ? vp : kp) + (sl * a.Hkv + g) * D + cc * 8);
+      const __nv_bfloat16* src = (isv ? vp : kp) + (sl * a.Hkv + g) * D;
+      __nv_bfloat16* dst = isv ? v_s : k_s;
+#pragma unroll
+      for (int cc = c0; cc < c0 + 4; ++cc) cp_async_16(dst + am_swz(r, cc * 8), src + cc * 8);
     }
   };
   const int split_at = max(kbeg, min(kend, past));

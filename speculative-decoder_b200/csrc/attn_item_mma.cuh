@@ -91,21 +91,26 @@ static __device__ void attention_item_mma(const AttnKernelArgs& ka, int b, int g
   attn_sync();
 
   // (2) K and V blocks through the ring: keys [lo, hi) of block j (zero past kend)
+  // Thread t takes half (t & 1) of the K (or V, (t >> 1) & 1) row of key t >> 2: one slot
+  // lookup per four 16-byte copies.
+  static_assert(kAttnThreads == 32 * 4, "four (row half) tasks per key of a 32-key block");
   auto load_keys = [&](int j, int lo, int hi) {
     __nv_bfloat16* blk = reinterpret_cast<__nv_bfloat16*>(ring) + (j % kAmRing) * 4096;
-    const int k0 = kbeg + j * 32;
-    for (int idx = tid; idx < 32 * 16; idx += kAttnThreads) {
-      const int r = idx >> 4, part = idx & 15, isv = part >> 3, cc = part & 7;
-      __nv_bfloat16* dst = blk + isv * 2048 + am_swz(r, cc * 8);
-      const int key = k0 + r;
-      if (key >= kend) {
-        if (lo == kbeg) *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-      } else if (key >= lo && key < hi) {
-        const int e = key / a.bs - tb0;
-        const int64_t blkid = e < kAmItemTab ? tab[e] : table[key / a.bs];
-        const int64_t sl = blkid * a.bs + key % a.bs;
-        cp_async_16(dst, (isv ? vp : kp) + (sl * a.Hkv + g) * D + cc * 8);
+    const int r = tid >> 2, isv = (tid >> 1) & 1, c0 = (tid & 1) * 4;
+    const int key = kbeg + j * 32 + r;
+    __nv_bfloat16* dst = blk + isv * 2048;
+    if (key >= kend) {
+      if (lo == kbeg) {
+#pragma unroll
+        for (int cc = c0; cc < c0 + 4; ++cc) *reinterpret_cast<uint4*>(dst + am_swz(r, cc * 8)) = make_uint4(0, 0, 0, 0);
       }
+    } else if (key >= lo && key < hi) {
+      const int e = key / a.bs - tb0;
+      const int64_t blkid = e < kAmItemTab ? tab[e] : table[key / a.bs];
+      const int64_t sl = blkid * a.bs + key % a.bs;
+      const __nv_bfloat16* src = (isv ? vp : kp) + (sl * a.Hkv + g) * D;
+#pragma unroll
+      for (int cc = c0; cc < c0 + 4; ++cc) cp_async_16(dst + am_swz(r, cc * 8), src + cc * 8);
     }
   };
   auto load_block = [&](int j) {

@@ -126,15 +126,19 @@ static __device__ void attention_prefill_cta(const AttnArgs& a, ApSmem& sm) {
   // keys [k0, k0 + 64) into buffer `buf` (one cp.async group); rows at or past kmax are zero
   auto load_block = [&](int k0, int buf) {
     const int nk = min(kApKeys, kmax - k0);
-    for (int idx = tid; idx < kApKeys * 16; idx += kApThreads) {
-      const int kr = idx >> 4, part = idx & 15, isv = part >> 3, cc = part & 7;
-      __nv_bfloat16* dst = &sm.kv[buf][isv][am_swz(kr, cc * 8)];
+    // one task per (key, K or V, row half): one slot lookup per four 16-byte copies
+    for (int idx = tid; idx < kApKeys * 4; idx += kApThreads) {
+      const int kr = idx >> 2, isv = (idx >> 1) & 1, c0 = (idx & 1) * 4;
+      __nv_bfloat16* dst = sm.kv[buf][isv];
       if (kr < nk) {
         const int key = k0 + kr;
         const int64_t sl = static_cast<int64_t>(__ldg(table + key / a.bs)) * a.bs + key % a.bs;
-        cp_async_16(dst, (isv ? vp : kp) + (sl * a.Hkv + g) * D + cc * 8);
+        const __nv_bfloat16* src = (isv ? vp : kp) + (sl * a.Hkv + g) * D;
+#pragma unroll
+        for (int cc = c0; cc < c0 + 4; ++cc) cp_async_16(dst + am_swz(kr, cc * 8), src + cc * 8);
       } else {
-        *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+#pragma unroll
+        for (int cc = c0; cc < c0 + 4; ++cc) *reinterpret_cast<uint4*>(dst + am_swz(kr, cc * 8)) = make_uint4(0, 0, 0, 0);
       }
     }
     cp_async_commit();

@@ -323,10 +323,13 @@ GemmShape plan_gemm(int M, int N, int K, bool tensor_core) {
   s.K = K;
   s.n_tiles = (N + kTileN - 1) / kTileN;
   if (tensor_core) {
-    s.BN = std::min(256, ((M + 15) / 16) * 16);
-    // Prefill and large batches: halve the token tile (kept a multiple of 16, the MMA's N
-    // granularity) until the grid covers the 148 SMs (a 512-token q/k/v projection gets 192
-    // CTAs of 128 tokens instead of 96 of 256).
+    // The fewest token tiles of at most 256, split evenly (a multiple of 16, the MMA's N
+    // granularity): 320 tokens run as 2 x 160, not 256 + 64 with a padded second tile.
+    const int mt = (M + 255) / 256;
+    s.BN = std::min(256, ((M + mt - 1) / mt + 15) / 16 * 16);
+    // Prefill and large batches: halve the token tile (kept a multiple of 16) until the grid
+    // covers the 148 SMs (a 512-token q/k/v projection gets 192 CTAs of 128 tokens instead of
+    // 96 of 256).
     if (M > 16)
       while (s.BN > 32 && s.n_tiles * ((M + s.BN - 1) / s.BN) < 148) s.BN = (s.BN / 2 + 15) / 16 * 16;
   } else {

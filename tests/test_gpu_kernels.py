@@ -329,7 +329,8 @@ def test_linear_fp32_matches_torch(m, n, k):
     (torch.bfloat16, 9, 3, 64, 1, 16, 4500), (torch.bfloat16, 4, 2, 64, 4, 1, 130),
     (torch.bfloat16, 9, 3, 64, 1, 32, 8448), (torch.bfloat16, 32, 32, 64, 7, 32, 8448),
     (torch.bfloat16, 32, 32, 64, 5, 32, 8448), (torch.bfloat16, 9, 3, 64, 40, 16, 700),
-    (torch.bfloat16, 4, 2, 64, 130, 1, 90), (torch.bfloat16, 32, 32, 64, 200, 32, 300)])
+    (torch.bfloat16, 4, 2, 64, 130, 1, 90), (torch.bfloat16, 32, 32, 64, 200, 32, 300),
+    (torch.bfloat16, 64, 64, 64, 5, 16, 700), (torch.bfloat16, 128, 64, 64, 3, 16, 700)])
 def test_attention_matches_dense_reference(dtype, hq, hkv, d, T, bs, long_past):
     """Paged attention over shuffled blocks vs the reference's mask (lm/forward.py:44-49) on
     a dense fp32 copy: rows of lengths 1 .. long_past incl. a padded row. bf16 shapes with at
@@ -338,7 +339,9 @@ def test_attention_matches_dense_reference(dtype, hq, hkv, d, T, bs, long_past):
     cluster (4500 cached, and config 5's 8448 at block 32 for the 135M and 1.7B head
     layouts, T = 1, 5 and 7), the tensor-core split items; bf16 prefill shapes (120, 260 and
     200 query rows per KV head, block sizes 16, 1 and 32) the tensor-core prefill kernel;
-    24 rows (32 / 4 heads, T = 3) and the fp32 cases run the fp32 items."""
+    decode shapes with many (sequence, KV head) pairs (3 x 64 pairs with 5 and 6 query rows
+    each, as a B = 64 verify's 64 x 32) the tensor-core split items; 24 rows (32 / 4 heads,
+    T = 3) and the fp32 cases run the fp32 items."""
     g = torch.Generator().manual_seed(hq + T)
     lens_past = [0, 37, long_past]
     n_new = [T, max(1, T - 2), T]
