@@ -133,7 +133,7 @@ SPECB200_DEVINL bool mbar_wait_warp(uint64_t* bar, uint32_t parity, int32_t* sta
   return __shfl_sync(0xffffffffu, ok, 0) != 0;
 }
 
-// ---------------------------------------------------------------- TMA (no multicast anywhere)
+// ---------------------------------------------------------------- TMA (single-CTA loads only)
 SPECB200_DEVINL void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
