@@ -47,6 +47,14 @@ extern "C" {
 int specb200_version(void);
 const char* specb200_last_error(void);
 
+/* Failure-path check of the bounded device waits (no reference counterpart; the reference has
+ * no device code): one kernel thread waits, with the helper every pipeline uses for its
+ * mbarrier waits, on a barrier phase that never completes. After the spin limit (~2 s) it
+ * records SPECB200_ERR_TIMEOUT in *status and writes 1 to *gave_up (2 if the wait gave up
+ * without raising the abort flag, 0 if it returned). Both are device int32 words; nothing else
+ * is in flight, so the context stays usable. Stream-ordered. */
+int specb200_wait_probe(int32_t* status, int32_t* gave_up, void* stream);
+
 /* ======================================================================================
  * K8/K10: fused accept-reject and sampling
  *   replaces spec/accept.py:44-79 (accept_reject), spec/accept.py:18-26

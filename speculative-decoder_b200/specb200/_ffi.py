@@ -51,6 +51,7 @@ class Batch(ctypes.Structure):
 PROTOTYPES: dict[str, tuple] = {
     "specb200_version": (c_int, []),
     "specb200_last_error": (ctypes.c_char_p, []),
+    "specb200_wait_probe": (c_int, [c_void_p, c_void_p, c_void_p]),
     "specb200_accept_workspace_bytes": (c_size_t, [c_int, c_int]),
     "specb200_accept": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_float,
                                 c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),

@@ -374,3 +374,31 @@ def test_attention_matches_dense_reference(dtype, hq, hkv, d, T, bs, long_past):
             ref = torch.einsum("hs,shd->hd", sc.softmax(-1), vv)
             tol = 2e-5 if dtype == torch.float32 else 1.5e-2
             assert (out[b, t].float() - ref).abs().max().item() <= tol, (b, t)
+
+
+# ---------------------------------------------------------------- bounded device waits
+def test_bounded_wait_gives_up_and_context_stays_usable():
+    """A kernel waits, with the bounded helper every pipeline uses for its mbarrier waits, on a
+    phase that nothing completes: the wait gives up after its spin limit (about 2 s at the boost
+    clock), the status word reads SPECB200_ERR_TIMEOUT and the abort flag was raised; the
+    context then runs a real kernel (greedy accept-reject) correctly."""
+    import time
+
+    from specb200 import _ffi
+    from specb200._ffi import lib, ptr
+
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    gave_up = torch.full((1,), -1, dtype=torch.int32, device=DEV)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    assert lib().specb200_wait_probe(ptr(status), ptr(gave_up), torch.cuda.current_stream().cuda_stream) == 0
+    torch.cuda.synchronize()
+    waited = time.perf_counter() - t0
+    assert status.item() == _ffi.ERR_TIMEOUT and gave_up.item() == 1, (status.item(), gave_up.item())
+    assert 0.2 < waited < 30.0, waited
+    g = torch.Generator(device=DEV).manual_seed(5)
+    pl = torch.randn(3, 3, 64, generator=g, device=DEV)
+    draft = pl[:, :2].argmax(-1)
+    n, nxt = _ops().accept(pl, None, draft, torch.zeros(3, 2, device=DEV), torch.zeros(3, device=DEV), logits=True,
+                           temperature=0.0, q_onehot=True)
+    assert n.tolist() == [2, 2, 2] and nxt.tolist() == pl[:, 2].argmax(-1).tolist()
