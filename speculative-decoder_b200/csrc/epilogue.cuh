@@ -130,7 +130,63 @@ __device__ void apply_epilogue_batch(const Epilogue& e, const float* tile, int n
 // Global inputs are loaded for 8 tokens at a time before any of them is used, so an epilogue
 // over T tokens costs about T / 8 memory round trips instead of T.
 template <typename T>
-__device__ void apply_epilogue(const Epilogue& e, const float* tile, int n0, int m0, int valid, int N) {
+__device__ void apply_epilogue(const Epilogue& e, float* tile, int n0, int m0, int valid, int N) {
+  const int t = threadIdx.x;
+  if (e.op == EPI_SILU_MUL) {
+    // all 128 threads: feature t % 64 of the tile's 64 gate/up pairs, tokens t / 64, + 2, ...
+    const int j = t & 63, n = n0 + j;
+    if (n >= N) return;
+    T* out = static_cast<T*>(e.out);
+    const int f = n0 / 2 + j;
+    for (int tok = t >> 6; tok < valid; tok += 2) {
+      const float g = round_to<T>(tile[tok * kEpiPitch + j]);
+      const float u = round_to<T>(tile[tok * kEpiPitch + 64 + j]);
+      const float act = round_to<T>(g / (1.0f + expf(-g)));
+      out[static_cast<int64_t>(m0 + tok) * e.ldo + f] = from_f32<T>(act * u);
+    }
+    return;
+  }
+  if (e.op == EPI_QKV && valid > kEpiBatch) {
+    // the tile's positions and pool slots in one round trip, into rows the tile does not use
+    // (rows valid .. of the staged tile); then each batch's rotary factors are requested before
+    // the previous batch is applied
+    int* spos = reinterpret_cast<int*>(tile + static_cast<size_t>(valid) * kEpiPitch);
+    int* sslot = spos + valid;
+    for (int i = t; i < valid; i += 128) {
+      spos[i] = e.pos[m0 + i];
+      sslot[i] = e.slot[m0 + i];
+    }
+    epi_bar_sync();
+    const int n = n0 + t;
+    const int d = e.head_dim, half = d / 2;
+    const int qd = e.n_heads * d, kd = e.n_kv_heads * d;
+    const int region = n < qd ? 0 : (n < qd + kd ? 1 : 2);
+    const int i = (n - (region == 0 ? 0 : (region == 1 ? qd : qd + kd))) % d;
+    auto load = [&](int t0, EpiInputs& in) {
+#pragma unroll
+      for (int j = 0; j < kEpiBatch; ++j) {
+        const bool live = t0 + j < valid;
+        in.slot[j] = (live && region > 0) ? sslot[t0 + j] : -1;
+        in.c[j] = 1.f;
+        in.s[j] = 0.f;
+        if (live && region < 2) {
+          const int64_t off = static_cast<int64_t>(spos[t0 + j]) * half + (i % half);
+          in.c[j] = round_to<T>(e.rope_cos[off]);
+          in.s[j] = round_to<T>(e.rope_sin[off]);
+        }
+      }
+    };
+    if (n >= N) return;
+    EpiInputs cur;
+    load(0, cur);
+    for (int t0 = 0; t0 < valid; t0 += kEpiBatch) {
+      EpiInputs nxt;
+      if (t0 + kEpiBatch < valid) load(t0 + kEpiBatch, nxt);
+      apply_epilogue_batch<T>(e, tile, n0, m0, t0, valid, N, cur);
+      cur = nxt;
+    }
+    return;
+  }
   for (int t0 = 0; t0 < valid; t0 += kEpiBatch) {
     EpiInputs in;
     load_epi_inputs<T>(e, n0, m0, t0, valid, N, in);

@@ -367,11 +367,12 @@ namespace {
 int tc_stages(int BN, size_t* smem_bytes) {
   const size_t stage = kWTileBytes + static_cast<size_t>(BN) * kTileK * 2;
   const size_t tile = static_cast<size_t>(BN) * kEpiPitch * 4;
-  // Weight-bound shapes (token tiles up to 48: decode, verify, small batches): about 110 KB of
-  // ring lets a CTA of the next GEMM share the SM and prefetch its weights (measured 1.343 vs
-  // 1.361 ms per verify with the 200 KB ring). Large token tiles (prefill, large batches) keep
-  // one CTA per SM with a deep ring, since their operand tiles are large and the GEMMs long.
-  const size_t budget = BN <= 48 ? 110 * 1024 : 200 * 1024;
+  // Token tiles up to 160 get about 110 KB of ring, so two CTAs share an SM: for decode and
+  // verify shapes a CTA of the next GEMM prefetches its weights beside the current one (1.343
+  // vs 1.361 ms per B = 1 verify against a 200 KB ring); for large batches one CTA's epilogue
+  // runs beside the other's mainloop and twice the tiles fit a wave (B = 64 verify 5.89 vs
+  // 7.38 ms, B = 32 4.22 vs 4.81 ms). Larger tiles keep one CTA per SM with a deep ring.
+  const size_t budget = BN <= 160 ? 110 * 1024 : 200 * 1024;
   int stages = static_cast<int>(std::min<size_t>(8, budget / stage));
   while (static_cast<size_t>(stages) * stage < tile) ++stages;
   stages = std::max(stages, 2);
