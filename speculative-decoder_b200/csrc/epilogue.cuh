@@ -1,12 +1,14 @@
-// Fused GEMM epilogues of the per-layer GEMM kernels (gemm.cu). Each runs on 128 threads over
-// an fp32 tile held in shared memory: tile[token][feature], pitch kEpiPitch, feature j = output
-// column n0 + j.
+// Fused GEMM epilogues of the per-layer GEMM kernels (gemm.cu). Each runs on 128 or 256
+// threads over an fp32 tile held in shared memory: tile[token][feature], pitch kEpiPitch,
+// feature j = output column n0 + j; thread x works on feature x % 128.
 #pragma once
 #include "gemm.cuh"
 
 namespace specb200 {
 
 SPECB200_DEVINL void epi_bar_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// The epilogue threads of a kernel (128 or 256) on named barrier 1.
+SPECB200_DEVINL void epi_bar_sync(int n) { asm volatile("bar.sync 1, %0;" ::"r"(n) : "memory"); }
 
 constexpr int kEpiBatch = 8;
 
@@ -21,8 +23,9 @@ struct EpiInputs {
 };
 
 template <typename T>
-__device__ void load_epi_inputs(const Epilogue& e, int n0, int m0, int t0, int valid, int N, EpiInputs& in) {
-  const int n = n0 + threadIdx.x;
+__device__ void load_epi_inputs(const Epilogue& e, int n0, int m0, int t0, int valid, int N, EpiInputs& in,
+                                int t = threadIdx.x) {
+  const int n = n0 + t;
   if (n >= N) return;
   if (e.op == EPI_RESID) {
     const T* out = static_cast<const T*>(e.out);
@@ -55,8 +58,7 @@ __device__ void load_epi_inputs(const Epilogue& e, int n0, int m0, int t0, int v
 // Tokens t0 .. min(valid, t0 + kEpiBatch) - 1 of the tile, with inputs from load_epi_inputs.
 template <typename T>
 __device__ void apply_epilogue_batch(const Epilogue& e, const float* tile, int n0, int m0, int t0, int valid, int N,
-                                     const EpiInputs& in) {
-  const int t = threadIdx.x;
+                                     const EpiInputs& in, int t = threadIdx.x) {
   const int n = n0 + t;
   const int t1 = min(valid, t0 + kEpiBatch);
   switch (e.op) {
@@ -126,19 +128,21 @@ __device__ void apply_epilogue_batch(const Epilogue& e, const float* tile, int n
   }
 }
 
-// tile: fp32 [BN][kEpiPitch] in shared memory, 128 threads; thread t owns feature column t.
-// Global inputs are loaded for 8 tokens at a time before any of them is used, so an epilogue
-// over T tokens costs about T / 8 memory round trips instead of T.
+// tile: fp32 [BN][kEpiPitch] in shared memory, nthr threads; thread x owns feature column
+// x % 128. Global inputs are loaded for 8 tokens at a time before any of them is used, so an
+// epilogue over T tokens costs about T / 8 memory round trips instead of T.
 template <typename T>
-__device__ void apply_epilogue(const Epilogue& e, float* tile, int n0, int m0, int valid, int N) {
-  const int t = threadIdx.x;
+__device__ void apply_epilogue(const Epilogue& e, float* tile, int n0, int m0, int valid, int N, int nthr = 128) {
+  // nthr threads (128 or 256): thread x takes feature x % 128 of the tile and, with 256, every
+  // other 8-token batch (x / 128 picks which)
+  const int x = threadIdx.x, t = x & 127, ph = x >> 7, nph = nthr >> 7;
   if (e.op == EPI_SILU_MUL) {
-    // all 128 threads: feature t % 64 of the tile's 64 gate/up pairs, tokens t / 64, + 2, ...
-    const int j = t & 63, n = n0 + j;
+    // feature x % 64 of the tile's 64 gate/up pairs, tokens x / 64, + nthr / 64, ...
+    const int j = x & 63, n = n0 + j;
     if (n >= N) return;
     T* out = static_cast<T*>(e.out);
     const int f = n0 / 2 + j;
-    for (int tok = t >> 6; tok < valid; tok += 2) {
+    for (int tok = x >> 6; tok < valid; tok += nthr >> 6) {
       const float g = round_to<T>(tile[tok * kEpiPitch + j]);
       const float u = round_to<T>(tile[tok * kEpiPitch + 64 + j]);
       const float act = round_to<T>(g / (1.0f + expf(-g)));
@@ -149,14 +153,14 @@ __device__ void apply_epilogue(const Epilogue& e, float* tile, int n0, int m0, i
   if (e.op == EPI_QKV && valid > kEpiBatch) {
     // the tile's positions and pool slots in one round trip, into rows the tile does not use
     // (rows valid .. of the staged tile); then each batch's rotary factors are requested before
-    // the previous batch is applied
+    // the thread's previous batch is applied
     int* spos = reinterpret_cast<int*>(tile + static_cast<size_t>(valid) * kEpiPitch);
     int* sslot = spos + valid;
-    for (int i = t; i < valid; i += 128) {
+    for (int i = x; i < valid; i += nthr) {
       spos[i] = e.pos[m0 + i];
       sslot[i] = e.slot[m0 + i];
     }
-    epi_bar_sync();
+    epi_bar_sync(nthr);
     const int n = n0 + t;
     const int d = e.head_dim, half = d / 2;
     const int qd = e.n_heads * d, kd = e.n_kv_heads * d;
@@ -178,19 +182,20 @@ __device__ void apply_epilogue(const Epilogue& e, float* tile, int n0, int m0, i
     };
     if (n >= N) return;
     EpiInputs cur;
-    load(0, cur);
-    for (int t0 = 0; t0 < valid; t0 += kEpiBatch) {
+    const int step = nph * kEpiBatch;
+    if (ph * kEpiBatch < valid) load(ph * kEpiBatch, cur);
+    for (int t0 = ph * kEpiBatch; t0 < valid; t0 += step) {
       EpiInputs nxt;
-      if (t0 + kEpiBatch < valid) load(t0 + kEpiBatch, nxt);
-      apply_epilogue_batch<T>(e, tile, n0, m0, t0, valid, N, cur);
+      if (t0 + step < valid) load(t0 + step, nxt);
+      apply_epilogue_batch<T>(e, tile, n0, m0, t0, valid, N, cur, t);
       cur = nxt;
     }
     return;
   }
-  for (int t0 = 0; t0 < valid; t0 += kEpiBatch) {
+  for (int t0 = ph * kEpiBatch; t0 < valid; t0 += nph * kEpiBatch) {
     EpiInputs in;
-    load_epi_inputs<T>(e, n0, m0, t0, valid, N, in);
-    apply_epilogue_batch<T>(e, tile, n0, m0, t0, valid, N, in);
+    load_epi_inputs<T>(e, n0, m0, t0, valid, N, in, t);
+    apply_epilogue_batch<T>(e, tile, n0, m0, t0, valid, N, in, t);
   }
 }
 

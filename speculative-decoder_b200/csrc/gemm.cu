@@ -4,11 +4,13 @@
 // with the 128-byte swizzle) is the MMA's A operand (M = 128) and the token tile (BN tokens x
 // 64, BN a multiple of 16 up to 256) is its B operand, so a verify step with 5 tokens costs
 // one M=128,N=16 MMA per 64-wide K block while the weights stream from HBM at full rate.
-// fp32 products of bf16 inputs are exact and accumulate in TMEM in fp32. Warp roles: warp 4
+// fp32 products of bf16 inputs are exact and accumulate in TMEM in fp32. Warp roles: warp 8
 // issues TMA (weights for the first stages before griddepcontrol.wait, so a kernel launched
 // with programmatic dependent launch streams its weights while the previous kernel drains),
-// warp 5 issues tcgen05.mma from one thread and owns the TMEM allocation, warps 0-3 read the
-// accumulator back (tcgen05.ld, one TMEM lane per thread) and run the epilogue.
+// warp 9 issues tcgen05.mma from one thread and owns the TMEM allocation, warps 0-7 read the
+// accumulator back (tcgen05.ld, warps w and w + 4 on TMEM lane quarter w, alternate 16-column
+// chunks) and run the epilogue (feature x % 128 of the tile per thread, every other 8-token
+// batch per warpgroup; the split-K reduction on the first warpgroup).
 //
 // fp32: an FFMA kernel with the same tiling and epilogue (tcgen05 has no fp32 inputs and
 // TF32 would change results; this path serves fp32 models such as BASELINE config 1).
@@ -26,15 +28,18 @@
 
 namespace specb200 {
 
-// Split-K reduction (when splits > 1) followed by the epilogue. Called by 128 threads that
-// hold this CTA's partial tile in `tile`; returns early in every CTA but the last of a tile.
+// Split-K reduction (when splits > 1) followed by the epilogue. Called by the nthr epilogue
+// threads (128 or 256) that hold this CTA's partial tile in `tile`; thread x works on feature
+// x % 128 (the split-K path on the first 128 threads only); returns early in every CTA but the
+// last of a tile.
 template <typename T>
 __device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, GemmScratch scratch, int tile_id,
-                            int split, int n0, int m0, unsigned long long* tr = nullptr) {
+                            int split, int n0, int m0, int nthr, unsigned long long* tr = nullptr) {
   __shared__ int sh_last;
-  const int t = threadIdx.x;
+  const int x = threadIdx.x, t = x & 127;
+  const bool lead = x < 128;
   auto stamp = [&](int k) {  // optional launch record (thread 0)
-    if (tr && t == 0) {
+    if (tr && x == 0) {
       unsigned long long v;
       asm volatile("mov.u64 %0, %globaltimer;" : "=l"(v));
       tr[k] = v;
@@ -45,7 +50,8 @@ __device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, 
     float* out = static_cast<float*>(e.out) + static_cast<size_t>(split) * s.M * s.N;
     const int n = n0 + t;
     if (n < s.N)
-      for (int tok = 0; tok < valid; ++tok) out[static_cast<size_t>(m0 + tok) * s.N + n] = tile[tok * kEpiPitch + t];
+      for (int tok = x >> 7; tok < valid; tok += nthr >> 7)
+        out[static_cast<size_t>(m0 + tok) * s.N + n] = tile[tok * kEpiPitch + t];
     return;
   }
   if (s.splits > 1) {
@@ -53,18 +59,20 @@ __device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, 
     float* parts = scratch.partials;
     const size_t tile_elems = static_cast<size_t>(s.BN) * kTileN;
     float* mine = parts + (static_cast<size_t>(tile_id) * s.splits + split) * tile_elems;
-    for (int tok = 0; tok < valid; ++tok) mine[tok * kTileN + t] = tile[tok * kEpiPitch + t];
-    // The first batch's epilogue inputs now, in every split CTA: off the critical path of the
-    // CTA that turns out to finish the tile.
     EpiInputs pre;
-    load_epi_inputs<T>(e, n0, m0, 0, valid, s.N, pre);
-    __threadfence();
-    epi_bar_sync();
+    if (lead) {
+      for (int tok = 0; tok < valid; ++tok) mine[tok * kTileN + t] = tile[tok * kEpiPitch + t];
+      // The first batch's epilogue inputs now, in every split CTA: off the critical path of
+      // the CTA that turns out to finish the tile.
+      load_epi_inputs<T>(e, n0, m0, 0, valid, s.N, pre, t);
+      __threadfence();
+    }
+    epi_bar_sync(nthr);
     stamp(5);
-    if (t == 0) sh_last = (atomicAdd(counters + tile_id, 1) == s.splits - 1);
-    epi_bar_sync();
+    if (x == 0) sh_last = (atomicAdd(counters + tile_id, 1) == s.splits - 1);
+    epi_bar_sync(nthr);
     stamp(6);
-    if (!sh_last) return;
+    if (!sh_last || !lead) return;  // the tile's last CTA finishes it on its first 128 threads
     __threadfence();
     const float* base = parts + static_cast<size_t>(tile_id) * s.splits * tile_elems;
     constexpr int kSplitBatch = 4;  // splits whose partials are loaded together (summed in split order)
@@ -92,17 +100,17 @@ __device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, 
         if (t0 + j < valid) tile[(t0 + j) * kEpiPitch + t] = acc[j];
     }
     if (t == 0) counters[tile_id] = 0;
-    epi_bar_sync();
+    epi_bar_sync();  // the first 128 threads only from here
     stamp(7);
-    apply_epilogue_batch<T>(e, tile, n0, m0, 0, valid, s.N, pre);
+    apply_epilogue_batch<T>(e, tile, n0, m0, 0, valid, s.N, pre, t);
     for (int t0 = kEpiBatch; t0 < valid; t0 += kEpiBatch) {
       EpiInputs in;
-      load_epi_inputs<T>(e, n0, m0, t0, valid, s.N, in);
-      apply_epilogue_batch<T>(e, tile, n0, m0, t0, valid, s.N, in);
+      load_epi_inputs<T>(e, n0, m0, t0, valid, s.N, in, t);
+      apply_epilogue_batch<T>(e, tile, n0, m0, t0, valid, s.N, in, t);
     }
     return;
   }
-  apply_epilogue<T>(e, tile, n0, m0, valid, s.N);
+  apply_epilogue<T>(e, tile, n0, m0, valid, s.N, nthr);
 }
 
 SPECB200_DEVINL void split_range(const GemmShape& s, int split, int& kb0, int& kb1) {
@@ -111,7 +119,8 @@ SPECB200_DEVINL void split_range(const GemmShape& s, int split, int& kb0, int& k
 }
 
 // ------------------------------------------------------------------------------ tcgen05 kernel
-constexpr int kTcThreads = 192;
+constexpr int kTcThreads = 320;  // 8 epilogue warps (two per TMEM lane quarter), the TMA warp, the MMA warp
+constexpr int kTcEpiThreads = 256;
 constexpr uint32_t kWTileBytes = kTileN * kTileK * 2;  // 16 KB
 
 SPECB200_DEVINL uint32_t tmem_cols_for(int BN) { return BN <= 32 ? 32u : BN <= 64 ? 64u : BN <= 128 ? 128u : 256u; }
@@ -160,7 +169,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tmem_alloc(tmem_holder, tmem_cols);
     tmem_relinquish();
   }
@@ -170,7 +179,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
 
-  if (warp == 4) {
+  if (warp == 8) {
     if (lane == 0) {
       tma_prefetch_desc(&w_map);
       tma_prefetch_desc(&x_map);
@@ -198,7 +207,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
         if (!mbar_wait_bounded(&empty[i % stages], (i / stages) & 1, status, abort_flag)) break;
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // The whole warp runs the loop and one elected lane issues each MMA: issuing from a lone
     // lane while the others wait diverged costs about a third more per instruction.
     const uint32_t idesc = umma_idesc_bf16(kTileN, BN);
@@ -223,22 +232,24 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     tc_fence_after();
     float* tile = reinterpret_cast<float*>(smem);  // the pipeline stages are idle now
     if (ok) {
-      for (int c = 0; c < BN; c += 16) {
+      // warps w and w + 4 read TMEM lane quarter w, alternate 16-column chunks
+      const int q = warp & 3;
+      for (int c = (warp >> 2) * 16; c < BN; c += 32) {
         float v[16];
-        tmem_ld16(tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + c, v);
+        tmem_ld16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) + c, v);
         tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 16; ++j) tile[(c + j) * kEpiPitch + warp * 32 + lane] = v[j];
+        for (int j = 0; j < 16; ++j) tile[(c + j) * kEpiPitch + q * 32 + lane] = v[j];
       }
     }
-    epi_bar_sync();
+    epi_bar_sync(kTcEpiThreads);
     if (ok && !*reinterpret_cast<volatile int*>(abort_flag))
-      finish_tile<__nv_bfloat16>(s, e, tile, scratch, tile_id, split, n_tile * kTileN, m_tile * BN, tr);
+      finish_tile<__nv_bfloat16>(s, e, tile, scratch, tile_id, split, n_tile * kTileN, m_tile * BN, kTcEpiThreads, tr);
     if (threadIdx.x == 0) stamp(4);
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc_fence_after();
     tmem_dealloc(tmem_base, tmem_cols);
   }
@@ -312,7 +323,7 @@ __global__ void __launch_bounds__(kSimtThreads)
   for (int j = 0; j < kSimtMaxBN; ++j)
     if (j < BN) tile[j * kEpiPitch + threadIdx.x] = acc[j];
   __syncthreads();
-  finish_tile<T>(s, e, tile, scratch, tile_id, split, n0, m0);
+  finish_tile<T>(s, e, tile, scratch, tile_id, split, n0, m0, kSimtThreads);
 }
 
 // ------------------------------------------------------------------------------ host side
