@@ -93,7 +93,7 @@ WORKLOADS = {
                      "(32 over 8 GPUs), 8192-token prompts of 64-id segments each repeated with p=0.5, k=6, greedy, "
                      "256 new tokens, block 32"),
 }
-NOISY_SIGMA = 0.09  # config 2b: N(0, sigma^2) on the target's logits, sigma measured for acceptance ~0.6
+NOISY_SIGMA = 0.06  # config 2b: N(0, sigma^2) on the target's logits; sigma 0.06 measured 0.61 acceptance (0.09: 0.49)
 
 
 def workload_prompts(w: dict, first: int, n: int) -> list[list[int]]:
