@@ -10,7 +10,8 @@
 // warp 9 issues tcgen05.mma from one thread and owns the TMEM allocation, warps 0-7 read the
 // accumulator back (tcgen05.ld, warps w and w + 4 on TMEM lane quarter w, alternate 16-column
 // chunks) and run the epilogue (feature x % 128 of the tile per thread, every other 8-token
-// batch per warpgroup; the split-K reduction on the first warpgroup).
+// batch per warpgroup; a split tile of one 8-token batch is reduced on the first warpgroup,
+// larger ones on all eight warps).
 //
 // fp32: an FFMA kernel with the same tiling and epilogue (tcgen05 has no fp32 inputs and
 // TF32 would change results; this path serves fp32 models such as BASELINE config 1).
@@ -29,9 +30,9 @@
 namespace specb200 {
 
 // Split-K reduction (when splits > 1) followed by the epilogue. Called by the nthr epilogue
-// threads (128 or 256) that hold this CTA's partial tile in `tile`; thread x works on feature
-// x % 128 (the split-K path on the first 128 threads only); returns early in every CTA but the
-// last of a tile.
+// threads (128 or 256) that hold this CTA's partial tile in `tile`; returns early in every CTA
+// but the last of a tile. The partials of each element are summed in split order (0, 1, ...)
+// whichever threads do it, so the result does not depend on the path taken.
 template <typename T>
 __device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, GemmScratch scratch, int tile_id,
                             int split, int n0, int m0, int nthr, unsigned long long* tr = nullptr) {
@@ -59,8 +60,19 @@ __device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, 
     float* parts = scratch.partials;
     const size_t tile_elems = static_cast<size_t>(s.BN) * kTileN;
     float* mine = parts + (static_cast<size_t>(tile_id) * s.splits + split) * tile_elems;
+    // Token tiles of more than one epilogue batch store, reduce and finish on all nthr threads
+    // in 16-byte pieces (32 per token row); one batch's tile keeps the first 128 threads and
+    // fetches its epilogue inputs before the ticket.
+    const bool wide = valid > kEpiBatch;
+    const int n4 = valid * (kTileN / 4);
     EpiInputs pre;
-    if (lead) {
+    if (wide) {
+      for (int p = x; p < n4; p += nthr) {
+        const int r = p >> 5, c = (p & 31) * 4;
+        *reinterpret_cast<float4*>(mine + r * kTileN + c) = *reinterpret_cast<const float4*>(tile + r * kEpiPitch + c);
+      }
+      __threadfence();
+    } else if (lead) {
       for (int tok = 0; tok < valid; ++tok) mine[tok * kTileN + t] = tile[tok * kEpiPitch + t];
       // The first batch's epilogue inputs now, in every split CTA: off the critical path of
       // the CTA that turns out to finish the tile.
@@ -72,10 +84,50 @@ __device__ void finish_tile(const GemmShape& s, const Epilogue& e, float* tile, 
     if (x == 0) sh_last = (atomicAdd(counters + tile_id, 1) == s.splits - 1);
     epi_bar_sync(nthr);
     stamp(6);
-    if (!sh_last || !lead) return;  // the tile's last CTA finishes it on its first 128 threads
-    __threadfence();
+    if (!sh_last) return;
     const float* base = parts + static_cast<size_t>(tile_id) * s.splits * tile_elems;
     constexpr int kSplitBatch = 4;  // splits whose partials are loaded together (summed in split order)
+    if (wide) {
+      __threadfence();
+      constexpr int kRows = 3;  // 16-byte pieces per thread whose loads are in flight together (no spills at 3)
+      for (int p0 = x; p0 < n4; p0 += kRows * nthr) {
+        float4 acc[kRows];
+#pragma unroll
+        for (int u = 0; u < kRows; ++u) acc[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int sp0 = 0; sp0 < s.splits; sp0 += kSplitBatch) {
+          float4 v[kSplitBatch][kRows];
+#pragma unroll
+          for (int q = 0; q < kSplitBatch; ++q)
+#pragma unroll
+            for (int u = 0; u < kRows; ++u) {
+              const int p = p0 + u * nthr;
+              v[q][u] = (sp0 + q < s.splits && p < n4)
+                            ? __ldcg(reinterpret_cast<const float4*>(base + (sp0 + q) * tile_elems + (p >> 5) * kTileN) +
+                                     (p & 31))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+          for (int q = 0; q < kSplitBatch; ++q)
+#pragma unroll
+            for (int u = 0; u < kRows; ++u)
+              if (sp0 + q < s.splits) {
+                acc[u].x += v[q][u].x; acc[u].y += v[q][u].y; acc[u].z += v[q][u].z; acc[u].w += v[q][u].w;
+              }
+        }
+#pragma unroll
+        for (int u = 0; u < kRows; ++u) {
+          const int p = p0 + u * nthr;
+          if (p < n4) *reinterpret_cast<float4*>(tile + (p >> 5) * kEpiPitch + (p & 31) * 4) = acc[u];
+        }
+      }
+      if (x == 0) counters[tile_id] = 0;
+      epi_bar_sync(nthr);
+      stamp(7);
+      apply_epilogue<T>(e, tile, n0, m0, valid, s.N, nthr);
+      return;
+    }
+    if (!lead) return;  // a one-batch tile is finished on the first 128 threads
+    __threadfence();
     for (int t0 = 0; t0 < valid; t0 += kEpiBatch) {
       float acc[kEpiBatch];
 #pragma unroll
@@ -333,6 +385,8 @@ GemmShape plan_gemm(int M, int N, int K, bool tensor_core) {
   s.N = N;
   s.K = K;
   s.n_tiles = (N + kTileN - 1) / kTileN;
+  const int kblocks = (K + kTileK - 1) / kTileK;
+  bool split_fill = false;  // fill two CTAs per SM with K-splits rather than smaller token tiles
   if (tensor_core) {
     // The fewest token tiles of at most 256, split evenly (a multiple of 16, the MMA's N
     // granularity): 320 tokens run as 2 x 160, not 256 + 64 with a padded second tile.
@@ -340,9 +394,24 @@ GemmShape plan_gemm(int M, int N, int K, bool tensor_core) {
     s.BN = std::min(256, ((M + mt - 1) / mt + 15) / 16 * 16);
     // Prefill and large batches: halve the token tile (kept a multiple of 16) until the grid
     // covers the 148 SMs (a 512-token q/k/v projection gets 192 CTAs of 128 tokens instead of
-    // 96 of 256).
-    if (M > 16)
-      while (s.BN > 32 && s.n_tiles * ((M + s.BN - 1) / s.BN) < 148) s.BN = (s.BN / 2 + 15) / 16 * 16;
+    // 96 of 256). Token tiles of at most 160 (two CTAs per SM) with a long K split K instead,
+    // once up to eight splits that fill two CTAs per SM leave every CTA at least 16 k-blocks:
+    // each halving re-reads every weight tile once more, and at 32 tokens a CTA streams the
+    // whole K (B = 64 down projection: 10 token tiles x 128 k-blocks per CTA).
+    if (M > 16) {
+      const bool two_per_sm = s.BN <= 160;
+      while (s.BN > 32 && s.n_tiles * ((M + s.BN - 1) / s.BN) < 148) {
+        if (two_per_sm) {
+          const int ctas = s.n_tiles * ((M + s.BN - 1) / s.BN);
+          const int want = std::min(8, (2 * 148 + ctas - 1) / ctas);
+          if (kblocks / want >= 16) {
+            split_fill = true;
+            break;
+          }
+        }
+        s.BN = (s.BN / 2 + 15) / 16 * 16;
+      }
+    }
   } else {
     s.BN = std::min(kSimtMaxBN, ((M + 3) / 4) * 4);
   }
@@ -357,7 +426,7 @@ GemmShape plan_gemm(int M, int N, int K, bool tensor_core) {
     const int per_stage = kTileN * kTileK * 2 + s.BN * kTileK * 2;
     const int stages = std::max(2, std::min(8, (200 * 1024) / per_stage));
     const int fit = (s.kblocks + stages - 1) / stages;
-    const int fill = std::max(1, 148 / ctas);
+    const int fill = split_fill ? std::max(1, std::min(8, 2 * 148 / ctas)) : std::max(1, 148 / ctas);
     splits = std::max(1, std::min({fit, fill, 16, s.kblocks}));
   } else {
     splits = (148 + ctas / 2) / ctas;
