@@ -82,7 +82,10 @@ Carve carve(const Model& m, int B, int T, int max_kv_len, int last_only) {
   const int qd = c.n_heads * c.head_dim;
   Carve r;
   r.g_qkv = plan_gemm(M, m.qkv_n, c.hidden, tc);
-  r.g_o = plan_gemm(M, c.hidden, qd, tc);
+  // o's partials are summed by the following residual RMSNorm: it may split K down to 4
+  // k-blocks per CTA (B = 64 verify: 12.25 -> 8.75 us per o GEMM). q/k/v keeps 16: a split q/k/v
+  // tile runs its RoPE epilogue after the reduction (30.5 -> 49.6 us per GEMM at B = 64).
+  r.g_o = plan_gemm(M, c.hidden, qd, tc, 4);
   r.g_gu = plan_gemm(M, 2 * c.intermediate, c.hidden, tc);
   r.g_down = plan_gemm(M, c.hidden, c.intermediate, tc);
   r.g_head = plan_gemm(rows_out, c.vocab, c.hidden, tc);

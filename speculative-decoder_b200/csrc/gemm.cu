@@ -379,7 +379,7 @@ __global__ void __launch_bounds__(kSimtThreads)
 }
 
 // ------------------------------------------------------------------------------ host side
-GemmShape plan_gemm(int M, int N, int K, bool tensor_core) {
+GemmShape plan_gemm(int M, int N, int K, bool tensor_core, int min_split_kblocks) {
   GemmShape s;
   s.M = M;
   s.N = N;
@@ -395,7 +395,9 @@ GemmShape plan_gemm(int M, int N, int K, bool tensor_core) {
     // Prefill and large batches: halve the token tile (kept a multiple of 16) until the grid
     // covers the 148 SMs (a 512-token q/k/v projection gets 192 CTAs of 128 tokens instead of
     // 96 of 256). Token tiles of at most 160 (two CTAs per SM) with a long K split K instead,
-    // once up to eight splits that fill two CTAs per SM leave every CTA at least 16 k-blocks:
+    // once up to eight splits that fill two CTAs per SM leave every CTA at least
+    // min_split_kblocks k-blocks (16 by default; 4 for the o projection, whose split partials
+    // go to the next RMSNorm, not through a split-K epilogue):
     // each halving re-reads every weight tile once more, and at 32 tokens a CTA streams the
     // whole K (B = 64 down projection: 10 token tiles x 128 k-blocks per CTA).
     if (M > 16) {
@@ -404,7 +406,7 @@ GemmShape plan_gemm(int M, int N, int K, bool tensor_core) {
         if (two_per_sm) {
           const int ctas = s.n_tiles * ((M + s.BN - 1) / s.BN);
           const int want = std::min(8, (2 * 148 + ctas - 1) / ctas);
-          if (kblocks / want >= 16) {
+          if (kblocks / want >= min_split_kblocks) {
             split_fill = true;
             break;
           }

@@ -46,7 +46,9 @@ struct GemmShape {
 };
 
 // Host-side choice of BN and split count for a weight-streaming GEMM on 148 SMs.
-GemmShape plan_gemm(int M, int N, int K, bool tensor_core);
+// min_split_kblocks: the fewest k-blocks per CTA at which a token tile of at most 160 keeps its
+// size and K is split to fill two CTAs per SM, rather than the tile being halved.
+GemmShape plan_gemm(int M, int N, int K, bool tensor_core, int min_split_kblocks = 16);
 size_t gemm_workspace_bytes(const GemmShape& s);
 
 // Launchers (gemm.cu). w_map is a tensor map over W [N, K] with box {64, 128}; x_map over
