@@ -168,6 +168,28 @@ def test_host_queries_need_no_gpu() -> None:
     assert lib.specb200_linear_workspace_bytes(5, 6144, 2048) > 0
 
 
+def test_linear_plan_splits_long_k_at_verify_batches() -> None:
+    """The workspace a bf16 linear asks for is 4096 B of tile counters plus, when K is split,
+    n_tiles x m_tiles x splits x BN x 128 fp32 partials. It shows the plan without a GPU: a long-K
+    projection at verify batch sizes keeps 160-token tiles (144 at 288 rows) and splits K 8
+    ways, where halving the tile to 32 tokens would make every CTA stream the whole K; prefill
+    sizes, short K and the 5-row verify keep their plans."""
+    from specb200 import _ffi
+
+    lib = _ffi.lib()
+    counters = 4096
+
+    def partials(n_tiles, m_tiles, splits, bn):
+        return counters + n_tiles * m_tiles * splits * bn * 128 * 4
+
+    assert lib.specb200_linear_workspace_bytes(320, 2048, 8192) == partials(16, 2, 8, 160)  # B = 64 down
+    assert lib.specb200_linear_workspace_bytes(160, 2048, 8192) == partials(16, 1, 8, 160)  # B = 32 down
+    assert lib.specb200_linear_workspace_bytes(288, 2048, 8192) == partials(16, 2, 8, 144)  # config 4 down
+    assert lib.specb200_linear_workspace_bytes(5, 2048, 8192) == partials(16, 1, 9, 16)  # B = 1 down
+    for m, n, k in ((512, 2048, 8192), (320, 6144, 2048), (320, 16384, 2048), (320, 2048, 2048)):
+        assert lib.specb200_linear_workspace_bytes(m, n, k) == counters, (m, n, k)  # no K split
+
+
 def test_host_argument_checks_reject_bad_calls() -> None:
     from specb200 import _ffi
 
